@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""SlottedGLU MoE layer throughput on B200 (tokens/s) with its roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (default ``cfg3``): the Qwen3-Next-style slotted MoE layer -- hidden
+2048, 512 experts, top-10 renormalised routing, expert intermediate 512, an
+always-on shared SwiGLU expert (intermediate 512) with a sigmoid gate,
+affine 8-bit group-64 weights -- at a decode batch of ``--tokens`` (256)
+tokens per GPU.  Every expert of the GPU's shard is resident in the arena
+(the reference's non-streaming branch), so a step is router -> routing ->
+dispatch -> gathered gate/up+SwiGLU -> down -> combine.  One step reads about
+1.7 GB of expert weights, well above the 126 MB L2, so no flush is needed.
+
+One JSON line on rank 0:
+  value     whole-job tokens/s, inputs resident in HBM, CUDA-event timed
+  e2e       tokens/s through the public layer call with the tokens copied
+            host->device and the output device->host every step
+  roofline  the routed gate/up kernel: algorithmic bytes / its event time
+  cpu_baseline  the CPU oracle port on a bounded token sample (rank 0, N=1)
+``--impl reference`` times that CPU port alone (the reference itself is MLX,
+which is not installed here) on the same workload, all host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "SlottedGLU tokens/s at 1/2/4/8 B200; expert-GEMM HBM GB/s vs 8 TB/s peak"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="cfg3")
+    ap.add_argument("--tokens", type=int, default=256, help="decode tokens per GPU per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def hbm_peak():
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"sg_clocks_{os.getpid()}.csv"
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU port (oracle)
+
+
+def cpu_port_step(cfg, x_bits, router_bits, expert_fn, shared, sgate_bits, threads):
+    """The CPU oracle's layer on a token sample, experts spread over threads."""
+    import numpy as np
+
+    from oracle import slotted_glu_oracle as orc
+
+    T = x_bits.shape[0]
+    x = orc.bf16_bits_to_f32(x_bits)
+    logits = orc.router_logits(x_bits, router_bits)
+    inds, sc, _ = orc.get_routings(logits, cfg.top_k, cfg.norm_topk_prob)
+    flat = inds.reshape(-1)
+    y = np.zeros((T * cfg.top_k, cfg.hidden), np.float32)
+
+    def run(eid):
+        pairs = np.nonzero(flat == eid)[0]
+        y[pairs] = orc.expert_forward(x[pairs // cfg.top_k], expert_fn(int(eid)))
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(run, np.unique(flat)))
+    sy = sg = None
+    if shared is not None:
+        sy = orc.expert_forward(x, shared)
+        sg = orc.bf16_bits_to_f32(orc.router_logits(x_bits, sgate_bits))
+    return orc.combine_shared(y.reshape(T, cfg.top_k, cfg.hidden), orc.bf16_bits_to_f32(sc), sy, sg)
+
+
+def _sample_tokens(cfg, n, i):
+    from preemptlm_b200.synthetic import _gen, _randn
+
+    return _randn((n, cfg.hidden), _gen(1000 * cfg.cfg_id + 500 + i, "cpu"), "cpu", 1.0)
+
+
+def _b16(t):
+    import numpy as np
+    import torch
+
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _deq(cfg, ts, i):
+    """Dequantised weights of expert ``i`` of a host tensor dict (the CPU
+    port's per-call dequantisation)."""
+    import numpy as np
+
+    from oracle import slotted_glu_oracle as orc
+
+    mats = []
+    for p in ("gate_proj", "up_proj", "down_proj"):
+        if cfg.bits == 16:
+            mats.append(orc.bf16_bits_to_f32(_b16(ts[f"{p}.weight"][i])))
+        else:
+            mats.append(orc.dequant_affine(ts[f"{p}.weight"][i].cpu().numpy().view(np.uint32),
+                                           _b16(ts[f"{p}.scales"][i]), _b16(ts[f"{p}.biases"][i]), cfg.bits))
+    return orc.ExpertWeights(*mats)
+
+
+def _host_layer(cfg, n_samples, sample_tokens, tens=None):
+    """Host copies of what the CPU port's samples touch: router, shared expert
+    and, per routed expert id, its packed tensors.  Copied from the GPU layer,
+    or generated on the host (reference arm: no GPU use at all; routed experts
+    then come from per-expert seeds).  Untimed set-up."""
+    from oracle import slotted_glu_oracle as orc
+    from preemptlm_b200.synthetic import _gen, _randn, make_expert_tensors
+
+    c = cfg.cfg_id
+    if tens is not None:
+        router, shared = tens["router"].cpu(), tens["shared"]
+        sgate = None if tens["shared_gate"] is None else tens["shared_gate"].cpu()
+    else:
+        router = _randn((cfg.num_experts, cfg.hidden), _gen(1000 * c + 1, "cpu"), "cpu", 0.02)
+        shared = sgate = None
+        if cfg.shared_inter is not None:
+            shared = make_expert_tensors(cfg, 1, cfg.shared_inter, 1000 * c + 3, "cpu")
+            sgate = _randn((1, cfg.hidden), _gen(1000 * c + 4, "cpu"), "cpu", 0.02)
+    if shared is not None:
+        shared = {k: v.cpu() for k, v in shared.items()}
+    needed = set()
+    rb = _b16(router)
+    for i in range(n_samples):
+        lg = orc.router_logits(_b16(_sample_tokens(cfg, sample_tokens, i)), rb)
+        needed.update(orc.get_routings(lg, cfg.top_k, cfg.norm_topk_prob)[0].reshape(-1).tolist())
+    experts = {}
+    for e in sorted(needed):
+        if tens is not None:
+            experts[e] = {k: v[e: e + 1].cpu() for k, v in tens["experts"].items()}
+        else:
+            experts[e] = make_expert_tensors(cfg, 1, cfg.inter, 1000 * c + 2 + 7919 * (e + 1), "cpu")
+    return experts, router, shared, sgate
+
+
+def time_cpu_port(cfg, sample_tokens, steps, host_layer, warmup=0):
+    threads = os.cpu_count() or 1
+    experts, router, shared_t, sgate = host_layer
+    rb = _b16(router)
+    sgate_bits = None if sgate is None else _b16(sgate)
+    expert_fn = lambda e: _deq(cfg, experts[e], 0)  # noqa: E731
+    times = []
+    for i in range(warmup + steps):
+        xb = _b16(_sample_tokens(cfg, sample_tokens, i))
+        t0 = time.perf_counter()
+        shared = None if shared_t is None else _deq(cfg, shared_t, 0)
+        cpu_port_step(cfg, xb, rb, expert_fn, shared, sgate_bits, threads)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return times, threads
+
+
+# --------------------------------------------------------------------------- our arm
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from preemptlm_b200 import ops
+    from preemptlm_b200.layer import Qwen3_xMoEWrapper
+    from preemptlm_b200.synthetic import CONFIGS, make_layer, make_tokens
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.workload]
+    if world > 1:
+        raise SystemExit("multi-GPU expert-parallel bench runs through preemptlm_b200.ep (see run_ep)")
+    T = args.tokens
+    block, tens = make_layer(cfg, device=dev)
+    moe = Qwen3_xMoEWrapper(block, "synthetic", "model.layers.0.mlp", 0)
+    n_in = args.warmup + args.steps
+    xs = [make_tokens(cfg, T, device=dev, step=i) for i in range(n_in)]
+    torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        moe.forward_resident(xs[i])
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- device-resident timing
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    timing: dict = {}
+    launches0 = ops.LAUNCHES[0]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        moe.forward_resident(xs[args.warmup + i], timing=timing)
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = ops.LAUNCHES[0] - launches0
+    ms_step = start.elapsed_time(end) / args.steps
+
+    # routed gate/up kernel: algorithmic bytes / event duration
+    H, I, k = cfg.hidden, cfg.inter, cfg.top_k
+    per_expert_gu = 2 * (I * H * cfg.bits // 8 + (I * H // 64) * 4 if cfg.bits != 16 else I * H * 2)
+    gu_ms, dn_ms, gu_bytes, dn_bytes, us = [], [], 0, 0, []
+    per_expert_dn = (H * I * cfg.bits // 8 + (H * I // 64) * 4) if cfg.bits != 16 else H * I * 2
+    for ev, d in zip(timing["events"], timing["dispatch"]):
+        U = int(d.counts[0].item())
+        us.append(U)
+        gu_ms.append(ev[0].elapsed_time(ev[1]))
+        dn_ms.append(ev[1].elapsed_time(ev[2]))
+        gu_bytes += U * per_expert_gu + T * H * 2 + T * k * I * 2
+        dn_bytes += U * per_expert_dn + T * k * I * 2 + T * k * H * 2
+    peak, peak_kind = hbm_peak()
+    gu_gbs = gu_bytes / (sum(gu_ms) * 1e-3) / 1e9
+    dn_gbs = dn_bytes / (sum(dn_ms) * 1e-3) / 1e9
+    # whole-step algorithmic bytes (every byte once): experts + shared + router + x + out
+    step_bytes = (statistics.mean(us) * cfg.expert_bytes() + cfg.shared_bytes() + cfg.num_experts * H * 2
+                  + 2 * T * H * 2)
+    step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    x_host = [torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for i, xh in enumerate(x_host):
+        xh.copy_(xs[i].cpu())
+    out_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    for i in range(args.warmup):
+        xd = x_host[i % 2].to(dev, non_blocking=True)
+        out_host.copy_(moe(xd.view(1, T, H)).view(T, H), non_blocking=True)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        xd = x_host[i % 2].to(dev, non_blocking=True)
+        out_host.copy_(moe(xd.view(1, T, H)).view(T, H), non_blocking=True)
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+
+    # ---------------------------------------------------------------- CPU baseline (oracle port)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample, n = 8, 4
+        times, threads = time_cpu_port(cfg, sample, n, _host_layer(cfg, n + 1, sample, tens), warmup=1)
+        cpu = {"value": round(sample * len(times) / sum(times), 3), "unit": "tokens/s", "cores": threads,
+               "kind": "port",
+               "sample": f"{len(times)} steps of {sample} tokens through the CPU oracle of the same layer "
+                         f"(routing, dequantise, fp32 matmul), experts over {threads} threads"}
+
+    value = T * world / (ms_step * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": f"u{cfg.bits}" if cfg.bits != 16 else "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)",
+        "config": {
+            "workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
+                        f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, decode {T} tokens/GPU, "
+                        f"all experts of the shard resident ({cfg.num_experts} slots)",
+            "tokens_per_gpu": T, "hidden": H, "experts": cfg.num_experts, "top_k": k, "inter": I,
+            "shared_inter": cfg.shared_inter, "bits": cfg.bits, "slots": cfg.num_experts,
+            "unique_experts_per_step": round(statistics.mean(us), 1),
+            "l2": "no flush: >1.7 GB of expert weights per step vs 126 MB L2",
+            "parallelism": f"ep{world}",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": "sg_glu_gate_up (routed, q8 GEMV)", "achieved": round(gu_gbs, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(gu_gbs / peak, 4), "peak_kind": peak_kind,
+            "traffic": None,
+            "bytes_per_launch": round(gu_bytes / len(gu_ms)), "ms_per_launch": round(statistics.mean(gu_ms), 5),
+            "down": {"achieved": round(dn_gbs, 1), "frac": round(dn_gbs / peak, 4),
+                     "ms_per_launch": round(statistics.mean(dn_ms), 5)},
+            "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+        },
+        "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- reference arm
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from preemptlm_b200.synthetic import CONFIGS
+
+    cfg = CONFIGS[args.workload]
+    sample = 4
+    host = _host_layer(cfg, args.warmup + args.steps, sample)
+    times, threads = time_cpu_port(cfg, sample, args.steps, host, warmup=args.warmup)
+    value = sample * len(times) / sum(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"u{cfg.bits}" if cfg.bits != 16 else "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)",
+        "config": {"workload": f"{cfg.name} (CPU port, {sample}-token sample per step)", "tokens_per_gpu": args.tokens,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens per step through the CPU oracle of the layer; the reference's "
+                                   "MLX path cannot be installed here (mlx/mlx-lm absent, no network)"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus if args.gpus == 1 else 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+/*
+ * sg_abi.h -- C-ABI of the B200 SlottedGLU MoE hot path (libsg_b200.so).
+ *
+ * Every entry point is extern "C", takes plain device pointers, sizes and a
+ * cudaStream_t passed as void*, returns an int status (SG_OK == 0, negative on
+ * error) and never throws.  The caller owns every buffer.  No entry point
+ * synchronises the stream except sg_refill_h2d's optional host wait.
+ *
+ * bf16 values are passed as uint16_t bit patterns.  A call whose token or pair
+ * count is 0 returns SG_OK without touching its (possibly NULL) data pointers.  Layout conventions follow
+ * the reference (preemptLM, preempt/backends/mlx_metal/...):
+ *   x        [T, H]            bf16 hidden states, row-major
+ *   router   [E, H]            bf16 (mlx_lm nn.Linear weight, out x in)
+ *   arena    gate/up [S, I, H], down [S, H, I]   (SlottedGLU, expert_cache.py:199-224)
+ *            or MLX affine: packed uint32 [S, out, in*bits/32] little-endian,
+ *            scales/biases bf16 [S, out, in/group_size]
+ *   pairs    p = t*k + j  (token t, routing rank j)
+ */
+#ifndef SG_ABI_H
+#define SG_ABI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum sg_status {
+  SG_OK = 0,
+  SG_ERR_INVALID_ARG = -1,   /* null pointer / negative size */
+  SG_ERR_SHAPE = -2,         /* unsupported dimension (see each call) */
+  SG_ERR_FORMAT = -3,        /* unsupported weight format (bits / group size) */
+  SG_ERR_CUDA = -4,          /* a CUDA runtime call or launch failed */
+  SG_ERR_CAPACITY = -5,      /* a caller buffer is too small */
+  SG_ERR_TIMEOUT = -6,       /* a bounded wait gave up */
+};
+
+/* Human-readable text of a status code (static storage). */
+const char* sg_status_string(int status);
+
+/* Library version, and the SM architecture the kernels were built for (1000). */
+int sg_version(void);
+int sg_built_arch(void);
+
+/* --------------------------------------------------------------- the arena
+ * Pre-allocated per-layer slot arena: SlottedGLU (expert_cache.py:199-224),
+ * plus MLX affine 4/8-bit layouts (ops/fused.py:77-88 calling convention,
+ * quantization.py:16-40 QuantSettings).  bits == 16 means plain bf16 weights
+ * (scale/bias pointers unused).  group_size must be 64 for bits 4 and 8. */
+typedef struct sg_arena {
+  int32_t num_slots;  /* S */
+  int32_t hidden;     /* H */
+  int32_t inter;      /* I */
+  int32_t bits;       /* 16, 8 or 4 */
+  int32_t group_size; /* 64 (affine) */
+  int32_t reserved;
+  const void* gate_w; const void* gate_s; const void* gate_b;
+  const void* up_w;   const void* up_s;   const void* up_b;
+  const void* down_w; const void* down_s; const void* down_b;
+} sg_arena;
+
+/* ----------------------------------------------------------- router (a1)
+ * logits[T, E] = bf16(x[T, H] @ w[E, H]^T), fp32 accumulation in a fixed order
+ * (32 lane partials over h = 256*i + 8*lane + e, then a pairwise fold).
+ * Replaces the router call `logits = self.inner.gate(x)` at
+ * preempt/backends/mlx_metal/module_wrappers/qwen3_x_moe.py:254 and the shared
+ * expert gate `self.inner.shared_expert_gate(x)` at qwen3_x_moe.py:259.
+ * Requires H % 256 == 0, E >= 1. */
+int sg_router_logits(const uint16_t* x, const uint16_t* w, uint16_t* logits,
+                     int T, int H, int E, void* stream);
+
+/* ---------------------------------------------------------- routing (a2)
+ * softmax(precise) -> top-k in the order (gate desc, expert id asc) ->
+ * optional renormalisation.  inds[T, k] int32, scores[T, k] bf16.
+ * Replaces `_get_routings` at qwen3_x_moe.py:26-40.
+ * Requires E % 32 == 0, E <= 1024, 1 <= k <= 32, k <= E. */
+int sg_route_topk(const uint16_t* logits, int T, int E, int k, int norm_topk_prob,
+                  int32_t* inds, uint16_t* scores, void* stream);
+
+/* --------------------------------------------------------- dispatch (a3/a6)
+ * Device-side replacement for the host part of `_maybe_admit`
+ * (qwen3_x_moe.py:145-156: np.unique with inverse, the miss set) and for
+ * `slot_ids = self._eid_lookup_table[unique_eids]` (qwen3_x_moe.py:277).
+ * One CTA; all scratch lives in shared memory.
+ *   in : inds[P] (P = T*k pair expert ids), eid2sid[E] (-1 = not resident)
+ *   out: unique[U] ascending, inverse[P], counts[0] = U, counts[1] = #missed,
+ *        slot_ids[U] = eid2sid[unique], miss_eids[#missed] ascending,
+ *        group_off[U+1] (pairs of unique u are perm[group_off[u]..group_off[u+1]) ),
+ *        perm[P] pair ids grouped by unique index.
+ *   max_unique bounds unique/slot_ids/miss_eids/group_off (needs >= min(P, E) + 1).
+ *   With P == 0, inds/inverse/perm may be NULL (counts and group_off[0] are still written).
+ * Requires 1 <= E <= 8192. */
+int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
+                int32_t* unique, int32_t* inverse, int32_t* counts,
+                int32_t* slot_ids, int32_t* miss_eids, int32_t* group_off,
+                int32_t* perm, int max_unique, void* stream);
+
+/* ------------------------------------------------- gathered SwiGLU (a9/a10)
+ * h[p, I] = swiglu(x[p / pair_div] @ gate^T, ... @ up^T) for every pair p of
+ * every group u < counts[0], against arena slot slot_ids[u]; pairs listed by
+ * perm/group_off (sg_dispatch layout).  Rounds x_up, x_gate, sigmoid, silu and
+ * the product to bf16 (experts.py:26-28).  pair_div = k for routed experts,
+ * 1 when pairs are tokens (the shared expert).  grid_groups is a host-side
+ * upper bound on counts[0].
+ * Replaces the up/gate `gather_mm` calls and `swiglu_activation` in
+ * `_gather_forward`, qwen3_x_moe.py:225-242.
+ * Requires H % 64 == 0 and I % 64 == 0. */
+int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int pair_div,
+                   const int32_t* counts, const int32_t* slot_ids,
+                   const int32_t* group_off, const int32_t* perm,
+                   int grid_groups, uint16_t* h, void* stream);
+
+/* y[p, H] = bf16(h[p, I] @ down^T) for every listed pair.
+ * Replaces the down `gather_mm` in `_gather_forward`, qwen3_x_moe.py:243-248. */
+int sg_glu_down(const sg_arena* arena, const uint16_t* h,
+                const int32_t* counts, const int32_t* slot_ids,
+                const int32_t* group_off, const int32_t* perm,
+                int grid_groups, uint16_t* y, void* stream);
+
+/* ---------------------------------------------------------- combine (a11)
+ * out[t] = bf16( bf16(sum_j bf16(y[t*k+j] * scores[t, j]))
+ *               + bf16(bf16(sigmoid(shared_gate[t])) * shared_y[t]) )
+ * The k-sum adds in fp32 in j order.  shared_y / shared_gate may both be NULL
+ * (no shared expert).  Replaces `_combine_shared`, qwen3_x_moe.py:71-80.
+ * Requires H % 8 == 0. */
+int sg_combine(const uint16_t* y, const uint16_t* scores, int T, int k, int H,
+               const uint16_t* shared_y, const uint16_t* shared_gate,
+               uint16_t* out, void* stream);
+
+/* ------------------------------------------------------------ refill (a8)
+ * Copies one serialized expert blob (pinned host memory, tensors concatenated
+ * in the bank's tensor_specs order: gate, up, down x weight[, scales, biases])
+ * into arena slot `sid` with one cudaMemcpyAsync per tensor on `stream`.
+ * Replaces `decode_serialized_expert` + the slot writes
+ * `self._weight_slots.{up,down,gate}_proj[sid] = ...` at
+ * qwen3_x_moe.py:186-195 (expert_cache.py:24-80).  blob_len must equal the
+ * expert's byte size for the arena format, else SG_ERR_SHAPE. */
+int sg_refill_h2d(const void* blob, size_t blob_len, const sg_arena* arena,
+                  int sid, void* stream);
+
+/* Byte size of one expert blob in the arena's format. */
+size_t sg_expert_bytes(const sg_arena* arena);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SG_ABI_H */

@@ -1,0 +1,293 @@
+// Gathered SwiGLU expert matmuls over the slot arena (a9, a10, a12):
+// streaming GEMV-style kernels for decode batch sizes.
+//
+// Work item = (group u, block of output rows).  A group is one expert slot with
+// the pairs routed to it (sg_dispatch layout).  Eight warps per CTA; each warp
+// owns WROWS weight rows and splits K across lanes in chunks of 16 weights
+// (lane j takes chunks j, j+32, ...).  The pairs' input rows are staged in
+// shared memory NT at a time.  Affine weights are never expanded: per chunk a
+// lane forms dot = sum(q * x) and xs = sum(x) and adds scale*dot + bias*xs,
+// which equals sum((scale*q + bias) * x) without the bf16 rounding of w.
+#include "sg_common.cuh"
+
+namespace sg {
+
+constexpr int GW_WARPS = 8;
+constexpr int GW_NT = 8;      // pairs staged per pass
+constexpr int GW_CHUNK = 16;  // weights per lane step
+
+// --------------------------------------------------------------- weight chunk
+template <int BITS>
+struct Chunk;
+
+template <>
+struct Chunk<16> {  // 16 bf16 = 32 bytes
+  uint4 a, b;
+  __device__ __forceinline__ void load(const uint8_t* row, int c) {
+    const uint4* p = reinterpret_cast<const uint4*>(row + (size_t)c * 32);
+    a = ldg_nc_v4(p);
+    b = ldg_nc_v4(p + 1);
+  }
+  __device__ __forceinline__ void to_float(float* w) const {
+    const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      w[2 * i] = lo_bf16(v[i]);
+      w[2 * i + 1] = hi_bf16(v[i]);
+    }
+  }
+};
+
+__device__ __forceinline__ float u8f(uint32_t q) {  // exact small unsigned int -> fp32
+  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+}
+
+template <>
+struct Chunk<8> {  // 16 x u8 = 16 bytes
+  uint4 a;
+  __device__ __forceinline__ void load(const uint8_t* row, int c) {
+    a = ldg_nc_v4(row + (size_t)c * 16);
+  }
+  __device__ __forceinline__ void to_float(float* w) const {
+    const uint32_t v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) w[4 * i + m] = u8f((v[i] >> (8 * m)) & 0xFFu);
+  }
+};
+
+template <>
+struct Chunk<4> {  // 16 x u4 = 8 bytes
+  uint2 a;
+  __device__ __forceinline__ void load(const uint8_t* row, int c) {
+    a = __ldg(reinterpret_cast<const uint2*>(row + (size_t)c * 8));
+  }
+  __device__ __forceinline__ void to_float(float* w) const {
+    const uint32_t v[2] = {a.x, a.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int m = 0; m < 8; ++m) w[8 * i + m] = u8f((v[i] >> (4 * m)) & 0xFu);
+  }
+};
+
+struct Mat {  // one projection of the arena
+  const uint8_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+  int out, k;
+};
+
+__device__ __forceinline__ size_t row_bytes(int bits, int k) { return (size_t)k * bits / 8; }
+
+// Accumulate WROWS rows x NT pairs over the whole K range.
+template <int BITS, int WROWS, int NT>
+__device__ __forceinline__ void gemv_rows(const Mat* mats, const int* mrow, int slot, const uint16_t* xs_smem, int K,
+                                          float (&acc)[WROWS][GW_NT]) {
+  const int lane = threadIdx.x & 31;
+  const int nchunks = K / GW_CHUNK;
+  const int groups = K / 64;
+  for (int c = lane; c < nchunks; c += 32) {
+    Chunk<BITS> ch[WROWS];
+    float sc[WROWS], bi[WROWS];
+#pragma unroll
+    for (int a = 0; a < WROWS; ++a) {
+      const Mat& m = mats[a];
+      const size_t r = (size_t)slot * m.out + mrow[a];
+      ch[a].load(m.w + r * row_bytes(BITS, K), c);
+      if (BITS != 16) {
+        sc[a] = bf16_to_f32(__ldg(m.s + r * groups + (c >> 2)));
+        bi[a] = bf16_to_f32(__ldg(m.b + r * groups + (c >> 2)));
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NT; ++b) {
+      const uint4* xp = reinterpret_cast<const uint4*>(xs_smem + (size_t)b * K + (size_t)c * GW_CHUNK);
+      const uint4 x0 = xp[0], x1 = xp[1];
+      const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      float xf[16];
+      float xsum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xf[2 * i] = lo_bf16(xv[i]);
+        xf[2 * i + 1] = hi_bf16(xv[i]);
+      }
+      if (BITS != 16) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xsum += xf[i];
+      }
+#pragma unroll
+      for (int a = 0; a < WROWS; ++a) {
+        float wf[16];
+        ch[a].to_float(wf);
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dot = fmaf(wf[i], xf[i], dot);
+        if (BITS != 16) {
+          acc[a][b] = fmaf(sc[a], dot, acc[a][b]);
+          acc[a][b] = fmaf(bi[a], xsum, acc[a][b]);
+        } else {
+          acc[a][b] += dot;
+        }
+      }
+    }
+  }
+}
+
+// DUAL: gate/up fused with SwiGLU -> h[p, I];  !DUAL: down -> y[p, H].
+template <int BITS, bool DUAL>
+__global__ void __launch_bounds__(GW_WARPS * 32)
+gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, const int32_t* __restrict__ counts,
+                const int32_t* __restrict__ slot_ids, const int32_t* __restrict__ group_off,
+                const int32_t* __restrict__ perm, uint16_t* __restrict__ out) {
+  constexpr int WROWS = 4;                        // weight rows per warp
+  constexpr int OROWS = DUAL ? WROWS / 2 : WROWS;  // output rows per warp
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);  // [GW_NT][K]
+  const int u = blockIdx.y;
+  if (u >= counts[0]) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int H = A.hidden, I = A.inter;
+  const int K = DUAL ? H : I;
+  const int OUT = DUAL ? I : H;
+  const int orow0 = (blockIdx.x * GW_WARPS + warp) * OROWS;
+  const int slot = slot_ids[u];
+  const int p_begin = group_off[u], p_end = group_off[u + 1];
+  const bool slot_ok = slot >= 0 && slot < A.num_slots;
+
+  Mat mats[WROWS];
+  int mrow[WROWS];
+#pragma unroll
+  for (int a = 0; a < WROWS; ++a) {
+    int r = DUAL ? orow0 + (a % OROWS) : orow0 + a;
+    mrow[a] = r < OUT ? r : OUT - 1;  // clamp reads; writes are masked
+    if (DUAL) {
+      const bool g = a < OROWS;
+      mats[a] = Mat{static_cast<const uint8_t*>(g ? A.gate_w : A.up_w), static_cast<const uint16_t*>(g ? A.gate_s : A.up_s),
+                    static_cast<const uint16_t*>(g ? A.gate_b : A.up_b), I, H};
+    } else {
+      mats[a] = Mat{static_cast<const uint8_t*>(A.down_w), static_cast<const uint16_t*>(A.down_s),
+                    static_cast<const uint16_t*>(A.down_b), H, I};
+    }
+  }
+
+  for (int p0 = p_begin; p0 < p_end; p0 += GW_NT) {
+    const int nb = min(GW_NT, p_end - p0);
+    __syncthreads();
+    const int cpr = K / 8;  // 16-byte chunks per row
+    for (int c = threadIdx.x; c < GW_NT * cpr; c += blockDim.x) {
+      int b = c / cpr, cc = c - b * cpr;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (b < nb) {
+        int row = perm[p0 + b] / pair_div;
+        v = reinterpret_cast<const uint4*>(xin + (size_t)row * K)[cc];
+      }
+      reinterpret_cast<uint4*>(xs)[c] = v;
+    }
+    __syncthreads();
+    float acc[WROWS][GW_NT];
+#pragma unroll
+    for (int a = 0; a < WROWS; ++a)
+#pragma unroll
+      for (int b = 0; b < GW_NT; ++b) acc[a][b] = 0.0f;
+    if (slot_ok && orow0 < OUT) {
+      if (nb == 1) gemv_rows<BITS, WROWS, 1>(mats, mrow, slot, xs, K, acc);
+      else if (nb == 2) gemv_rows<BITS, WROWS, 2>(mats, mrow, slot, xs, K, acc);
+      else if (nb <= 4) gemv_rows<BITS, WROWS, 4>(mats, mrow, slot, xs, K, acc);
+      else gemv_rows<BITS, WROWS, GW_NT>(mats, mrow, slot, xs, K, acc);
+    }
+    if (orow0 >= OUT) continue;
+    // fold partials and write: lane (o * GW_NT + b) owns output row o, pair b
+#pragma unroll
+    for (int o = 0; o < OROWS; ++o) {
+#pragma unroll
+      for (int b = 0; b < GW_NT; ++b) {
+        if (b >= nb) break;
+        const int r = orow0 + o;
+        if (DUAL) {
+          float g = warp_fold_sum(acc[o][b]);
+          float up = warp_fold_sum(acc[o + OROWS][b]);
+          if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
+            const int p = perm[p0 + b];
+            out[(size_t)p * OUT + r] = slot_ok ? swiglu_bf16(g, up) : (uint16_t)0;
+          }
+        } else {
+          float y = warp_fold_sum(acc[o][b]);
+          if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
+            const int p = perm[p0 + b];
+            out[(size_t)p * OUT + r] = slot_ok ? f32_to_bf16(y) : (uint16_t)0;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int BITS, bool DUAL>
+static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
+                       const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                       uint16_t* out, cudaStream_t s) {
+  const int K = DUAL ? A->hidden : A->inter;
+  const int OUT = DUAL ? A->inter : A->hidden;
+  const int orows_cta = GW_WARPS * (DUAL ? 2 : 4);
+  const size_t smem = (size_t)GW_NT * K * 2;
+  static bool attr_done = false;
+  if (!attr_done) {
+    SG_CUDA_TRY(cudaFuncSetAttribute(gemv_glu_kernel<BITS, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     160 * 1024));
+    attr_done = true;
+  }
+  dim3 grid((OUT + orows_cta - 1) / orows_cta, grid_groups);
+  gemv_glu_kernel<BITS, DUAL><<<grid, GW_WARPS * 32, smem, s>>>(*A, xin, pair_div, counts, slot_ids, group_off,
+                                                                 perm, out);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+int check_arena(const sg_arena* A) {
+  if (!A || !A->gate_w || !A->up_w || !A->down_w) return SG_ERR_INVALID_ARG;
+  if (A->num_slots < 1 || A->hidden < 64 || A->inter < 64) return SG_ERR_SHAPE;
+  if (A->hidden % 64 || A->inter % 64) return SG_ERR_SHAPE;
+  if ((size_t)A->hidden * 2 * GW_NT > 160 * 1024) return SG_ERR_SHAPE;
+  if (A->bits == 16) return SG_OK;
+  if (A->bits != 4 && A->bits != 8) return SG_ERR_FORMAT;
+  if (A->group_size != 64) return SG_ERR_FORMAT;
+  if (!A->gate_s || !A->gate_b || !A->up_s || !A->up_b || !A->down_s || !A->down_b) return SG_ERR_INVALID_ARG;
+  return SG_OK;
+}
+
+}  // namespace sg
+
+extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int pair_div, const int32_t* counts,
+                              const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm,
+                              int grid_groups, uint16_t* h, void* stream) {
+  int st = sg::check_arena(arena);
+  if (st) return st;
+  if (!x || !counts || !slot_ids || !group_off || !perm || !h || pair_div < 1 || grid_groups < 0)
+    return SG_ERR_INVALID_ARG;
+  if (grid_groups == 0) return SG_OK;
+  if (grid_groups > 65535) return SG_ERR_SHAPE;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (arena->bits) {
+    case 16: return sg::launch_gemv<16, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
+    case 8: return sg::launch_gemv<8, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
+    default: return sg::launch_gemv<4, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
+  }
+}
+
+extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, const int32_t* counts, const int32_t* slot_ids,
+                           const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* y,
+                           void* stream) {
+  int st = sg::check_arena(arena);
+  if (st) return st;
+  if (!h || !counts || !slot_ids || !group_off || !perm || !y || grid_groups < 0) return SG_ERR_INVALID_ARG;
+  if (grid_groups == 0) return SG_OK;
+  if (grid_groups > 65535) return SG_ERR_SHAPE;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (arena->bits) {
+    case 16: return sg::launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
+    case 8: return sg::launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
+    default: return sg::launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
+  }
+}

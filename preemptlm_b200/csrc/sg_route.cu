@@ -1,0 +1,302 @@
+// Router logits (a1), softmax/top-k/renorm (a2) and the device-side unique /
+// inverse / slot lookup / pair permutation (a3, a6) of the slotted MoE block.
+#include "sg_common.cuh"
+
+namespace sg {
+
+// ============================================================== router logits
+// CTA = 8 warps; a CTA covers RT_TOK tokens x (8 * RT_EXP) experts.  Each warp
+// owns RT_EXP experts and all RT_TOK tokens of the tile; lane j accumulates
+// h = 256*i + 8*j + e in (i, e) order, then every (expert, token) partial is
+// folded 16, 8, 4, 2, 1 across the warp.  x for the token tile is staged in
+// shared memory; router rows stream from global (read once per token tile).
+constexpr int RT_TOK = 8;
+constexpr int RT_EXP = 4;
+constexpr int RT_WARPS = 8;
+
+__global__ void __launch_bounds__(RT_WARPS * 32)
+router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                     uint16_t* __restrict__ logits, int T, int H, int E) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint4* xs = reinterpret_cast<uint4*>(smem_raw);  // [RT_TOK][H/8] 16-byte chunks
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * RT_TOK;
+  const int e0 = (blockIdx.y * RT_WARPS + warp) * RT_EXP;
+  const int chunks = H >> 3;  // 16-byte chunks per row
+
+  for (int c = threadIdx.x; c < RT_TOK * chunks; c += blockDim.x) {
+    int tt = c / chunks, cc = c - tt * chunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t0 + tt < T) v = reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H)[cc];
+    xs[c] = v;
+  }
+  __syncthreads();
+
+  float acc[RT_EXP][RT_TOK];
+#pragma unroll
+  for (int a = 0; a < RT_EXP; ++a)
+#pragma unroll
+    for (int b = 0; b < RT_TOK; ++b) acc[a][b] = 0.0f;
+
+  const int iters = H >> 8;
+  for (int i = 0; i < iters; ++i) {
+    const int cc = i * 32 + lane;  // this lane's 16-byte chunk of the row
+    uint4 wv[RT_EXP];
+#pragma unroll
+    for (int a = 0; a < RT_EXP; ++a) {
+      int e = e0 + a;
+      wv[a] = (e < E) ? ldg_nc_v4(w + (size_t)e * H + (size_t)cc * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int b = 0; b < RT_TOK; ++b) {
+      uint4 xv = xs[b * chunks + cc];
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int a = 0; a < RT_EXP; ++a) {
+        const uint32_t ww[4] = {wv[a].x, wv[a].y, wv[a].z, wv[a].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          // element order e = 2q, 2q+1 within the chunk; products are exact
+          acc[a][b] = __fmaf_rn(lo_bf16(xw[q]), lo_bf16(ww[q]), acc[a][b]);
+          acc[a][b] = __fmaf_rn(hi_bf16(xw[q]), hi_bf16(ww[q]), acc[a][b]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < RT_EXP; ++a) {
+#pragma unroll
+    for (int b = 0; b < RT_TOK; ++b) {
+      float s = warp_fold_sum(acc[a][b]);
+      int e = e0 + a, t = t0 + b;
+      if (lane == ((a * RT_TOK + b) & 31) && e < E && t < T) logits[(size_t)t * E + e] = f32_to_bf16(s);
+    }
+  }
+}
+
+// ============================================================== routing
+// One warp per token.  Lane j holds logits e = j + 32c.  softmax in fp32 with
+// routing_exp and the lane-order sum, gates rounded to bf16, then k rounds of
+// a warp-wide max over the key (gate_bits << 16) | (0xFFFF - e), which orders
+// by gate descending and expert id ascending.
+template <int C>
+__global__ void __launch_bounds__(256)
+route_topk_kernel(const uint16_t* __restrict__ logits, int T, int E, int k, int norm,
+                  int32_t* __restrict__ inds, uint16_t* __restrict__ scores) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint16_t* row = logits + (size_t)t * E;
+  float v[C];
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    v[c] = bf16_to_f32(row[c * 32 + lane]);
+    m = fmaxf(m, v[c]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    v[c] = routing_exp(__fsub_rn(v[c], m));
+    s = __fadd_rn(s, v[c]);
+  }
+  s = warp_fold_sum(s);
+  uint32_t key[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    uint32_t g = f32_to_bf16(__fdiv_rn(v[c], s));
+    key[c] = (g << 16) | (0xFFFFu - static_cast<uint32_t>(c * 32 + lane));
+  }
+  float ssum = 0.0f;
+  uint32_t my_key = 0;  // lane j keeps the j-th selected key
+  for (int j = 0; j < k; ++j) {
+    uint32_t best = 0;
+#pragma unroll
+    for (int c = 0; c < C; ++c) best = key[c] > best ? key[c] : best;
+    best = __reduce_max_sync(0xffffffffu, best);
+    const int e = static_cast<int>(0xFFFFu - (best & 0xFFFFu));
+    if ((e & 31) == lane) {
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        if (c == (e >> 5)) key[c] = 0;
+    }
+    if (lane == j) my_key = best;
+    ssum = __fadd_rn(ssum, bf16_to_f32(static_cast<uint16_t>(best >> 16)));
+  }
+  if (lane < k) {
+    const int e = static_cast<int>(0xFFFFu - (my_key & 0xFFFFu));
+    float sc = bf16_to_f32(static_cast<uint16_t>(my_key >> 16));
+    if (norm) sc = __fdiv_rn(sc, round_bf16(ssum));
+    inds[(size_t)t * k + lane] = e;
+    scores[(size_t)t * k + lane] = f32_to_bf16(sc);
+  }
+}
+
+// ============================================================== dispatch
+// Single CTA of 1024 threads.  Shared memory: cnt[E] (pair counts, later the
+// scatter cursor) and rank[E] (index of e among the present experts).
+constexpr int DSP_THREADS = 1024;
+
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_tot, int* total) {
+  // exclusive scan over the block in thread order; returns prefix of v
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int wv = (lane < (blockDim.x >> 5)) ? warp_tot[lane] : 0;
+    int wi = wv;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int o = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += o;
+    }
+    if (lane < (blockDim.x >> 5)) warp_tot[lane] = wi - wv;
+    if (lane == 31) *total = wi;
+  }
+  __syncthreads();
+  int r = incl - v + warp_tot[warp];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(DSP_THREADS)
+dispatch_kernel(const int32_t* __restrict__ inds, int P, int E, const int32_t* __restrict__ eid2sid,
+                int32_t* __restrict__ unique, int32_t* __restrict__ inverse, int32_t* __restrict__ counts,
+                int32_t* __restrict__ slot_ids, int32_t* __restrict__ miss_eids,
+                int32_t* __restrict__ group_off, int32_t* __restrict__ perm) {
+  extern __shared__ int smem_i[];
+  int* cnt = smem_i;        // [E]
+  int* rank = smem_i + E;   // [E]
+  __shared__ int warp_tot[32];
+  __shared__ int tot_a, tot_b, tot_c;
+
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    int e = inds[p];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+
+  // each thread owns a contiguous run of experts [e_lo, e_hi)
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int e_lo = min(E, threadIdx.x * per), e_hi = min(E, e_lo + per);
+  int n_present = 0, n_pairs = 0, n_miss = 0;
+  for (int e = e_lo; e < e_hi; ++e) {
+    if (cnt[e] > 0) {
+      ++n_present;
+      n_pairs += cnt[e];
+      if (eid2sid[e] < 0) ++n_miss;
+    }
+  }
+  int base_u = block_excl_scan(n_present, warp_tot, &tot_a);
+  int base_p = block_excl_scan(n_pairs, warp_tot, &tot_b);
+  int base_m = block_excl_scan(n_miss, warp_tot, &tot_c);
+  for (int e = e_lo; e < e_hi; ++e) {
+    int c = cnt[e];
+    if (c > 0) {
+      int sid = eid2sid[e];
+      unique[base_u] = e;
+      slot_ids[base_u] = sid;
+      group_off[base_u] = base_p;
+      if (sid < 0) miss_eids[base_m++] = e;
+      rank[e] = base_u++;
+      cnt[e] = base_p;  // becomes the scatter cursor
+      base_p += c;
+    }
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = tot_a;
+    counts[1] = tot_c;
+    group_off[tot_a] = tot_b;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    int e = inds[p];
+    if (e >= 0 && e < E) {
+      int pos = atomicAdd(&cnt[e], 1);
+      perm[pos] = p;
+      inverse[p] = rank[e];
+    } else {
+      inverse[p] = -1;
+    }
+  }
+}
+
+}  // namespace sg
+
+// ============================================================== C-ABI
+extern "C" int sg_router_logits(const uint16_t* x, const uint16_t* w, uint16_t* logits, int T, int H,
+                                int E, void* stream) {
+  if (T < 0 || E < 1 || H < 256) return SG_ERR_INVALID_ARG;
+  if (H % 256 != 0) return SG_ERR_SHAPE;
+  if (T == 0) return SG_OK;
+  if (!x || !w || !logits) return SG_ERR_INVALID_ARG;
+  const size_t smem = (size_t)sg::RT_TOK * H * 2;
+  if (smem > 200 * 1024) return SG_ERR_SHAPE;
+  static bool attr_done = false;
+  if (!attr_done) {
+    SG_CUDA_TRY(cudaFuncSetAttribute(sg::router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024));
+    attr_done = true;
+  }
+  dim3 grid((T + sg::RT_TOK - 1) / sg::RT_TOK, (E + sg::RT_WARPS * sg::RT_EXP - 1) / (sg::RT_WARPS * sg::RT_EXP));
+  sg::router_logits_kernel<<<grid, sg::RT_WARPS * 32, smem, (cudaStream_t)stream>>>(x, w, logits, T, H, E);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_route_topk(const uint16_t* logits, int T, int E, int k, int norm_topk_prob, int32_t* inds,
+                             uint16_t* scores, void* stream) {
+  if (T < 0) return SG_ERR_INVALID_ARG;
+  if (E % 32 != 0 || E < 32 || E > 1024 || k < 1 || k > 32 || k > E) return SG_ERR_SHAPE;
+  if (T == 0) return SG_OK;
+  if (!logits || !inds || !scores) return SG_ERR_INVALID_ARG;
+  const int warps = 8;
+  dim3 grid((T + warps - 1) / warps);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int C = E / 32;
+#define SG_ROUTE_CASE(CC) \
+  case CC: sg::route_topk_kernel<CC><<<grid, warps * 32, 0, s>>>(logits, T, E, k, norm_topk_prob, inds, scores); break;
+  switch (C) {
+    SG_ROUTE_CASE(1) SG_ROUTE_CASE(2) SG_ROUTE_CASE(3) SG_ROUTE_CASE(4) SG_ROUTE_CASE(5) SG_ROUTE_CASE(6)
+    SG_ROUTE_CASE(7) SG_ROUTE_CASE(8) SG_ROUTE_CASE(9) SG_ROUTE_CASE(10) SG_ROUTE_CASE(11) SG_ROUTE_CASE(12)
+    SG_ROUTE_CASE(13) SG_ROUTE_CASE(14) SG_ROUTE_CASE(15) SG_ROUTE_CASE(16) SG_ROUTE_CASE(17)
+    SG_ROUTE_CASE(18) SG_ROUTE_CASE(19) SG_ROUTE_CASE(20) SG_ROUTE_CASE(21) SG_ROUTE_CASE(22)
+    SG_ROUTE_CASE(23) SG_ROUTE_CASE(24) SG_ROUTE_CASE(25) SG_ROUTE_CASE(26) SG_ROUTE_CASE(27)
+    SG_ROUTE_CASE(28) SG_ROUTE_CASE(29) SG_ROUTE_CASE(30) SG_ROUTE_CASE(31) SG_ROUTE_CASE(32)
+    default: return SG_ERR_SHAPE;
+  }
+#undef SG_ROUTE_CASE
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid, int32_t* unique,
+                           int32_t* inverse, int32_t* counts, int32_t* slot_ids, int32_t* miss_eids,
+                           int32_t* group_off, int32_t* perm, int max_unique, void* stream) {
+  if (P < 0 || !eid2sid || !unique || !counts || !slot_ids || !miss_eids || !group_off) return SG_ERR_INVALID_ARG;
+  if (P > 0 && (!inds || !inverse || !perm)) return SG_ERR_INVALID_ARG;
+  if (E < 1 || E > 8192) return SG_ERR_SHAPE;
+  const int need = (P < E ? P : E) + 1;
+  if (max_unique < need) return SG_ERR_CAPACITY;
+  const size_t smem = (size_t)2 * E * sizeof(int);
+  static bool attr_done = false;
+  if (!attr_done) {
+    SG_CUDA_TRY(cudaFuncSetAttribute(sg::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+    attr_done = true;
+  }
+  sg::dispatch_kernel<<<1, sg::DSP_THREADS, smem, (cudaStream_t)stream>>>(inds, P, E, eid2sid, unique, inverse,
+                                                                           counts, slot_ids, miss_eids, group_off,
+                                                                           perm);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}

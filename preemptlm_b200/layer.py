@@ -1,0 +1,290 @@
+"""The slotted MoE block: ``Qwen3_xMoEWrapper`` on B200.
+
+Mirrors preempt/backends/mlx_metal/module_wrappers/qwen3_x_moe.py:85-337:
+the constructor arguments, ``_maybe_admit``, ``_gather_forward``, ``_touch``,
+``_choose_slots``, ``__call__`` and ``make_wrapper_factory`` keep their names
+and meaning.  The math runs in the libsg_b200 kernels:
+
+  router GEMV -> routing (softmax/top-k/renorm) -> device dispatch
+  (unique, inverse, slot lookup, permutation) -> gate/up + SwiGLU -> down
+  -> weighted combine with the sigmoid-gated shared expert.
+
+Differences from the reference, all deliberate:
+* the device->host sync of the routed ids (qwen3_x_moe.py:145) is replaced by
+  a device-side unique/lookup; the host reads back two counters, and the
+  unique ids only when a slot must be refilled;
+* ``mx.take`` copies of the arena (qwen3_x_moe.py:225-227) are gone: the
+  kernels read slots in place;
+* when the non-streaming branch is taken (``expert_cache is None``,
+  qwen3_x_moe.py:272-273) the full expert stack ``inner.switch_mlp`` is an
+  arena with slot == expert id.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import numpy as np
+import torch
+
+from . import ops
+from .arena import SlottedGLU
+from .quant import QuantSettings
+from .slot_map import EMPTY, SlotTable
+
+BaseMoEWrapper = SlotTable
+
+
+@dataclass
+class SparseMoeBlock:
+    """The fields of mlx_lm's ``Qwen3NextSparseMoeBlock`` that the wrapper uses
+    (``gate``, ``switch_mlp``, ``shared_expert``, ``shared_expert_gate``,
+    ``top_k``, ``norm_topk_prob``, ``num_experts``), as torch tensors.
+
+    gate: router weight [E, H] bf16.  switch_mlp: all routed experts as an
+    arena with one slot per expert, or None when the experts are streamed.
+    shared_expert: a one-slot arena, or None.  shared_expert_gate: [1, H] bf16.
+    """
+
+    gate: torch.Tensor
+    top_k: int
+    norm_topk_prob: bool
+    moe_intermediate_size: int
+    quant: QuantSettings | None = None
+    switch_mlp: SlottedGLU | None = None
+    shared_expert: SlottedGLU | None = None
+    shared_expert_gate: torch.Tensor | None = None
+    sharding_group: object | None = None
+
+    @property
+    def num_experts(self) -> int:
+        return int(self.gate.shape[0])
+
+    @property
+    def hidden_size(self) -> int:
+        return int(self.gate.shape[1])
+
+
+# --------------------------------------------------------------------------- functional pieces
+
+
+def _get_routings(logits: torch.Tensor, top_k: int, norm_topk_prob: bool):
+    """qwen3_x_moe.py:26-40.  Returns (inds int32 [T, k], scores bf16 [T, k])
+    in the order (gate desc, expert id asc)."""
+    shape = logits.shape
+    inds, scores = ops.route_topk(logits.reshape(-1, shape[-1]), top_k, norm_topk_prob)
+    return inds.reshape(*shape[:-1], top_k), scores.reshape(*shape[:-1], top_k)
+
+
+def _combine_shared(y, scores, shared_y, shared_gate):
+    """qwen3_x_moe.py:71-80.  y [..., k, H], scores [..., k] -> [..., H]."""
+    H = y.shape[-1]
+    k = scores.shape[-1]
+    lead = scores.shape[:-1]
+    T = int(np.prod(lead)) if len(lead) else 1
+    out = ops.combine(y.reshape(T * k, H), scores.reshape(T, k),
+                      None if shared_y is None else shared_y.reshape(T, H),
+                      None if shared_gate is None else shared_gate.reshape(T))
+    return out.reshape(*lead, H)
+
+
+def shared_expert_forward(arena: SlottedGLU, x2: torch.Tensor) -> torch.Tensor:
+    """Dense SwiGLU of the shared expert (mlx_lm Qwen3NextMLP) on every token."""
+    d = ops.token_dispatch(x2.shape[0], x2.device)
+    h = ops.glu_gate_up(arena, x2, d, pair_div=1)
+    return ops.glu_down(arena, h, d)
+
+
+# --------------------------------------------------------------------------- the wrapper
+
+
+class Qwen3_xMoEWrapper(SlotTable):
+    """Slotted MoE block wrapper (qwen3_x_moe.py:85-297) over libsg_b200."""
+
+    def __init__(self, inner: SparseMoeBlock, model_fingerprint: str | None, layer_path: str, block_idx: int,
+                 recorder=None, capture_gate_logits: bool = False, expert_loader=None, expert_cache=None,
+                 num_slots: int = 0, slot_size: int = 0, slot_policy: str = "reference",
+                 device: str | torch.device | None = None):
+        # base_moe_wrapper.py:84-87
+        if expert_loader is not None and any(v is None for v in (expert_cache, num_slots, slot_size)):
+            raise ValueError("expert_loader requires expert_cache, num_slots and slot_size")
+        device = torch.device(device) if device is not None else inner.gate.device
+        super().__init__(inner.num_experts, num_slots or 0, slot_policy=slot_policy, device=device)
+        self.inner = inner
+        self.model_fingerprint = model_fingerprint
+        self.layer_path = layer_path
+        self.block_idx = int(block_idx)
+        self.recorder = recorder
+        self._capture_gate_logits = capture_gate_logits
+        self.expert_loader = expert_loader
+        self.expert_cache = expert_cache
+        self.slot_size = slot_size or 0
+        self._quants = inner.quant
+        self._pending: list = []  # (event, pinned blobs) kept alive until their copies finish
+        self._weight_slots: SlottedGLU | None = None
+        if expert_loader is not None or expert_cache is not None:
+            H, I = inner.hidden_size, inner.moe_intermediate_size
+            self._weight_slots = SlottedGLU(self.num_slots, (I, H), (H, I), torch.bfloat16, quant=inner.quant,
+                                            device=device)
+        self._identity = None
+        if expert_cache is None:
+            if inner.switch_mlp is None:
+                raise ValueError("non-streaming wrapper needs inner.switch_mlp (all experts resident)")
+            self._identity = torch.arange(inner.num_experts, dtype=torch.int32, device=device)
+
+    # ------------------------------------------------------------------ properties
+    @property
+    def is_quantized(self) -> bool:
+        return self._quants is not None
+
+    @property
+    def should_capture_traces(self) -> bool:
+        return self.recorder is not None
+
+    @property
+    def should_stream_experts(self) -> bool:
+        return self.expert_loader is not None
+
+    @property
+    def arena(self) -> SlottedGLU:
+        return self._weight_slots if self._weight_slots is not None else self.inner.switch_mlp
+
+    # ------------------------------------------------------------------ admission
+    def _release_finished(self) -> None:
+        self._pending = [(ev, keep) for ev, keep in self._pending if not ev.query()]
+
+    def _maybe_admit(self, routed_eids: torch.Tensor):
+        """qwen3_x_moe.py:136-208.  Returns (unique eids on host, inverse_map
+        on device, the step's Dispatch with resolved slot ids)."""
+        assert self.expert_loader is not None and self._weight_slots is not None
+        self._release_finished()
+        d = ops.dispatch(routed_eids, self.num_experts, self.eid2sid_device)
+        counts = d.counts.cpu()  # the one host read of a hit-only step
+        n_unique, n_missed = int(counts[0]), int(counts[1])
+        if n_unique > self.num_slots:
+            raise RuntimeError(
+                f"MoE block {self.block_idx}: total slots available ({self.num_slots}) "
+                f" < unique experts routed across the batch ({n_unique}). Either "
+                f"decrease batch size or initialize {self.__class__.__name__!r} with more slots."
+            )
+        unique = d.unique[:n_unique].cpu().numpy()
+        if n_missed == 0:
+            return unique, d.inverse, d
+        missed = unique[self._eid_lookup_table[unique] < 0]
+        glob_eids = self.block_idx * self.num_experts + missed
+        acquired = self._choose_slots(missed.size, protected=unique)
+        old = self._sid_lookup_table[acquired]
+        evicted = old[old >= 0]
+        self._eid_lookup_table[evicted] = EMPTY
+        self._sid_lookup_table[acquired] = EMPTY
+        blobs = self.expert_loader.load_sync(glob_eids.tolist())
+        stream = torch.cuda.current_stream(self._device)
+        for eid, sid, payload in zip(missed, acquired, blobs):
+            self._weight_slots.refill_from_blob(int(sid), payload.as_tensor(), stream)
+            self._eid_lookup_table[eid] = sid
+            self._sid_lookup_table[sid] = eid
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._pending.append((ev, blobs))
+        self.sync_device()
+        d.slot_ids[:n_unique] = self.eid2sid_device[d.unique[:n_unique].long()]
+        return unique, d.inverse, d
+
+    # ------------------------------------------------------------------ forward
+    def _gather_forward_dispatched(self, x2: torch.Tensor, d: ops.Dispatch, arena: SlottedGLU) -> torch.Tensor:
+        h = ops.glu_gate_up(arena, x2, d, pair_div=self.inner.top_k)
+        return ops.glu_down(arena, h, d)
+
+    def _gather_forward(self, x, gate_proj, up_proj, down_proj, slot_idxs, inverse_map):
+        """qwen3_x_moe.py:210-248: pair p = t*k + j runs expert slot
+        ``slot_idxs[inverse_map[p]]``.  The projections must be this block's
+        arena tensors (they are read in place).  Returns [B, S, k, H]."""
+        arena = self.arena
+        if gate_proj is not arena.gate_proj or up_proj is not arena.up_proj or down_proj is not arena.down_proj:
+            raise ValueError("_gather_forward reads this block's arena in place; pass its gate/up/down tensors")
+        B, S, H = x.shape
+        k = self.inner.top_k
+        slot_idxs = torch.as_tensor(slot_idxs, dtype=torch.int32, device=x.device)
+        inv = torch.as_tensor(inverse_map, dtype=torch.int32, device=x.device).reshape(-1)
+        d = ops.dispatch(inv, int(slot_idxs.numel()), slot_idxs)
+        y = self._gather_forward_dispatched(x.reshape(B * S, H), d, arena)
+        return y.reshape(B, S, k, H)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """qwen3_x_moe.py:250-297.  x [B, S, H] bf16 -> [B, S, H] bf16."""
+        if self.inner.sharding_group is not None:
+            raise NotImplementedError("tensor-parallel sharding groups are not supported; use ep.ExpertParallelMoE")
+        B, S, H = x.shape
+        x2 = x.reshape(B * S, H).contiguous()
+        logits = ops.router_linear(x2, self.inner.gate)
+        inds, scores = _get_routings(logits, self.inner.top_k, self.inner.norm_topk_prob)
+        shared_y = shared_gate = None
+        if self.inner.shared_expert is not None:
+            shared_y = shared_expert_forward(self.inner.shared_expert, x2)
+            shared_gate = ops.router_linear(x2, self.inner.shared_expert_gate)
+        if self.should_capture_traces:
+            self.recorder.capture(layer_path=self.layer_path, layer_class="Qwen3NextSparseMoeBlock",
+                                  block_idx=self.block_idx, expert_ids=inds, softmax_weights=scores,
+                                  gate_logits=logits if self._capture_gate_logits else None)
+        if self.expert_cache is None:
+            d = ops.dispatch(inds, self.num_experts, self._identity)
+            y = self._gather_forward_dispatched(x2, d, self.inner.switch_mlp)
+        else:
+            unique, _inverse, d = self._maybe_admit(inds)
+            slot_ids = self._eid_lookup_table[unique]
+            y = self._gather_forward_dispatched(x2, d, self._weight_slots)
+            self._touch(slot_ids)
+        out = _combine_shared(y.reshape(B * S, self.inner.top_k, H), scores, shared_y, shared_gate)
+        return out.reshape(B, S, H)
+
+    def forward_resident(self, x2: torch.Tensor, timing: dict | None = None) -> torch.Tensor:
+        """The non-streaming step on [T, H] with no host synchronisation at all
+        (capturable in a CUDA graph): every expert is resident.  ``timing``
+        (optional) receives CUDA events around the routed gate/up and down
+        kernels plus the step's Dispatch, for per-kernel timing."""
+        if self._identity is None:
+            raise RuntimeError("forward_resident needs the non-streaming (all-resident) wrapper")
+        logits = ops.router_linear(x2, self.inner.gate)
+        inds, scores = ops.route_topk(logits, self.inner.top_k, self.inner.norm_topk_prob)
+        shared_y = shared_gate = None
+        if self.inner.shared_expert is not None:
+            shared_y = shared_expert_forward(self.inner.shared_expert, x2)
+            shared_gate = ops.router_linear(x2, self.inner.shared_expert_gate)
+        d = ops.dispatch(inds, self.num_experts, self._identity)
+        arena = self.inner.switch_mlp
+        if timing is None:
+            y = self._gather_forward_dispatched(x2, d, arena)
+        else:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            h = ops.glu_gate_up(arena, x2, d, pair_div=self.inner.top_k)
+            ev[1].record()
+            y = ops.glu_down(arena, h, d)
+            ev[2].record()
+            timing.setdefault("events", []).append(ev)
+            timing.setdefault("dispatch", []).append(d)
+        return ops.combine(y, scores, shared_y, None if shared_gate is None else shared_gate.reshape(-1))
+
+    # ------------------------------------------------------------------ factory
+    @staticmethod
+    def make_wrapper_factory(*, model_fingerprint: str | None = None, recorder=None, capture_gate_logits: bool = False,
+                             expert_loader=None, expert_cache=None, num_slots: int = 0, slot_size: int = 0,
+                             slot_policy: str = "reference") -> Callable:
+        """qwen3_x_moe.py:299-337.  ``candidate`` needs ``layer_path`` and
+        ``block_idx`` attributes (LayerCandidate)."""
+
+        def factory(module: SparseMoeBlock, candidate) -> Qwen3_xMoEWrapper:
+            if getattr(candidate, "block_idx", None) is None:
+                raise ValueError(
+                    f"Cannot instrument layer {getattr(candidate, 'layer_path', '?')!r} because the index of its "
+                    "parent transformer block could not be determined."
+                )
+            return Qwen3_xMoEWrapper(module, model_fingerprint, candidate.layer_path, candidate.block_idx,
+                                     recorder, capture_gate_logits, expert_loader, expert_cache, num_slots,
+                                     slot_size, slot_policy=slot_policy)
+
+        return factory
+
+
+SlottedMoE = Qwen3_xMoEWrapper

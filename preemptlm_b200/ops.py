@@ -1,0 +1,164 @@
+"""Torch-facing wrappers of the C-ABI kernels (one function per entry point).
+
+All tensors must be CUDA tensors on the current device; results are
+allocated with torch and written by the kernels on the current stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _abi
+
+# number of kernel launches issued through this module (read by the benchmark)
+LAUNCHES = [0]
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _bf16_2d(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.bfloat16 or not t.is_cuda or t.dim() != 2:
+        raise TypeError(f"{name} must be a 2-D bf16 CUDA tensor")
+    return t.contiguous()
+
+
+def router_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """bf16(x @ w^T), fp32 accumulation in the fixed router order
+    (``sg_router_logits``; qwen3_x_moe.py:254, :259)."""
+    x = _bf16_2d(x, "x")
+    w = _bf16_2d(w, "w")
+    T, H = x.shape
+    E = w.shape[0]
+    out = torch.empty((T, E), dtype=torch.bfloat16, device=x.device)
+    LAUNCHES[0] += T > 0
+    _abi.call("sg_router_logits", x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, E, _stream())
+    return out
+
+
+def route_topk(logits: torch.Tensor, top_k: int, norm_topk_prob: bool):
+    """``_get_routings`` (qwen3_x_moe.py:26-40): (inds int32 [T, k], scores bf16 [T, k])."""
+    logits = _bf16_2d(logits, "logits")
+    T, E = logits.shape
+    inds = torch.empty((T, top_k), dtype=torch.int32, device=logits.device)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=logits.device)
+    LAUNCHES[0] += T > 0
+    _abi.call("sg_route_topk", logits.data_ptr(), T, E, int(top_k), int(bool(norm_topk_prob)), inds.data_ptr(),
+              scores.data_ptr(), _stream())
+    return inds, scores
+
+
+@dataclass
+class Dispatch:
+    """Device-side unique/inverse/slot/permutation of one step (sg_dispatch)."""
+
+    unique: torch.Tensor     # [max_unique] int32, first counts[0] valid (ascending)
+    inverse: torch.Tensor    # [P] int32
+    counts: torch.Tensor     # [2] int32: (U, #missed)
+    slot_ids: torch.Tensor   # [max_unique] int32
+    miss_eids: torch.Tensor  # [max_unique] int32
+    group_off: torch.Tensor  # [max_unique] int32 (U + 1 valid)
+    perm: torch.Tensor       # [P] int32
+    grid_groups: int         # host upper bound on U
+
+
+def dispatch(ids: torch.Tensor, num_ids: int, eid2sid: torch.Tensor) -> Dispatch:
+    ids = ids.reshape(-1)
+    if ids.dtype != torch.int32 or not ids.is_cuda:
+        raise TypeError("ids must be int32 CUDA")
+    if eid2sid.dtype != torch.int32 or eid2sid.numel() < num_ids:
+        raise TypeError("eid2sid must be int32 with num_ids entries")
+    P = ids.numel()
+    mu = min(P, num_ids) + 1
+    dev = ids.device
+    d = Dispatch(
+        unique=torch.empty(mu, dtype=torch.int32, device=dev),
+        inverse=torch.empty(P, dtype=torch.int32, device=dev),
+        counts=torch.empty(2, dtype=torch.int32, device=dev),
+        slot_ids=torch.empty(mu, dtype=torch.int32, device=dev),
+        miss_eids=torch.empty(mu, dtype=torch.int32, device=dev),
+        group_off=torch.empty(mu, dtype=torch.int32, device=dev),
+        perm=torch.empty(P, dtype=torch.int32, device=dev),
+        grid_groups=mu - 1,
+    )
+    LAUNCHES[0] += 1
+    _abi.call("sg_dispatch", ids.contiguous().data_ptr(), P, int(num_ids), eid2sid.data_ptr(), d.unique.data_ptr(),
+              d.inverse.data_ptr(), d.counts.data_ptr(), d.slot_ids.data_ptr(), d.miss_eids.data_ptr(),
+              d.group_off.data_ptr(), d.perm.data_ptr(), mu, _stream())
+    return d
+
+
+_TOKEN_DISPATCH: dict = {}
+
+
+def token_dispatch(T: int, device) -> Dispatch:
+    """A single group holding every token (the shared expert): pairs are
+    tokens, slot 0.  Cached per (device, T): building it copies from the host."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    key = (str(dev), int(T))
+    if key not in _TOKEN_DISPATCH:
+        _TOKEN_DISPATCH[key] = _make_token_dispatch(T, dev)
+    return _TOKEN_DISPATCH[key]
+
+
+def _make_token_dispatch(T: int, dev) -> Dispatch:
+    return Dispatch(
+        unique=torch.zeros(2, dtype=torch.int32, device=dev),
+        inverse=torch.zeros(T, dtype=torch.int32, device=dev),
+        counts=torch.tensor([1, 0], dtype=torch.int32, device=dev),
+        slot_ids=torch.zeros(2, dtype=torch.int32, device=dev),
+        miss_eids=torch.zeros(2, dtype=torch.int32, device=dev),
+        group_off=torch.tensor([0, T], dtype=torch.int32, device=dev),
+        perm=torch.arange(T, dtype=torch.int32, device=dev),
+        grid_groups=1,
+    )
+
+
+def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
+    """h[p] = swiglu over the arena (``sg_glu_gate_up``)."""
+    x = _bf16_2d(x, "x")
+    P = d.perm.numel()
+    h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
+    if P == 0:
+        return h
+    LAUNCHES[0] += 1
+    lib = _abi.load()
+    _abi.check(lib.sg_glu_gate_up(ctypes.byref(arena.desc()), x.data_ptr(), int(pair_div), d.counts.data_ptr(),
+                                  d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
+                                  h.data_ptr(), _stream()), "sg_glu_gate_up")
+    return h
+
+
+def glu_down(arena, h: torch.Tensor, d: Dispatch) -> torch.Tensor:
+    """y[p] = h[p] @ down^T over the arena (``sg_glu_down``)."""
+    h = _bf16_2d(h, "h")
+    P = d.perm.numel()
+    y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=h.device)
+    if P == 0:
+        return y
+    LAUNCHES[0] += 1
+    lib = _abi.load()
+    _abi.check(lib.sg_glu_down(ctypes.byref(arena.desc()), h.data_ptr(), d.counts.data_ptr(), d.slot_ids.data_ptr(),
+                               d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),
+               "sg_glu_down")
+    return y
+
+
+def combine(y: torch.Tensor, scores: torch.Tensor, shared_y: torch.Tensor | None,
+            shared_gate: torch.Tensor | None) -> torch.Tensor:
+    """``_combine_shared`` (qwen3_x_moe.py:71-80) -> out [T, H] bf16."""
+    T, k = scores.shape
+    H = y.shape[-1]
+    y = y.reshape(T * k, H).contiguous()
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=y.device)
+    sy = shared_y.contiguous().data_ptr() if shared_y is not None else None
+    sg = shared_gate.contiguous().data_ptr() if shared_gate is not None else None
+    LAUNCHES[0] += T > 0
+    _abi.call("sg_combine", y.data_ptr(), scores.contiguous().data_ptr(), T, k, H, sy, sg, out.data_ptr(), _stream())
+    return out

@@ -1,0 +1,81 @@
+"""CPU: the C-ABI library builds, loads and exports every symbol the header
+declares (no kernel is launched here)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from preemptlm_b200 import _abi
+from preemptlm_b200.build import LIB_PATH, build_library
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "sg_abi.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sg_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_library()
+    assert LIB_PATH.exists()
+    return _abi.load()
+
+
+def test_header_declares_expected_symbols():
+    assert set(header_symbols()) == set(_abi.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_header_symbol(lib):
+    for name in header_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_status_strings_and_version(lib):
+    assert lib.sg_version() >= 1
+    assert lib.sg_built_arch() == 1000
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.sg_status_string(code).decode()
+    assert "unknown" in lib.sg_status_string(-99).decode()
+
+
+def test_host_side_argument_checks(lib):
+    # shape / format checks run before any CUDA call
+    a = _abi.sg_arena(num_slots=4, hidden=2048, inter=512, bits=8, group_size=64)
+    n = 3 * 2048 * 512
+    assert lib.sg_expert_bytes(ctypes.byref(a)) == n + n // 64 * 4
+    a.bits = 16
+    assert lib.sg_expert_bytes(ctypes.byref(a)) == 2 * n
+    a.bits = 4
+    assert lib.sg_expert_bytes(ctypes.byref(a)) == n // 2 + n // 64 * 4
+    a.bits = 3
+    assert lib.sg_expert_bytes(ctypes.byref(a)) == 0
+    assert lib.sg_router_logits(None, None, None, 1, 2048, 8, None) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_router_logits(1, 1, 1, 1, 100 + 256, 8, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_route_topk(1, 1, 33, 2, 1, 1, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_route_topk(1, 1, 64, 33, 1, 1, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_dispatch(1, 8, 9000, 1, 1, 1, 1, 1, 1, 1, 1, 100, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_dispatch(1, 8, 64, 1, 1, 1, 1, 1, 1, 1, 1, 4, None) == _abi.SG_ERR_CAPACITY
+    a = _abi.sg_arena(num_slots=4, hidden=2048, inter=512, bits=5, group_size=64, gate_w=1, up_w=1, down_w=1)
+    assert lib.sg_glu_gate_up(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_FORMAT
+    a.bits = 8
+    a.group_size = 32
+    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_FORMAT
+    a.bits, a.group_size, a.hidden = 16, 64, 100
+    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_combine(1, 1, 1, 2, 12, None, None, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_combine(1, 1, 1, 2, 16, 1, None, 1, None) == _abi.SG_ERR_INVALID_ARG
+    a = _abi.sg_arena(num_slots=4, hidden=256, inter=128, bits=16, group_size=64, gate_w=1, up_w=1, down_w=1)
+    assert lib.sg_refill_h2d(1, 10, ctypes.byref(a), 0, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_refill_h2d(1, 3 * 256 * 128 * 2, ctypes.byref(a), 4, None) == _abi.SG_ERR_SHAPE
+
+
+def test_ops_fail_loudly_without_library(monkeypatch, tmp_path):
+    monkeypatch.setattr(_abi, "_lib", None)
+    monkeypatch.setenv("SG_B200_LIB", str(tmp_path / "missing.so"))
+    with pytest.raises(ImportError):
+        _abi.load()

@@ -1,0 +1,221 @@
+"""GPU parity: every kernel through the C-ABI against the CPU oracle.
+
+Routing (logits, top-k ids, scores, unique/inverse, slot ids) is bit-exact;
+GLU / layer outputs meet max-abs 2e-2 and rel-L2 1e-2 (bf16 tolerance).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import slotted_glu_oracle as orc
+from preemptlm_b200 import ops
+from preemptlm_b200.synthetic import CONFIGS, LayerConfig, make_layer, make_tokens
+from preemptlm_b200.layer import Qwen3_xMoEWrapper
+
+from ._util import LazyExperts, assert_close, bits16, f32
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _bf16(shape, seed, std=1.0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=DEV) * std).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- router / routing
+
+@pytest.mark.parametrize("T,H,E", [(1, 2048, 512), (7, 256, 128), (33, 4096, 64), (9, 2048, 1), (256, 2048, 512)])
+def test_router_logits_bitexact(T, H, E):
+    x = _bf16((T, H), 1)
+    w = _bf16((E, H), 2, 0.02)
+    dev = bits16(ops.router_linear(x, w))
+    ref = orc.router_logits(bits16(x), bits16(w))
+    assert np.array_equal(dev, ref)
+
+
+@pytest.mark.parametrize("E,k,norm", [(32, 1, True), (128, 8, True), (512, 10, True), (512, 10, False),
+                                      (1024, 32, True), (96, 5, True)])
+def test_route_topk_bitexact(E, k, norm):
+    T = 300
+    logits = _bf16((T, E), 3, 1.0)
+    inds, scores = ops.route_topk(logits, k, norm)
+    ri, rs, _ = orc.get_routings(bits16(logits), k, norm)
+    assert np.array_equal(inds.cpu().numpy(), ri)
+    assert np.array_equal(bits16(scores), rs)
+
+
+def test_route_topk_ties_bitexact():
+    """Logits on a coarse grid: many exact bf16 ties at the k-th gate."""
+    T, E, k = 512, 512, 10
+    g = torch.Generator(device=DEV).manual_seed(4)
+    logits = torch.randint(-3, 4, (T, E), generator=g, device=DEV).float().mul(0.5).to(torch.bfloat16)
+    inds, scores = ops.route_topk(logits, k, True)
+    ri, rs, gates = orc.get_routings(bits16(logits), k, True)
+    assert np.array_equal(inds.cpu().numpy(), ri)
+    assert np.array_equal(bits16(scores), rs)
+    kth = np.sort(gates, axis=1)[:, -k]
+    ties = ((gates == kth[:, None]).sum(1) > 1).sum()
+    assert ties > T // 2  # the case is really tie-heavy
+
+
+def test_routing_from_router_bitexact_cfg3_full_size():
+    cfg = CONFIGS["cfg3"]
+    T = 256
+    x = make_tokens(cfg, T)
+    w = _bf16((cfg.num_experts, cfg.hidden), 5, 0.02)
+    logits = ops.router_linear(x, w)
+    inds, scores = ops.route_topk(logits, cfg.top_k, True)
+    rl = orc.router_logits(bits16(x), bits16(w))
+    ri, rs, _ = orc.get_routings(rl, cfg.top_k, True)
+    assert np.array_equal(bits16(logits), rl)
+    assert np.array_equal(inds.cpu().numpy(), ri)
+    assert np.array_equal(bits16(scores), rs)
+
+
+# ----------------------------------------------------------------------------- dispatch
+
+@pytest.mark.parametrize("P,E,resident", [(1, 128, 1.0), (80, 128, 0.5), (2560, 512, 0.25), (65536, 128, 0.9),
+                                          (40, 8192, 0.5)])
+def test_dispatch_matches_numpy(P, E, resident):
+    g = np.random.default_rng(P + E)
+    ids = g.integers(0, E, size=P).astype(np.int32)
+    eid2sid = np.where(g.random(E) < resident, g.permutation(E), -1).astype(np.int32)
+    d = ops.dispatch(torch.from_numpy(ids).to(DEV), E, torch.from_numpy(eid2sid).to(DEV))
+    U, nmiss = d.counts.cpu().tolist()
+    uq, inv = np.unique(ids, return_inverse=True)
+    assert U == uq.size
+    assert np.array_equal(d.unique[:U].cpu().numpy(), uq)
+    assert np.array_equal(d.inverse.cpu().numpy(), inv)
+    assert np.array_equal(d.slot_ids[:U].cpu().numpy(), eid2sid[uq])
+    miss = uq[eid2sid[uq] < 0]
+    assert nmiss == miss.size and np.array_equal(d.miss_eids[:nmiss].cpu().numpy(), miss)
+    off = d.group_off[: U + 1].cpu().numpy()
+    perm = d.perm.cpu().numpy()
+    assert off[0] == 0 and off[-1] == P
+    assert np.array_equal(np.sort(perm), np.arange(P))
+    for u in range(U):
+        grp = perm[off[u]: off[u + 1]]
+        assert np.all(inv[grp] == u)
+
+
+# ----------------------------------------------------------------------------- gathered GLU
+
+@pytest.mark.parametrize("bits", [16, 8, 4])
+@pytest.mark.parametrize("H,I,E,T,k", [(256, 128, 8, 5, 2), (2048, 768, 16, 33, 4), (1024, 512, 6, 1, 6)])
+def test_glu_matches_oracle(bits, H, I, E, T, k):
+    cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
+    block, tens = make_layer(cfg, device=DEV)
+    x = _bf16((T, H), 11)
+    g = np.random.default_rng(T * 7 + E)
+    inds = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    d = ops.dispatch(torch.from_numpy(inds).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    h = ops.glu_gate_up(block.switch_mlp, x, d, pair_div=k)
+    y = ops.glu_down(block.switch_mlp, h, d)
+    ex = LazyExperts(tens["experts"], bits)
+    xf = f32(x)
+    href = np.zeros((T * k, I), np.float32)
+    yref = np.zeros((T * k, H), np.float32)
+    for p in range(T * k):
+        ew = ex[inds.reshape(-1)[p]]
+        xr = xf[p // k: p // k + 1]
+        up = orc._mm_bf16(xr, ew.up)
+        gate = orc._mm_bf16(xr, ew.gate)
+        href[p] = orc.swiglu(up, gate)[0]
+        yref[p] = orc._mm_bf16(href[p: p + 1], ew.down)[0]
+    assert_close(f32(h), href, what="h")
+    assert_close(f32(y), yref, what="y")
+    # the device's own h through the oracle's down projection: isolates down
+    hdev = f32(h)
+    ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
+    assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what="y|h")
+
+
+def test_glu_skips_missing_slots():
+    cfg = LayerConfig("t", 9, 256, 4, 1, 128, None, 8, 4)
+    block, _ = make_layer(cfg, device=DEV)
+    x = _bf16((3, 256), 12)
+    inds = torch.tensor([[0], [1], [2]], dtype=torch.int32, device=DEV)
+    eid2sid = torch.tensor([0, -1, 2, 3], dtype=torch.int32, device=DEV)
+    d = ops.dispatch(inds, 4, eid2sid)
+    assert d.counts.cpu().tolist() == [3, 1]
+    h = ops.glu_gate_up(block.switch_mlp, x, d, pair_div=1)
+    assert torch.all(h[1] == 0) and torch.any(h[0] != 0)
+
+
+# ----------------------------------------------------------------------------- combine
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_combine_matches_oracle(shared):
+    T, k, H = 37, 10, 2048
+    y = _bf16((T * k, H), 20, 0.1)
+    sc = torch.rand((T, k), device=DEV).to(torch.bfloat16)
+    sy = _bf16((T, H), 21, 0.1) if shared else None
+    sg = _bf16((T,), 22) if shared else None
+    out = ops.combine(y, sc, sy, sg)
+    ref = orc.combine_shared(f32(y).reshape(T, k, H), f32(sc), None if sy is None else f32(sy),
+                             None if sg is None else f32(sg))
+    assert_close(f32(out), ref, max_abs=1e-6, rel=1e-6, what="combine") if not shared else \
+        assert_close(f32(out), ref, max_abs=4e-3, rel=2e-3, what="combine")
+
+
+# ----------------------------------------------------------------------------- whole layer
+
+@pytest.mark.parametrize("cfg_name,T", [("cfg1", 1), ("cfg1", 4), ("cfg2", 16), ("cfg3", 1), ("cfg3", 8),
+                                        ("cfg4", 2)])
+def test_layer_matches_oracle(cfg_name, T):
+    cfg = CONFIGS[cfg_name]
+    block, tens = make_layer(cfg, device=DEV)
+    moe = Qwen3_xMoEWrapper(block, "fp", "model.layers.0.mlp", 0)
+    x = make_tokens(cfg, T)
+    out = moe(x.reshape(1, T, cfg.hidden)).reshape(T, cfg.hidden)
+    shared = None
+    if tens["shared"] is not None:
+        shared = LazyExperts(tens["shared"], cfg.bits)[0]
+    ref = orc.layer_forward(bits16(x), bits16(tens["router"]), cfg.top_k, cfg.norm_topk_prob,
+                            LazyExperts(tens["experts"], cfg.bits), shared,
+                            None if tens["shared_gate"] is None else bits16(tens["shared_gate"]))
+    assert_close(f32(out), ref["out"], what=f"{cfg_name} T={T}")
+    res = moe.forward_resident(x)
+    assert torch.equal(res, out)
+
+
+def test_layer_full_size_sampled_tokens_cfg3():
+    """cfg3 at its largest decode batch (T=256): routing bit-exact for every
+    token, outputs checked on a sample of tokens."""
+    cfg = CONFIGS["cfg3"]
+    T = 256
+    block, tens = make_layer(cfg, device=DEV)
+    moe = Qwen3_xMoEWrapper(block, "fp", "l", 0)
+    x = make_tokens(cfg, T)
+    out = f32(moe.forward_resident(x))
+    logits = orc.router_logits(bits16(x), bits16(tens["router"]))
+    inds, sc, _ = orc.get_routings(logits, cfg.top_k, True)
+    dl = ops.router_linear(x, block.gate)
+    di, ds = ops.route_topk(dl, cfg.top_k, True)
+    assert np.array_equal(di.cpu().numpy(), inds) and np.array_equal(bits16(ds), sc)
+    sample = np.random.default_rng(0).choice(T, 6, replace=False)
+    ex = LazyExperts(tens["experts"], cfg.bits)
+    sh = LazyExperts(tens["shared"], cfg.bits)[0]
+    sg = orc.bf16_bits_to_f32(orc.router_logits(bits16(x[sample]), bits16(tens["shared_gate"])))
+    xs = f32(x)[sample]
+    y = np.stack([np.stack([orc.expert_forward(xs[i: i + 1], ex[inds[t, j]])[0] for j in range(cfg.top_k)])
+                  for i, t in enumerate(sample)])
+    ref = orc.combine_shared(y, orc.bf16_bits_to_f32(sc[sample]), orc.expert_forward(xs, sh), sg)
+    assert_close(out[sample], ref, what="cfg3 T=256 sampled")
+
+
+def test_layer_ragged_and_empty():
+    cfg = LayerConfig("t", 9, 256, 32, 3, 128, 128, 8, 32)
+    block, tens = make_layer(cfg, device=DEV)
+    moe = Qwen3_xMoEWrapper(block, "fp", "l", 0)
+    x = torch.zeros((0, 256), dtype=torch.bfloat16, device=DEV)
+    assert moe.forward_resident(x).shape == (0, 256)
+    for T in (1, 3, 17):
+        x = make_tokens(cfg, T)
+        out = moe(x.reshape(1, T, 256)).reshape(T, 256)
+        ref = orc.layer_forward(bits16(x), bits16(tens["router"]), cfg.top_k, True,
+                                LazyExperts(tens["experts"], 8), LazyExperts(tens["shared"], 8)[0],
+                                bits16(tens["shared_gate"]))
+        assert_close(f32(out), ref["out"], what=f"T={T}")
