@@ -226,9 +226,36 @@ def time_cpu_port(cfg, sample_tokens, steps, host_layer, warmup=0):
 # --------------------------------------------------------------------------- our arm
 
 
+def _kernel_roofline(cfg, timing, rows_per_step, T_local):
+    """Algorithmic bytes / CUDA-event time of the routed gate/up (and down)
+    launches recorded in ``timing``."""
+    import statistics as st
+
+    H, I, k = cfg.hidden, cfg.inter, cfg.top_k
+    if cfg.bits == 16:
+        per_gu, per_dn = 2 * I * H * 2, H * I * 2
+    else:
+        per_gu = 2 * (I * H * cfg.bits // 8 + (I * H // 64) * 4)
+        per_dn = H * I * cfg.bits // 8 + (H * I // 64) * 4
+    gu_ms, dn_ms, gu_b, dn_b, us = [], [], 0, 0, []
+    for i, (ev, d) in enumerate(zip(timing["events"], timing["dispatch"])):
+        U = int(d.counts[0].item())
+        P = rows_per_step[i] if rows_per_step else T_local * k
+        n_in = T_local if not rows_per_step else P  # distinct input rows read
+        us.append(U)
+        gu_ms.append(ev[0].elapsed_time(ev[1]))
+        dn_ms.append(ev[1].elapsed_time(ev[2]))
+        gu_b += U * per_gu + n_in * H * 2 + P * I * 2
+        dn_b += U * per_dn + P * I * 2 + P * H * 2
+    return {"gu_ms": gu_ms, "dn_ms": dn_ms, "gu_bytes": gu_b, "dn_bytes": dn_b, "unique": us,
+            "gu_gbs": gu_b / (sum(gu_ms) * 1e-3) / 1e9, "dn_gbs": dn_b / (sum(dn_ms) * 1e-3) / 1e9,
+            "mean_unique": st.mean(us)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
+    from datetime import timedelta
 
     from preemptlm_b200 import ops
     from preemptlm_b200.layer import Qwen3_xMoEWrapper
@@ -237,17 +264,36 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = CONFIGS[args.workload]
-    if world > 1:
-        raise SystemExit("multi-GPU expert-parallel bench runs through preemptlm_b200.ep (see run_ep)")
     T = args.tokens
-    block, tens = make_layer(cfg, device=dev)
-    moe = Qwen3_xMoEWrapper(block, "synthetic", "model.layers.0.mlp", 0)
+    H = cfg.hidden
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        from preemptlm_b200.ep import ExpertParallelMoE, shard_layer
+
+        backend, _ = shard_layer(cfg, rank, world, dev)
+        ep = ExpertParallelMoE(backend, cfg.num_experts, H, cfg.top_k)
+        step = ep.forward
+        tens = None
+    else:
+        block, tens = make_layer(cfg, device=dev)
+        moe = Qwen3_xMoEWrapper(block, "synthetic", "model.layers.0.mlp", 0)
+        backend = None
     n_in = args.warmup + args.steps
-    xs = [make_tokens(cfg, T, device=dev, step=i) for i in range(n_in)]
+    xs = [make_tokens(cfg, T, device=dev, step=i + 1000 * rank) for i in range(n_in)]
     torch.cuda.synchronize()
 
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def run_step(x, timing=None):
+        if world > 1:
+            backend.timing = timing
+            return step(x)
+        return moe.forward_resident(x, timing=timing)
+
     for i in range(args.warmup):
-        moe.forward_resident(xs[i])
+        run_step(xs[i])
     torch.cuda.synchronize()
 
     # ---------------------------------------------------------------- device-resident timing
@@ -257,34 +303,27 @@ def run_ours(args, rank, world, local_rank):
     timing: dict = {}
     launches0 = ops.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     torch.cuda.synchronize()
     start.record()
     for i in range(args.steps):
-        moe.forward_resident(xs[args.warmup + i], timing=timing)
+        run_step(xs[args.warmup + i], timing=timing)
     end.record()
     torch.cuda.synchronize()
+    barrier()
     clk = clocks.stop()
     launches = ops.LAUNCHES[0] - launches0
     ms_step = start.elapsed_time(end) / args.steps
+    if world > 1:
+        backend.timing = None
+        t = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
 
-    # routed gate/up kernel: algorithmic bytes / event duration
-    H, I, k = cfg.hidden, cfg.inter, cfg.top_k
-    per_expert_gu = 2 * (I * H * cfg.bits // 8 + (I * H // 64) * 4 if cfg.bits != 16 else I * H * 2)
-    gu_ms, dn_ms, gu_bytes, dn_bytes, us = [], [], 0, 0, []
-    per_expert_dn = (H * I * cfg.bits // 8 + (H * I // 64) * 4) if cfg.bits != 16 else H * I * 2
-    for ev, d in zip(timing["events"], timing["dispatch"]):
-        U = int(d.counts[0].item())
-        us.append(U)
-        gu_ms.append(ev[0].elapsed_time(ev[1]))
-        dn_ms.append(ev[1].elapsed_time(ev[2]))
-        gu_bytes += U * per_expert_gu + T * H * 2 + T * k * I * 2
-        dn_bytes += U * per_expert_dn + T * k * I * 2 + T * k * H * 2
+    rl = _kernel_roofline(cfg, timing, timing.get("rows"), T)
     peak, peak_kind = hbm_peak()
-    gu_gbs = gu_bytes / (sum(gu_ms) * 1e-3) / 1e9
-    dn_gbs = dn_bytes / (sum(dn_ms) * 1e-3) / 1e9
-    # whole-step algorithmic bytes (every byte once): experts + shared + router + x + out
-    step_bytes = (statistics.mean(us) * cfg.expert_bytes() + cfg.shared_bytes() + cfg.num_experts * H * 2
-                  + 2 * T * H * 2)
+    us_mean = rl["mean_unique"]
+    step_bytes = (us_mean * cfg.expert_bytes() + cfg.shared_bytes() + cfg.num_experts * H * 2 + 2 * T * H * 2)
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
 
     # ---------------------------------------------------------------- end to end (host buffers)
@@ -292,18 +331,28 @@ def run_ours(args, rank, world, local_rank):
     for i, xh in enumerate(x_host):
         xh.copy_(xs[i].cpu())
     out_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-    for i in range(args.warmup):
+
+    def e2e_step(i):
         xd = x_host[i % 2].to(dev, non_blocking=True)
-        out_host.copy_(moe(xd.view(1, T, H)).view(T, H), non_blocking=True)
+        out = step(xd) if world > 1 else moe(xd.view(1, T, H)).view(T, H)
+        out_host.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     e_start.record()
     for i in range(args.steps):
-        xd = x_host[i % 2].to(dev, non_blocking=True)
-        out_host.copy_(moe(xd.view(1, T, H)).view(T, H), non_blocking=True)
+        e2e_step(i)
     e_end.record()
     torch.cuda.synchronize()
+    barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
 
     # ---------------------------------------------------------------- CPU baseline (oracle port)
     cpu = None
@@ -315,6 +364,7 @@ def run_ours(args, rank, world, local_rank):
                "sample": f"{len(times)} steps of {sample} tokens through the CPU oracle of the same layer "
                          f"(routing, dequantise, fp32 matmul), experts over {threads} threads"}
 
+    shard = cfg.num_experts // world
     value = T * world / (ms_step * 1e-3)
     line = {
         "metric": METRIC,
@@ -332,20 +382,21 @@ def run_ours(args, rank, world, local_rank):
         "config": {
             "workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
                         f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, decode {T} tokens/GPU, "
-                        f"all experts of the shard resident ({cfg.num_experts} slots)",
-            "tokens_per_gpu": T, "hidden": H, "experts": cfg.num_experts, "top_k": k, "inter": I,
-            "shared_inter": cfg.shared_inter, "bits": cfg.bits, "slots": cfg.num_experts,
-            "unique_experts_per_step": round(statistics.mean(us), 1),
-            "l2": "no flush: >1.7 GB of expert weights per step vs 126 MB L2",
+                        f"expert-parallel over {world} GPU(s), all {shard} experts of each shard resident",
+            "tokens_per_gpu": T, "hidden": H, "experts": cfg.num_experts, "top_k": cfg.top_k, "inter": cfg.inter,
+            "shared_inter": cfg.shared_inter, "bits": cfg.bits, "slots_per_gpu": shard,
+            "unique_experts_per_step_per_gpu": round(us_mean, 1),
+            "l2": "no flush: each step streams >126 MB (L2) of expert weights per GPU",
             "parallelism": f"ep{world}",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "sg_glu_gate_up (routed, q8 GEMV)", "achieved": round(gu_gbs, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(gu_gbs / peak, 4), "peak_kind": peak_kind,
+            "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
+            "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4), "peak_kind": peak_kind,
             "traffic": None,
-            "bytes_per_launch": round(gu_bytes / len(gu_ms)), "ms_per_launch": round(statistics.mean(gu_ms), 5),
-            "down": {"achieved": round(dn_gbs, 1), "frac": round(dn_gbs / peak, 4),
-                     "ms_per_launch": round(statistics.mean(dn_ms), 5)},
+            "bytes_per_launch": round(rl["gu_bytes"] / len(rl["gu_ms"])),
+            "ms_per_launch": round(statistics.mean(rl["gu_ms"]), 5),
+            "down": {"achieved": round(rl["dn_gbs"], 1), "frac": round(rl["dn_gbs"] / peak, 4),
+                     "ms_per_launch": round(statistics.mean(rl["dn_ms"]), 5)},
             "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
         },
         "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
@@ -356,6 +407,9 @@ def run_ours(args, rank, world, local_rank):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -390,7 +444,9 @@ def run_reference(args, rank, world):
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
-    world = int(os.environ.get("WORLD_SIZE", args.gpus if args.gpus == 1 else 1))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if args.gpus > 1 and world == 1:
+        raise SystemExit("--gpus N > 1 runs under torch.distributed.run (one process per GPU)")
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -249,7 +249,7 @@ int check_arena(const sg_arena* A) {
   if (!A || !A->gate_w || !A->up_w || !A->down_w) return SG_ERR_INVALID_ARG;
   if (A->num_slots < 1 || A->hidden < 64 || A->inter < 64) return SG_ERR_SHAPE;
   if (A->hidden % 64 || A->inter % 64) return SG_ERR_SHAPE;
-  if ((size_t)A->hidden * 2 * GW_NT > 160 * 1024) return SG_ERR_SHAPE;
+  if ((size_t)A->hidden * 2 * GW_NT > 160 * 1024 || (size_t)A->inter * 2 * GW_NT > 160 * 1024) return SG_ERR_SHAPE;
   if (A->bits == 16) return SG_OK;
   if (A->bits != 4 && A->bits != 8) return SG_ERR_FORMAT;
   if (A->group_size != 64) return SG_ERR_FORMAT;

@@ -1,0 +1,172 @@
+"""Expert parallelism for the slotted MoE layer: one process per GPU, the
+experts of every layer split evenly across ranks, token dispatch and combine
+by NCCL all-to-all over NVLink.
+
+Rank r of R owns experts [r*E/R, (r+1)*E/R) in its arena (slot = expert id -
+r*E/R); the router and the shared expert are replicated; every rank routes its
+own tokens.  Per layer:
+
+  1. route the local tokens (router GEMV + softmax/top-k);
+  2. order the T*k (token, expert) pairs by owning rank; exchange the per-rank
+     pair counts (all-to-all of R ints, the one host read of the step);
+  3. all-to-all the pairs' hidden rows and their local expert ids;
+  4. run the gathered SwiGLU on the received rows against the local arena;
+  5. all-to-all the expert outputs back, restore pair order, combine with the
+     routing scores and the local shared expert.
+
+The math of steps 1, 4, 5 goes through a ``backend`` object so that the same
+exchange logic runs with the CUDA kernels (``CudaBackend``) on GPUs and with a
+CPU implementation in the multi-process CPU tests.  The exchange itself uses
+``torch.distributed.all_to_all_single`` (NCCL on GPUs, gloo on CPU).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .arena import SlottedGLU
+
+
+@dataclass
+class ExpertShard:
+    """This rank's slice of a layer: experts [first, first + count)."""
+
+    rank: int
+    world: int
+    num_experts: int
+
+    @property
+    def count(self) -> int:
+        return self.num_experts // self.world
+
+    @property
+    def first(self) -> int:
+        return self.rank * self.count
+
+
+def check_divisible(num_experts: int, world: int) -> None:
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split evenly over {world} ranks")
+
+
+class CudaBackend:
+    """Per-rank math on the libsg_b200 kernels."""
+
+    def __init__(self, router: torch.Tensor, top_k: int, norm_topk_prob: bool, arena: SlottedGLU,
+                 shared: SlottedGLU | None, shared_gate: torch.Tensor | None):
+        self.router, self.top_k, self.norm = router, top_k, norm_topk_prob
+        self.arena, self.shared, self.shared_gate = arena, shared, shared_gate
+        self.ident = torch.arange(arena.num_slots, dtype=torch.int32, device=router.device)
+        self.timing: dict | None = None  # receives events around the expert kernels when set
+
+    def route(self, x: torch.Tensor):
+        logits = ops.router_linear(x, self.router)
+        return ops.route_topk(logits, self.top_k, self.norm)
+
+    def experts(self, rows: torch.Tensor, local_eids: torch.Tensor) -> torch.Tensor:
+        d = ops.dispatch(local_eids, self.arena.num_slots, self.ident)
+        if self.timing is None:
+            h = ops.glu_gate_up(self.arena, rows, d, pair_div=1)
+            return ops.glu_down(self.arena, h, d)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        h = ops.glu_gate_up(self.arena, rows, d, pair_div=1)
+        ev[1].record()
+        y = ops.glu_down(self.arena, h, d)
+        ev[2].record()
+        self.timing.setdefault("events", []).append(ev)
+        self.timing.setdefault("dispatch", []).append(d)
+        self.timing.setdefault("rows", []).append(rows.shape[0])
+        return y
+
+    def shared_terms(self, x: torch.Tensor):
+        if self.shared is None:
+            return None, None
+        from .layer import shared_expert_forward
+
+        return shared_expert_forward(self.shared, x), ops.router_linear(x, self.shared_gate).reshape(-1)
+
+    def combine(self, y: torch.Tensor, scores: torch.Tensor, shared_y, shared_gate) -> torch.Tensor:
+        return ops.combine(y, scores, shared_y, shared_gate)
+
+
+class ExpertParallelMoE:
+    """One slotted MoE layer split expert-parallel over the process group."""
+
+    def __init__(self, backend, num_experts: int, hidden: int, top_k: int, group=None):
+        self.backend = backend
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        check_divisible(num_experts, self.world)
+        self.shard = ExpertShard(self.rank, self.world, num_experts)
+        self.num_experts, self.hidden, self.top_k = num_experts, hidden, top_k
+        self.last_counts = None  # (send, recv) per-rank pair counts of the last step
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
+        if out.dtype == torch.bfloat16:  # moved as raw bytes (an all-to-all is a copy; gloo has no bf16)
+            out, inp = out.view(torch.uint8), inp.contiguous().view(torch.uint8)
+        dist.all_to_all_single(out, inp.contiguous(), output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=self.group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x [T, H] bf16 (this rank's tokens) -> [T, H] bf16."""
+        T, H = x.shape
+        k, R, per = self.top_k, self.world, self.shard.count
+        inds, scores = self.backend.route(x)
+        flat = inds.reshape(-1).to(torch.int64)
+        dest = torch.div(flat, per, rounding_mode="floor")
+        order = torch.argsort(dest, stable=True)            # pair ids in send order
+        send_counts = torch.bincount(dest, minlength=R)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        counts = torch.stack([send_counts, recv_counts]).cpu()
+        send, recv = counts[0].tolist(), counts[1].tolist()
+        self.last_counts = (send, recv)
+        n_recv = sum(recv)
+
+        send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+        send_eid = (flat.index_select(0, order) - dest.index_select(0, order) * per).to(torch.int32)
+        recv_rows = torch.empty((n_recv, H), dtype=x.dtype, device=x.device)
+        recv_eid = torch.empty((n_recv,), dtype=torch.int32, device=x.device)
+        self._a2a(recv_rows, send_rows, recv, send)
+        self._a2a(recv_eid, send_eid, recv, send)
+
+        y_local = self.backend.experts(recv_rows, recv_eid)
+        y_back = torch.empty((T * k, H), dtype=x.dtype, device=x.device)
+        self._a2a(y_back, y_local, send, recv)
+        y = torch.empty_like(y_back)
+        y.index_copy_(0, order, y_back)
+        shared_y, shared_gate = self.backend.shared_terms(x)
+        return self.backend.combine(y, scores, shared_y, shared_gate)
+
+    __call__ = forward
+
+
+def shard_layer(cfg, rank: int, world: int, device, seed_offset: int = 0):
+    """This rank's shard of the seeded synthetic layer ``cfg``: the same global
+    weights for any world size (all experts generated, the shard kept)."""
+    from .synthetic import _gen, _randn, fill_arena, make_expert_tensors
+
+    check_divisible(cfg.num_experts, world)
+    sh = ExpertShard(rank, world, cfg.num_experts)
+    c = cfg.cfg_id
+    router = _randn((cfg.num_experts, cfg.hidden), _gen(1000 * c + 1, device), device, 0.02)
+    full = make_expert_tensors(cfg, cfg.num_experts, cfg.inter, 1000 * c + 2 + seed_offset, device)
+    mine = {k: v[sh.first: sh.first + sh.count].contiguous() for k, v in full.items()}
+    del full
+    arena = SlottedGLU(sh.count, (cfg.inter, cfg.hidden), (cfg.hidden, cfg.inter), quant=cfg.quant, device=device)
+    fill_arena(arena, mine)
+    shared = sgate = None
+    if cfg.shared_inter is not None:
+        st = make_expert_tensors(cfg, 1, cfg.shared_inter, 1000 * c + 3, device)
+        shared = SlottedGLU(1, (cfg.shared_inter, cfg.hidden), (cfg.hidden, cfg.shared_inter), quant=cfg.quant,
+                            device=device)
+        fill_arena(shared, st)
+        sgate = _randn((1, cfg.hidden), _gen(1000 * c + 4, device), device, 0.02)
+    backend = CudaBackend(router, cfg.top_k, cfg.norm_topk_prob, arena, shared, sgate)
+    return backend, mine

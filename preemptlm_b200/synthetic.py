@@ -80,9 +80,10 @@ def make_expert_tensors(cfg: LayerConfig, n: int, inter: int, seed: int, device)
         if cfg.bits == 16:
             out[f"{p}.weight"] = w
         else:
-            q, s, b = quantize_affine(w, cfg.bits, 64)
-            out[f"{p}.weight"], out[f"{p}.scales"], out[f"{p}.biases"] = q, s, b
-            del w
+            parts = [quantize_affine(w[i: i + 32], cfg.bits, 64) for i in range(0, n, 32)]
+            for j, part in enumerate(("weight", "scales", "biases")):
+                out[f"{p}.{part}"] = torch.cat([q[j] for q in parts]) if len(parts) > 1 else parts[0][j]
+            del w, parts
     return out
 
 

@@ -124,8 +124,11 @@ def test_glu_matches_oracle(bits, H, I, E, T, k):
         gate = orc._mm_bf16(xr, ew.gate)
         href[p] = orc.swiglu(up, gate)[0]
         yref[p] = orc._mm_bf16(href[p: p + 1], ew.down)[0]
-    assert_close(f32(h), href, what="h")
-    assert_close(f32(y), yref, what="y")
+    # intermediates: the north-star bound scaled by the largest magnitude (a
+    # one-ulp bf16 flip of |h| ~ 8 is 0.06; the kernel skips the oracle's bf16
+    # rounding of dequantised weights, so flips near rounding ties are expected)
+    assert_close(f32(h), href, max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="h")
+    assert_close(f32(y), yref, max_abs=2e-2 * max(1.0, float(np.abs(yref).max())), what="y")
     # the device's own h through the oracle's down projection: isolates down
     hdev = f32(h)
     ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
