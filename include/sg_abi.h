@@ -100,24 +100,39 @@ int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
 /* ------------------------------------------------- gathered SwiGLU (a9/a10)
  * h[p, I] = swiglu(x[p / pair_div] @ gate^T, ... @ up^T) for every pair p of
  * every group u < counts[0], against arena slot slot_ids[u]; pairs listed by
- * perm/group_off (sg_dispatch layout).  Rounds x_up, x_gate, sigmoid, silu and
+ * perm/group_off (sg_dispatch layout); num_pairs = P (length of perm, rows of
+ * h; x has ceil(P / pair_div) rows).  Runs on the tcgen05 tensor-core kernel
+ * or the streaming GEMV (see sg_set_glu_path).  Rounds x_up, x_gate, sigmoid, silu and
  * the product to bf16 (experts.py:26-28).  pair_div = k for routed experts,
  * 1 when pairs are tokens (the shared expert).  grid_groups is a host-side
  * upper bound on counts[0].
  * Replaces the up/gate `gather_mm` calls and `swiglu_activation` in
  * `_gather_forward`, qwen3_x_moe.py:225-242.
  * Requires H % 64 == 0 and I % 64 == 0. */
-int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int pair_div,
+int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                    const int32_t* counts, const int32_t* slot_ids,
                    const int32_t* group_off, const int32_t* perm,
                    int grid_groups, uint16_t* h, void* stream);
 
-/* y[p, H] = bf16(h[p, I] @ down^T) for every listed pair.
+/* y[p, H] = bf16(h[p, I] @ down^T) for every listed pair (num_pairs rows).
  * Replaces the down `gather_mm` in `_gather_forward`, qwen3_x_moe.py:243-248. */
-int sg_glu_down(const sg_arena* arena, const uint16_t* h,
+int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs,
                 const int32_t* counts, const int32_t* slot_ids,
                 const int32_t* group_off, const int32_t* perm,
                 int grid_groups, uint16_t* y, void* stream);
+
+/* Kernel choice for sg_glu_gate_up / sg_glu_down: 0 = automatic (tcgen05 when
+ * the mean pairs per group is >= 2 and the shape allows: in-dim % 64, out-dim
+ * % 128, <= 2048 groups), 1 = streaming GEMV always, 2 = tcgen05 whenever the
+ * shape allows.  Process-wide.  No counterpart in the reference (MLX picks
+ * its own gather_mm kernels). */
+int sg_set_glu_path(int mode);
+
+/* First error a kernel of this library recorded on the current device since
+ * the last reset (SG_OK if none; SG_ERR_TIMEOUT when a bounded wait inside a
+ * kernel expired and the kernel gave up).  Synchronises with the device.
+ * No counterpart in the reference (MLX raises host exceptions). */
+int sg_device_status(int reset);
 
 /* ---------------------------------------------------------- combine (a11)
  * out[t] = bf16( bf16(sum_j bf16(y[t*k+j] * scores[t, j]))

@@ -259,16 +259,42 @@ int check_arena(const sg_arena* A) {
 
 }  // namespace sg
 
-extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int pair_div, const int32_t* counts,
-                              const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm,
-                              int grid_groups, uint16_t* h, void* stream) {
+namespace sg {
+bool tc_supported(const sg_arena* A, bool dual, int grid_groups);
+int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_by_pos,
+                  int out_by_pos, int P, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
+static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05
+
+// auto: the tensor-core path once the mean pairs per group reaches 2
+static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
+  if (g_glu_path == 1 || !tc_supported(A, dual, grid_groups)) return false;
+  if (g_glu_path == 2) return true;
+  return P >= 2 * grid_groups;
+}
+}  // namespace sg
+
+extern "C" int sg_set_glu_path(int mode) {
+  if (mode < 0 || mode > 2) return SG_ERR_INVALID_ARG;
+  sg::g_glu_path = mode;
+  return SG_OK;
+}
+
+extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                              const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                              const int32_t* perm, int grid_groups, uint16_t* h, void* stream) {
   int st = sg::check_arena(arena);
   if (st) return st;
-  if (!x || !counts || !slot_ids || !group_off || !perm || !h || pair_div < 1 || grid_groups < 0)
-    return SG_ERR_INVALID_ARG;
-  if (grid_groups == 0) return SG_OK;
+  if (num_pairs < 0 || pair_div < 1 || grid_groups < 0) return SG_ERR_INVALID_ARG;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!x || !counts || !slot_ids || !group_off || !perm || !h) return SG_ERR_INVALID_ARG;
   if (grid_groups > 65535) return SG_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
+  if (sg::use_tc(arena, true, num_pairs, grid_groups)) {
+    const int in_rows = (num_pairs + pair_div - 1) / pair_div;
+    return sg::tc_glu_launch(arena, true, x, in_rows, pair_div, 0, 0, num_pairs, counts, slot_ids, group_off, perm,
+                             grid_groups, h, s);
+  }
   switch (arena->bits) {
     case 16: return sg::launch_gemv<16, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
     case 8: return sg::launch_gemv<8, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
@@ -276,15 +302,19 @@ extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int pair
   }
 }
 
-extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, const int32_t* counts, const int32_t* slot_ids,
-                           const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* y,
-                           void* stream) {
+extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs, const int32_t* counts,
+                           const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                           uint16_t* y, void* stream) {
   int st = sg::check_arena(arena);
   if (st) return st;
-  if (!h || !counts || !slot_ids || !group_off || !perm || !y || grid_groups < 0) return SG_ERR_INVALID_ARG;
-  if (grid_groups == 0) return SG_OK;
+  if (num_pairs < 0 || grid_groups < 0) return SG_ERR_INVALID_ARG;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!h || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
   if (grid_groups > 65535) return SG_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
+  if (sg::use_tc(arena, false, num_pairs, grid_groups))
+    return sg::tc_glu_launch(arena, false, h, num_pairs, 1, 0, 0, num_pairs, counts, slot_ids, group_off, perm,
+                             grid_groups, y, s);
   switch (arena->bits) {
     case 16: return sg::launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
     case 8: return sg::launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);

@@ -129,7 +129,7 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Ten
         return h
     LAUNCHES[0] += 1
     lib = _abi.load()
-    _abi.check(lib.sg_glu_gate_up(ctypes.byref(arena.desc()), x.data_ptr(), int(pair_div), d.counts.data_ptr(),
+    _abi.check(lib.sg_glu_gate_up(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                   d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                   h.data_ptr(), _stream()), "sg_glu_gate_up")
     return h
@@ -144,10 +144,25 @@ def glu_down(arena, h: torch.Tensor, d: Dispatch) -> torch.Tensor:
         return y
     LAUNCHES[0] += 1
     lib = _abi.load()
-    _abi.check(lib.sg_glu_down(ctypes.byref(arena.desc()), h.data_ptr(), d.counts.data_ptr(), d.slot_ids.data_ptr(),
+    _abi.check(lib.sg_glu_down(ctypes.byref(arena.desc()), h.data_ptr(), P, d.counts.data_ptr(), d.slot_ids.data_ptr(),
                                d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),
                "sg_glu_down")
     return y
+
+
+GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2}
+
+
+def set_glu_path(mode: str) -> None:
+    """Pick the gathered-GLU kernel: "auto", "gemv" (streaming CUDA-core
+    GEMV) or "tc" (tcgen05 tensor cores)."""
+    _abi.call("sg_set_glu_path", GLU_PATHS[mode])
+
+
+def device_status(reset: bool = True) -> int:
+    """First error recorded by a kernel (SG_ERR_TIMEOUT after a bounded wait
+    expired), or 0."""
+    return int(_abi.load().sg_device_status(int(reset)))
 
 
 def combine(y: torch.Tensor, scores: torch.Tensor, shared_y: torch.Tensor | None,

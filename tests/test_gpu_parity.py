@@ -102,9 +102,19 @@ def test_dispatch_matches_numpy(P, E, resident):
 
 # ----------------------------------------------------------------------------- gathered GLU
 
+@pytest.fixture
+def glu_path(request):
+    ops.set_glu_path(request.param)
+    yield request.param
+    ops.set_glu_path("auto")
+    assert ops.device_status(reset=True) == 0  # no kernel gave up on a bounded wait
+
+
+@pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
 @pytest.mark.parametrize("bits", [16, 8, 4])
-@pytest.mark.parametrize("H,I,E,T,k", [(256, 128, 8, 5, 2), (2048, 768, 16, 33, 4), (1024, 512, 6, 1, 6)])
-def test_glu_matches_oracle(bits, H, I, E, T, k):
+@pytest.mark.parametrize("H,I,E,T,k", [(256, 128, 8, 5, 2), (2048, 768, 16, 33, 4), (1024, 512, 6, 1, 6),
+                                       (512, 256, 4, 300, 2)])
+def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((T, H), 11)
@@ -165,9 +175,10 @@ def test_combine_matches_oracle(shared):
 
 # ----------------------------------------------------------------------------- whole layer
 
-@pytest.mark.parametrize("cfg_name,T", [("cfg1", 1), ("cfg1", 4), ("cfg2", 16), ("cfg3", 1), ("cfg3", 8),
-                                        ("cfg4", 2)])
-def test_layer_matches_oracle(cfg_name, T):
+@pytest.mark.parametrize("glu_path", ["auto", "tc"], indirect=True)
+@pytest.mark.parametrize("cfg_name,T", [("cfg1", 1), ("cfg1", 4), ("cfg2", 16), ("cfg2", 512), ("cfg3", 1),
+                                        ("cfg3", 8), ("cfg4", 2)])
+def test_layer_matches_oracle(glu_path, cfg_name, T):
     cfg = CONFIGS[cfg_name]
     block, tens = make_layer(cfg, device=DEV)
     moe = Qwen3_xMoEWrapper(block, "fp", "model.layers.0.mlp", 0)
@@ -184,7 +195,8 @@ def test_layer_matches_oracle(cfg_name, T):
     assert torch.equal(res, out)
 
 
-def test_layer_full_size_sampled_tokens_cfg3():
+@pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
+def test_layer_full_size_sampled_tokens_cfg3(glu_path):
     """cfg3 at its largest decode batch (T=256): routing bit-exact for every
     token, outputs checked on a sample of tokens."""
     cfg = CONFIGS["cfg3"]
