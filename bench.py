@@ -25,6 +25,7 @@ which is not installed here) on the same workload, all host cores.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -51,6 +52,11 @@ def parse_args():
     ap.add_argument("--workload", default="cfg3")
     ap.add_argument("--tokens", type=int, default=256, help="decode tokens per GPU per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=None, help="override the expert count (profiling cases)")
+    ap.add_argument("--no-shared", action="store_true", help="drop the shared expert (profiling cases)")
+    ap.add_argument("--glu-path", choices=("auto", "gemv", "tc"), default="auto")
+    ap.add_argument("--profile", action="store_true",
+                    help="only warm-up + timed device-resident steps (for ncu captures); prints ms/step")
     return ap.parse_args()
 
 
@@ -264,6 +270,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = CONFIGS[args.workload]
+    if args.experts:
+        cfg = cfg.scaled(num_experts=args.experts, num_slots=args.experts)
+    if args.no_shared:
+        cfg = cfg.scaled(shared_inter=None)
+    ops.set_glu_path(args.glu_path)
     T = args.tokens
     H = cfg.hidden
     if world > 1:
@@ -305,21 +316,41 @@ def run_ours(args, rank, world, local_rank):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    host_t = []
+    gc.collect()
+    gc.disable()  # host-side collector pauses would leave the GPU idle between launches
     start.record()
     for i in range(args.steps):
+        step_ev[i].record()
+        h0 = time.perf_counter()
         run_step(xs[args.warmup + i], timing=timing)
+        host_t.append(time.perf_counter() - h0)
+    step_ev[args.steps].record()
     end.record()
     torch.cuda.synchronize()
+    gc.enable()
     barrier()
     clk = clocks.stop()
     launches = ops.LAUNCHES[0] - launches0
     ms_step = start.elapsed_time(end) / args.steps
+    per_step = [step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(args.steps)]
+    step_stats = {"min_ms": round(min(per_step), 4), "median_ms": round(statistics.median(per_step), 4),
+                  "max_ms": round(max(per_step), 4), "host_median_ms": round(1e3 * statistics.median(host_t), 4),
+                  "host_max_ms": round(1e3 * max(host_t), 4)}
     if world > 1:
         backend.timing = None
         t = torch.tensor([ms_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = float(t.item())
 
+    if args.profile:
+        if rank == 0:
+            print(json.dumps({"profile": cfg.name, "experts": cfg.num_experts, "tokens": T, "ms_per_step": ms_step,
+                          "steps_detail": step_stats}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     rl = _kernel_roofline(cfg, timing, timing.get("rows"), T)
     peak, peak_kind = hbm_peak()
     us_mean = rl["mean_unique"]
@@ -342,11 +373,14 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    gc.collect()
+    gc.disable()
     e_start.record()
     for i in range(args.steps):
         e2e_step(i)
     e_end.record()
     torch.cuda.synchronize()
+    gc.enable()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     if world > 1:
@@ -402,6 +436,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": launches,
+        "step_detail": step_stats,
         "clocks": clk,
         "cpu_baseline": cpu,
     }

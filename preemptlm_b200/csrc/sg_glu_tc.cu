@@ -8,15 +8,18 @@
 // SwiGLU; the down projection has one.  Accumulators are double buffered so
 // the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// Warp roles (11 warps, one CTA per SM, persistent over a static tile list):
+// Warp roles (15 warps, one CTA per SM, persistent over a static tile list):
 //   w0      TMA producer of weight tiles: bf16 straight into the SW128 operand
-//           layout, or packed 8/4-bit words (SW64 / SW32) for the dequantisers
+//           layout, or packed 8/4-bit words (128 bytes per row, SW128) for the
+//           dequantisers
 //   w1      TMEM allocation + single-thread tcgen05.mma issue + commits
 //   w2      TMA gather4 producer of the B rows (token rows picked by the
-//           dispatch permutation)
-//   w3-w6   dequantisers (quantised arenas): thread r owns row r of the tile,
-//           w = bf16(scale * q + bias) written in the SW128 operand layout
-//   w7-w10  epilogue: tcgen05.ld -> SwiGLU / bf16 -> global, one warp per
+//           dispatch permutation) into its own ring
+//   w3-w10  dequantisers (quantised arenas): 256 threads, each one row of one
+//           matrix (gate/up) or half a row (down); w = bf16(scale * q + bias)
+//           computed exactly in fp32 with magic-number integer-to-float and
+//           packed f32x2 FMA/ADD, written in the SW128 operand layout
+//   w11-w14 epilogue: tcgen05.ld -> SwiGLU / bf16 -> global, one warp per
 //           32-lane TMEM quadrant
 //
 // Every mbarrier wait is bounded (about one second of clock64); on expiry the
@@ -36,9 +39,10 @@ namespace tc {
 
 constexpr int BM = 128;            // weight rows per tile (MMA M)
 constexpr int BK = 64;             // K per pipeline stage (one 128-byte swizzle atom of bf16)
-constexpr int NUM_WARPS = 11;
+constexpr int NUM_WARPS = 15;
 constexpr int NUM_THREADS = NUM_WARPS * 32;
-constexpr int RING_BUDGET = 192 * 1024;
+constexpr int DQ_WARP0 = 3, DQ_WARPS = 8;  // epilogue warps follow: 11..14
+constexpr int RING_BUDGET = 208 * 1024;
 constexpr int PLAN_MAX_GROUPS = 2048;
 constexpr long long WAIT_CYCLES = 2000000000LL;  // ~1 s
 
@@ -54,22 +58,25 @@ struct Cfg {
   static constexpr int NMAT = DUAL ? 2 : 1;
   static constexpr int A_MAT = BM * BK * 2;                       // one bf16 operand tile
   static constexpr int A_BYTES = NMAT * A_MAT;
-  static constexpr int P_MAT = BITS == 16 ? 0 : BM * BK * BITS / 8;  // one packed tile
+  // one packed tile: 128 rows x 128 bytes (KP operand stages of BK weights)
+  static constexpr int KP = BITS == 16 ? 1 : 128 * 8 / (BK * BITS);
+  static constexpr int P_MAT = BITS == 16 ? 0 : BM * 128;
   static constexpr int P_BYTES = NMAT * P_MAT;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int SA = BITS == 16 ? cmin(8, RING_BUDGET / (A_BYTES + B_BYTES)) : (DUAL ? 3 : 4);
-  static constexpr int SP = BITS == 16 ? 0 : cmin(8, (RING_BUDGET - SA * (A_BYTES + B_BYTES)) / P_BYTES);
+  static constexpr int SB = cmin(8, 32768 / B_BYTES < 2 ? 2 : 32768 / B_BYTES);
+  static constexpr int SA = BITS == 16 ? cmin(8, (RING_BUDGET - SB * B_BYTES) / A_BYTES) : (DUAL ? 3 : 4);
+  static constexpr int SP = BITS == 16 ? 0 : cmin(6, (RING_BUDGET - SA * A_BYTES - SB * B_BYTES) / P_BYTES);
   static constexpr int ACC_COLS = NMAT * BN;
   static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = pow2ceil(NACC * ACC_COLS < 32 ? 32 : NACC * ACC_COLS);
   // shared memory carve-up (offsets from a 1024-aligned base)
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + SA * A_BYTES;
-  static constexpr int OFF_P = OFF_B + SA * B_BYTES;
+  static constexpr int OFF_P = OFF_B + SB * B_BYTES;
   static constexpr int OFF_PLAN = OFF_P + SP * P_BYTES;
   static constexpr int OFF_ROWS = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
   static constexpr int OFF_BAR = (OFF_ROWS + BN * 4 + 15) & ~15;
-  static constexpr int NUM_BARS = 3 * SA + 2 * SP + 2 * NACC;
+  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC;
   static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
   static_assert(SA >= 2 && (BITS == 16 || SP >= 2), "pipeline too shallow");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -175,58 +182,108 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------ dequantisation
-__device__ __forceinline__ float qf(uint32_t q) {  // exact small unsigned int -> fp32
-  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+// w = fp32(scale * q + bias), exactly as the oracle forms it, then bf16:
+//   v = 2^15 + q * 2^(p - 8) is built by placing q at bit p of the mantissa of
+//   2^15 (one PRMT / LOP3; the field must end below bit 23, the exponent);
+//   fma(v, s_p, -2^15 * s_p) = q * scale exactly (s_p = scale * 2^(8 - p), a
+//   power-of-two rescale); then one add of bias.
+// Two weights at a time with packed fma.rn.f32x2 / add.rn.f32x2.
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
 }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+__device__ __forceinline__ uint32_t dq_pair(uint32_t v_lo, uint32_t v_hi, unsigned long long s2,
+                                            unsigned long long c2, unsigned long long b2) {
+  const unsigned long long v = (static_cast<unsigned long long>(v_hi) << 32) | v_lo;
+  unsigned long long t, w;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(t) : "l"(v), "l"(s2), "l"(c2));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(w) : "l"(t), "l"(b2));
+  __nv_bfloat162 r = __floats2bfloat162_rn(__uint_as_float(static_cast<uint32_t>(w)),
+                                           __uint_as_float(static_cast<uint32_t>(w >> 32)));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// Row r of one packed stage tile -> 64 bf16 (8 x 16-byte chunks) in the SW128
-// operand layout of the A stage tile.
+struct GroupScale {  // one (scale, bias) group in the forms the converters use
+  // q8: p1 = (s, s).  q4: p1 = (s8, s12), p2 = (s16, s8), p3 = (s12, s16) with
+  // s_p = scale * 2^(8 - p); c* = -2^15 * s*; b = (bias, bias)
+  unsigned long long p1, c1, p2, c2, p3, c3, b;
+};
 template <int BITS>
-__device__ __forceinline__ void dequant_row(const uint8_t* p_tile, uint8_t* a_tile, int r, float s, float b) {
-  uint8_t* arow = a_tile + r * 128;
+__device__ __forceinline__ GroupScale make_scale(float s, float b) {
+  GroupScale g;
+  g.b = f2pack(b, b);
   if (BITS == 8) {
-    // SW64 packed tile: 64-byte rows, 16-byte chunk c at c ^ ((r >> 1) & 3)
-    const uint8_t* prow = p_tile + r * 64;
+    g.p1 = f2pack(s, s);
+    g.c1 = f2pack(-32768.0f * s, -32768.0f * s);
+  } else {
+    const float s8 = s, s12 = s * 0.0625f, s16 = s * 0.00390625f;
+    g.p1 = f2pack(s8, s12);
+    g.c1 = f2pack(-32768.0f * s8, -32768.0f * s12);
+    g.p2 = f2pack(s16, s8);
+    g.c2 = f2pack(-32768.0f * s16, -32768.0f * s8);
+    g.p3 = f2pack(s12, s16);
+    g.c3 = f2pack(-32768.0f * s12, -32768.0f * s16);
+  }
+  return g;
+}
+
+// q8: 16-byte packed chunk (16 weights) -> two 16-byte bf16 chunks
+__device__ __forceinline__ void dq8_chunk(uint4 v, const GroupScale& g, uint4& o0, uint4& o1) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(prow + ((c ^ ((r >> 1) & 3)) << 4));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t a0 = __byte_perm(w[i], 0x47000000u, 0x7404);
+    const uint32_t a1 = __byte_perm(w[i], 0x47000000u, 0x7414);
+    const uint32_t a2 = __byte_perm(w[i], 0x47000000u, 0x7424);
+    const uint32_t a3 = __byte_perm(w[i], 0x47000000u, 0x7434);
+    o[2 * i] = dq_pair(a0, a1, g.p1, g.c1, g.b);
+    o[2 * i + 1] = dq_pair(a2, a3, g.p1, g.c1, g.b);
+  }
+  o0 = make_uint4(o[0], o[1], o[2], o[3]);
+  o1 = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// q4: one packed word (8 weights, nibble m at bits 4m) -> one 16-byte bf16 chunk.
+// A nibble may sit at mantissa bit 8, 12 or 16 only (bits 20-23 would reach
+// the exponent), so three shifted copies of the word feed the eight weights.
+__device__ __forceinline__ uint4 dq4_word(uint32_t w, const GroupScale& g) {
+  const uint32_t a = w << 8, b = w >> 4, c = w >> 16;
+  const uint32_t M = 0x47000000u;
+  const uint32_t v0 = (a & 0x00000F00u) | M, v1 = (a & 0x0000F000u) | M;  // nibbles 0,1 at bits 8,12
+  const uint32_t v2 = (a & 0x000F0000u) | M, v3 = (b & 0x00000F00u) | M;  // nibbles 2,3 at bits 16,8
+  const uint32_t v4 = (b & 0x0000F000u) | M, v5 = (b & 0x000F0000u) | M;  // nibbles 4,5 at bits 12,16
+  const uint32_t v6 = (c & 0x00000F00u) | M, v7 = (c & 0x0000F000u) | M;  // nibbles 6,7 at bits 8,12
+  return make_uint4(dq_pair(v0, v1, g.p1, g.c1, g.b), dq_pair(v2, v3, g.p2, g.c2, g.b),
+                    dq_pair(v4, v5, g.p3, g.c3, g.b), dq_pair(v6, v7, g.p1, g.c1, g.b));
+}
+
+// Dequantise output chunks [oc0, oc0 + NOC) of row r (8 weights per chunk)
+// of operand sub-stage j (BK weights) from a packed stage tile (SW128: 128-byte
+// rows, 16-byte chunk c at c ^ (r & 7)) into the SW128 bf16 operand tile.
+template <int BITS, int NOC>
+__device__ __forceinline__ void dequant_part(const uint8_t* p_tile, uint8_t* a_tile, int r, int j, int oc0,
+                                             const GroupScale& g) {
+  uint8_t* arow = a_tile + r * 128;
+  const uint8_t* prow = p_tile + r * 128;
+  if (BITS == 8) {
+    // sub-stage j = bytes [64 j, 64 j + 64) = packed chunks 4j .. 4j+3 (16 weights each)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // output chunk oc = 2c + h holds weights 8oc .. 8oc+7
-        uint4 o;
-        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t word = w[2 * h + (q >> 1)];
-          const int sh = (q & 1) * 16;
-          op[q] = pack_bf16x2(fmaf(qf((word >> sh) & 0xFFu), s, b), fmaf(qf((word >> (sh + 8)) & 0xFFu), s, b));
-        }
-        const int oc = 2 * c + h;
-        *reinterpret_cast<uint4*>(arow + ((oc ^ (r & 7)) << 4)) = o;
-      }
+    for (int c = oc0 / 2; c < (oc0 + NOC) / 2; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(prow + (((4 * j + c) ^ (r & 7)) << 4));
+      uint4 o0, o1;
+      dq8_chunk(v, g, o0, o1);
+      *reinterpret_cast<uint4*>(arow + (((2 * c) ^ (r & 7)) << 4)) = o0;
+      *reinterpret_cast<uint4*>(arow + (((2 * c + 1) ^ (r & 7)) << 4)) = o1;
     }
   } else {
-    // SW32 packed tile: 32-byte rows, 16-byte chunk c at c ^ ((r >> 2) & 1)
-    const uint8_t* prow = p_tile + r * 32;
+    // sub-stage j = bytes [32 j, 32 j + 32) = packed chunks 2j, 2j+1 (32 weights each)
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(prow + ((c ^ ((r >> 2) & 1)) << 4));
+    for (int c = oc0 / 4; c < (oc0 + NOC) / 4; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(prow + (((2 * j + c) ^ (r & 7)) << 4));
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {  // output chunk oc = 4c + h = one 32-bit word (8 weights)
-        uint4 o;
-        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-        const uint32_t word = w[h];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          op[q] = pack_bf16x2(fmaf(qf((word >> (8 * q)) & 0xFu), s, b), fmaf(qf((word >> (8 * q + 4)) & 0xFu), s, b));
-        const int oc = 4 * c + h;
-        *reinterpret_cast<uint4*>(arow + ((oc ^ (r & 7)) << 4)) = o;
-      }
+      for (int h = 0; h < 4; ++h)
+        *reinterpret_cast<uint4*>(arow + (((4 * c + h) ^ (r & 7)) << 4)) = dq4_word(w[h], g);
     }
   }
 }
@@ -274,6 +331,152 @@ __device__ __forceinline__ Tile tile_of(int t, const int* plan, int U, int NT, c
 }
 
 // ------------------------------------------------------------------ the kernel
+// Scale/bias stream of one dequantiser thread: V groups per vector load
+// (V = 4 when the group count allows 8-byte loads, else 1), the next vector
+// always in flight, crossing into the next tile of the thread's walk.
+template <int V>
+struct ScaleVec;
+template <>
+struct ScaleVec<4> {
+  uint2 s, b;
+  __device__ __forceinline__ void load(const uint16_t* sp, const uint16_t* bp, int v) {
+    s = __ldg(reinterpret_cast<const uint2*>(sp) + v);
+    b = __ldg(reinterpret_cast<const uint2*>(bp) + v);
+  }
+  __device__ __forceinline__ float sc(int j) const {
+    const uint32_t w = j < 2 ? s.x : s.y;
+    return (j & 1) ? hi_bf16(w) : lo_bf16(w);
+  }
+  __device__ __forceinline__ float bi(int j) const {
+    const uint32_t w = j < 2 ? b.x : b.y;
+    return (j & 1) ? hi_bf16(w) : lo_bf16(w);
+  }
+};
+template <>
+struct ScaleVec<1> {
+  uint16_t s, b;
+  __device__ __forceinline__ void load(const uint16_t* sp, const uint16_t* bp, int v) {
+    s = __ldg(sp + v);
+    b = __ldg(bp + v);
+  }
+  __device__ __forceinline__ float sc(int) const { return bf16_to_f32(s); }
+  __device__ __forceinline__ float bi(int) const { return bf16_to_f32(b); }
+};
+
+template <int BITS, bool DUAL, int BN, int V>
+__device__ __forceinline__ void dequant_role(const Args& args, const int* plan, int U, int NT, int total,
+                                             uint8_t* sA, const uint8_t* sP, uint64_t* a_full, uint64_t* a_empty,
+                                             uint64_t* p_full, uint64_t* p_empty, Ctl ctl) {
+  using C = Cfg<BITS, DUAL, BN>;
+  const int d = (threadIdx.x >> 5) * 32 - DQ_WARP0 * 32 + (threadIdx.x & 31);  // 0..255
+  const int r = d & 127;
+  const int part = d >> 7;               // DUAL: matrix (gate / up); single: half row
+  const int mat = DUAL ? part : 0;
+  const int oc0 = DUAL ? 0 : part * 4;   // first output chunk of this thread
+  const int K = args.K, NKB = K / BK, groups = K / 64, nvec = groups / V;
+  const uint16_t* sbase = mat ? args.s1 : args.s0;
+  const uint16_t* bbase = mat ? args.b1 : args.b0;
+  // per-thread row pointers of a tile (a slot outside the arena reads row 0 and
+  // dequantises zeros: its A tile is the TMA's zero fill and the epilogue
+  // writes zeros for it)
+  auto row_ptrs = [&](int t, const uint16_t*& sp, const uint16_t*& bp, bool& sok) {
+    const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+    sok = tl.slot >= 0 && tl.slot < args.num_slots;
+    const size_t row = sok ? (size_t)tl.slot * args.OUT + tl.m * BM + r : 0;
+    sp = sbase + row * groups;
+    bp = bbase + row * groups;
+  };
+  int sa = 0, sp_i = 0;
+  uint32_t pa = 0, pp = 0;
+  bool ok = true;
+  int t = blockIdx.x;
+  if (t >= total) return;
+  const uint16_t *cs, *cb;
+  bool csok;
+  row_ptrs(t, cs, cb, csok);
+  ScaleVec<V> cur, nxt;
+  cur.load(cs, cb, 0);
+  int nxt_t = t, nxt_v = 1;  // (tile, vector) held in nxt
+  if (nvec == 1) {
+    nxt_t = t + gridDim.x;
+    nxt_v = 0;
+  }
+  if (nxt_t < total) {
+    const uint16_t *ns, *nb;
+    bool nsok;
+    row_ptrs(nxt_t, ns, nb, nsok);
+    nxt.load(ns, nb, nxt_v);
+  }
+  for (; t < total && ok; t += gridDim.x) {
+    bool sok;
+    const uint16_t *tsp, *tbp;
+    row_ptrs(t, tsp, tbp, sok);
+    for (int kb = 0; kb < NKB; ++kb) {
+      const int j = kb % V;
+      if (j == 0 && kb > 0) {  // next vector of this tile becomes current
+        cur = nxt;
+        int vn = kb / V + 1;
+        int tn = t;
+        if (vn >= nvec) {
+          vn = 0;
+          tn = t + gridDim.x;
+        }
+        if (tn < total) {
+          const uint16_t *ns, *nb;
+          bool nsok;
+          row_ptrs(tn, ns, nb, nsok);
+          nxt.load(ns, nb, vn);
+        }
+      }
+      const GroupScale g = make_scale<BITS>(sok ? cur.sc(j) : 0.f, sok ? cur.bi(j) : 0.f);
+      const int jp = kb % C::KP;  // operand sub-stage within the packed stage
+      ok = (jp != 0 || wait_bar(&p_full[sp_i], pp, ctl)) && wait_bar(&a_empty[sa], pa ^ 1, ctl);
+      ok = __all_sync(0xffffffffu, ok);  // keep the warp converged for __syncwarp
+      if (!ok) break;
+      const uint8_t* ptile = sP + sp_i * C::P_BYTES + mat * C::P_MAT;
+      uint8_t* atile = sA + sa * C::A_BYTES + mat * C::A_MAT;
+      if (DUAL) dequant_part<BITS, 8>(ptile, atile, r, jp, 0, g);
+      else dequant_part<BITS, 4>(ptile, atile, r, jp, oc0, g);
+      fence_async_smem();
+      __syncwarp();
+      const bool last_sub = jp == C::KP - 1 || kb == NKB - 1;
+      if ((threadIdx.x & 31) == 0) {
+        mbar_arrive(&a_full[sa]);
+        if (last_sub) mbar_arrive(&p_empty[sp_i]);
+      }
+      if (++sa == C::SA) { sa = 0; pa ^= 1; }
+      if (last_sub && ++sp_i == C::SP) { sp_i = 0; pp ^= 1; }
+    }
+    // the first vector of the next tile is already in nxt
+    if (nvec > 1 || V == 1) {
+      cur = nxt;
+      const int tn = t + gridDim.x;
+      if (tn < total) {
+        int vn = 1, tt = tn;
+        if (nvec == 1) {
+          vn = 0;
+          tt = tn + gridDim.x;
+        }
+        if (tt < total) {
+          const uint16_t *ns, *nb;
+          bool nsok;
+          row_ptrs(tt, ns, nb, nsok);
+          nxt.load(ns, nb, vn);
+        }
+      }
+    } else {
+      cur = nxt;
+      const int tt = t + 2 * gridDim.x;
+      if (tt < total) {
+        const uint16_t *ns, *nb;
+        bool nsok;
+        row_ptrs(tt, ns, nb, nsok);
+        nxt.load(ns, nb, 0);
+      }
+    }
+  }
+}
+
 template <int BITS, bool DUAL, int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
@@ -287,11 +490,12 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   int* plan = reinterpret_cast<int*>(smem + C::OFF_PLAN);
   int* rows = reinterpret_cast<int*>(smem + C::OFF_ROWS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* a_full = bars;                   // [SA] A stage ready (TMA tx or 4 dequant warps)
-  uint64_t* b_full = a_full + C::SA;         // [SA] B stage ready (TMA tx)
-  uint64_t* a_empty = b_full + C::SA;        // [SA] A+B stage consumed (MMA commit)
-  uint64_t* p_full = a_empty + C::SA;        // [SP] packed stage landed (TMA tx)
-  uint64_t* p_empty = p_full + C::SP;        // [SP] packed stage consumed (4 dequant warps)
+  uint64_t* a_full = bars;                   // [SA] A stage ready (TMA tx or 8 dequant warps)
+  uint64_t* a_empty = a_full + C::SA;        // [SA] A stage consumed (MMA commit)
+  uint64_t* b_full = a_empty + C::SA;        // [SB] B stage landed (TMA tx)
+  uint64_t* b_empty = b_full + C::SB;        // [SB] B stage consumed (MMA commit)
+  uint64_t* p_full = b_empty + C::SB;        // [SP] packed stage landed (TMA tx)
+  uint64_t* p_empty = p_full + C::SP;        // [SP] packed stage consumed (8 dequant warps)
   uint64_t* acc_full = p_empty + C::SP;      // [NACC] accumulator ready (MMA commit)
   uint64_t* acc_empty = acc_full + C::NACC;  // [NACC] accumulator drained (4 epilogue warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
@@ -305,13 +509,16 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::SA; ++i) {
-      mbar_init(&a_full[i], BITS == 16 ? 1 : 4);
-      mbar_init(&b_full[i], 1);
+      mbar_init(&a_full[i], BITS == 16 ? 1 : DQ_WARPS);
       mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < C::SB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < C::SP; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], 4);
+      mbar_init(&p_empty[i], DQ_WARPS);
     }
     for (int i = 0; i < C::NACC; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -357,87 +564,105 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   if (warp == 0) {
     // ---------------------------------------------------------------- weight producer
     if (lane == 0) {
-      int sa = 0, sp = 0;
-      uint32_t pa = 0, pp = 0;  // phase bits
-      int issued_a = 0, issued_p = 0;
+      int s_i = 0;
+      uint32_t ph = 0;
+      int issued = 0;
       bool ok = true;
+      constexpr int RING = BITS == 16 ? C::SA : C::SP;
+      uint64_t* full = BITS == 16 ? a_full : p_full;
+      uint64_t* empty = BITS == 16 ? a_empty : p_empty;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = tile_of<BN>(t, plan, U, NT, args);
         const int row0 = tl.slot * args.OUT + tl.m * BM;
-        for (int kb = 0; kb < NKB && ok; ++kb) {
+        const int nstage = BITS == 16 ? NKB : (NKB + C::KP - 1) / C::KP;
+        for (int kb = 0; kb < nstage; ++kb) {
+          ok = wait_bar(&empty[s_i], ph ^ 1, ctl);
+          if (!ok) break;
           if (BITS == 16) {
-            ok = wait_bar(&a_empty[sa], pa ^ 1, ctl);
-            if (!ok) break;
-            mbar_expect_tx(&a_full[sa], C::A_BYTES);
-            tma_load_2d(sA + sa * C::A_BYTES, &tmA0, kb * BK, row0, &a_full[sa]);
-            if (DUAL) tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, kb * BK, row0, &a_full[sa]);
-            ++issued_a;
-            if (++sa == C::SA) { sa = 0; pa ^= 1; }
+            mbar_expect_tx(&full[s_i], C::A_BYTES);
+            tma_load_2d(sA + s_i * C::A_BYTES, &tmA0, kb * BK, row0, &full[s_i]);
+            if (DUAL) tma_load_2d(sA + s_i * C::A_BYTES + C::A_MAT, &tmA1, kb * BK, row0, &full[s_i]);
           } else {
-            ok = wait_bar(&p_empty[sp], pp ^ 1, ctl);
-            if (!ok) break;
-            mbar_expect_tx(&p_full[sp], C::P_BYTES);
-            const int col = kb * BK * BITS / 32;  // packed uint32 column
-            tma_load_2d(sP + sp * C::P_BYTES, &tmA0, col, row0, &p_full[sp]);
-            if (DUAL) tma_load_2d(sP + sp * C::P_BYTES + C::P_MAT, &tmA1, col, row0, &p_full[sp]);
-            ++issued_p;
-            if (++sp == C::SP) { sp = 0; pp ^= 1; }
+            // 128 bytes of every row: columns beyond the row end are the TMA's
+            // zero fill and are never dequantised
+            mbar_expect_tx(&full[s_i], C::P_BYTES);
+            const int col = kb * 32;  // packed uint32 column (32 words = 128 bytes)
+            tma_load_2d(sP + s_i * C::P_BYTES, &tmA0, col, row0, &full[s_i]);
+            if (DUAL) tma_load_2d(sP + s_i * C::P_BYTES + C::P_MAT, &tmA1, col, row0, &full[s_i]);
           }
+          ++issued;
+          if (++s_i == RING) { s_i = 0; ph ^= 1; }
         }
       }
       if (!ok) {  // drain this thread's copies still in flight (bounded)
-        Ctl drain_ctl = ctl;
-        int depth = BITS == 16 ? min(issued_a, C::SA) : min(issued_p, C::SP);
-        for (int i = 0; i < depth; ++i) {
-          int s = (BITS == 16 ? sa : sp) - 1 - i;
-          uint32_t ph = BITS == 16 ? pa : pp;
-          const int ring = BITS == 16 ? C::SA : C::SP;
-          if (s < 0) { s += ring; ph ^= 1; }
-          uint64_t* fb = BITS == 16 ? &a_full[s] : &p_full[s];
+        for (int i = 0; i < min(issued, RING); ++i) {
+          int s = s_i - 1 - i;
+          uint32_t p = ph;
+          if (s < 0) { s += RING; p ^= 1; }
           const long long t0 = clock64();
-          while (!mbar_try_wait(fb, ph) && clock64() - t0 < WAIT_CYCLES) {
+          while (!mbar_try_wait(&full[s], p) && clock64() - t0 < WAIT_CYCLES) {
           }
-          (void)drain_ctl;
         }
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------------- B gather producer
-    int sa = 0;
-    uint32_t pa = 0;
+    // rows[] holds the current tile's B rows; every lane loads the next tile's
+    // row for its column before lane 0 issues the current tile, so the perm
+    // lookups overlap the issue loop.
+    int sb = 0;
+    uint32_t pb = 0;
     bool ok = true;
     int issued = 0;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    auto row_of = [&](const Tile& tl, int j) {
+      const int pos = tl.goff + tl.n0 + (j < tl.nvalid ? j : 0);
+      return args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
+    };
+    constexpr int RPL = (BN + 31) / 32;  // rows per lane
+    int nxt[RPL];
+    int t = blockIdx.x;
+    if (t < total) {
       const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+#pragma unroll
+      for (int i = 0; i < RPL; ++i)
+        if (lane + 32 * i < BN) nxt[i] = row_of(tl, lane + 32 * i);
+    }
+    for (; t < total && ok; t += gridDim.x) {
       __syncwarp();
-      for (int j = lane; j < BN; j += 32) {
-        const int pos = tl.goff + tl.n0 + (j < tl.nvalid ? j : 0);
-        rows[j] = args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i)
+        if (lane + 32 * i < BN) rows[lane + 32 * i] = nxt[i];
+      __syncwarp();
+      const int tn = t + gridDim.x;
+      if (tn < total) {  // loads in flight while lane 0 issues tile t
+        const Tile tl = tile_of<BN>(tn, plan, U, NT, args);
+#pragma unroll
+        for (int i = 0; i < RPL; ++i)
+          if (lane + 32 * i < BN) nxt[i] = row_of(tl, lane + 32 * i);
       }
-      __syncwarp();
       if (lane == 0) {
         for (int kb = 0; kb < NKB; ++kb) {
-          ok = wait_bar(&a_empty[sa], pa ^ 1, ctl);
+          ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
           if (!ok) break;
-          mbar_expect_tx(&b_full[sa], C::B_BYTES);
-          uint8_t* dst = sB + sa * C::B_BYTES;
+          mbar_expect_tx(&b_full[sb], C::B_BYTES);
+          uint8_t* dst = sB + sb * C::B_BYTES;
 #pragma unroll 1
           for (int g = 0; g < BN / 4; ++g)
             tma_gather4(dst + g * 512, &tmB, kb * BK, rows[4 * g], rows[4 * g + 1], rows[4 * g + 2],
-                        rows[4 * g + 3], &b_full[sa]);
+                        rows[4 * g + 3], &b_full[sb]);
           ++issued;
-          if (++sa == C::SA) { sa = 0; pa ^= 1; }
+          if (++sb == C::SB) { sb = 0; pb ^= 1; }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
     if (!ok && lane == 0) {
-      for (int i = 0; i < min(issued, C::SA); ++i) {
-        int s = sa - 1 - i;
-        uint32_t ph = pa;
-        if (s < 0) { s += C::SA; ph ^= 1; }
+      for (int i = 0; i < min(issued, C::SB); ++i) {
+        int s = sb - 1 - i;
+        uint32_t p = pb;
+        if (s < 0) { s += C::SB; p ^= 1; }
         const long long t0 = clock64();
-        while (!mbar_try_wait(&b_full[s], ph) && clock64() - t0 < WAIT_CYCLES) {
+        while (!mbar_try_wait(&b_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
         }
       }
     }
@@ -445,8 +670,8 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16<BN>();
-      int sa = 0;
-      uint32_t pa = 0;
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
@@ -457,11 +682,11 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         tc_fence_after();
         const uint32_t d0 = tmem + ab * C::ACC_COLS;
         for (int kb = 0; kb < NKB; ++kb) {
-          ok = wait_bar(&a_full[sa], pa, ctl) && wait_bar(&b_full[sa], pa, ctl);
+          ok = wait_bar(&a_full[sa], pa, ctl) && wait_bar(&b_full[sb], pb, ctl);
           if (!ok) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + sa * C::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + sa * C::B_BYTES);
+          const uint32_t b_base = smem_u32(sB + sb * C::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t bd = desc_sw128(b_base + kk * 32);
@@ -470,68 +695,23 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             if (DUAL) umma_bf16(d0 + BN, desc_sw128(a_base + C::A_MAT + kk * 32), bd, idesc, acc);
           }
           umma_commit(&a_empty[sa]);
+          umma_commit(&b_empty[sb]);
           if (++sa == C::SA) { sa = 0; pa ^= 1; }
+          if (++sb == C::SB) { sb = 0; pb ^= 1; }
         }
         if (ok) umma_commit(&acc_full[ab]);
       }
     }
-  } else if (warp >= 3 && warp <= 6) {
+  } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + DQ_WARPS) {
     // ---------------------------------------------------------------- dequantisers
     if (BITS != 16) {
-      const int r = (warp - 3) * 32 + lane;
-      const int groups = K / 64;
-      int sa = 0, sp = 0;
-      uint32_t pa = 0, pp = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const Tile tl = tile_of<BN>(t, plan, U, NT, args);
-        // a slot outside the arena (a miss) reads no scales: its A tile is the
-        // TMA's zero fill, its outputs are written as zeros by the epilogue
-        const bool sok = tl.slot >= 0 && tl.slot < args.num_slots;
-        const size_t row = sok ? (size_t)tl.slot * args.OUT + tl.m * BM + r : 0;
-        const uint16_t* s0 = args.s0 + row * groups;
-        const uint16_t* b0 = args.b0 + row * groups;
-        const uint16_t* s1 = DUAL ? args.s1 + row * groups : nullptr;
-        const uint16_t* b1 = DUAL ? args.b1 + row * groups : nullptr;
-        float ns0 = 0.f, nb0 = 0.f, ns1 = 0.f, nb1 = 0.f;
-        if (sok) {
-          ns0 = bf16_to_f32(s0[0]);
-          nb0 = bf16_to_f32(b0[0]);
-          if (DUAL) {
-            ns1 = bf16_to_f32(s1[0]);
-            nb1 = bf16_to_f32(b1[0]);
-          }
-        }
-        for (int kb = 0; kb < NKB; ++kb) {
-          const float cs0 = ns0, cb0 = nb0, cs1 = ns1, cb1 = nb1;
-          if (sok && kb + 1 < NKB) {  // one group ahead
-            ns0 = bf16_to_f32(s0[kb + 1]);
-            nb0 = bf16_to_f32(b0[kb + 1]);
-            if (DUAL) {
-              ns1 = bf16_to_f32(s1[kb + 1]);
-              nb1 = bf16_to_f32(b1[kb + 1]);
-            }
-          }
-          ok = wait_bar(&p_full[sp], pp, ctl) && wait_bar(&a_empty[sa], pa ^ 1, ctl);
-          ok = __all_sync(0xffffffffu, ok);  // keep the warp converged for __syncwarp
-          if (!ok) break;
-          const uint8_t* ptile = sP + sp * C::P_BYTES;
-          uint8_t* atile = sA + sa * C::A_BYTES;
-          dequant_row<BITS>(ptile, atile, r, cs0, cb0);
-          if (DUAL) dequant_row<BITS>(ptile + C::P_MAT, atile + C::A_MAT, r, cs1, cb1);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&a_full[sa]);
-            mbar_arrive(&p_empty[sp]);
-          }
-          if (++sa == C::SA) { sa = 0; pa ^= 1; }
-          if (++sp == C::SP) { sp = 0; pp ^= 1; }
-        }
-      }
+      if ((K / 64) % 4 == 0)
+        dequant_role<BITS, DUAL, BN, 4>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl);
+      else
+        dequant_role<BITS, DUAL, BN, 1>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 7-10)
+    // ---------------------------------------------------------------- epilogue (warps 11-14)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     int it = 0;
@@ -539,31 +719,41 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
       const int ab = it % C::NACC;
       const uint32_t accp = static_cast<uint32_t>((it / C::NACC) & 1);
+      const Tile tl = tile_of<BN>(t, plan, U, NT, args);
       ok = wait_bar(&acc_full[ab], accp, ctl);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
       if (!ok) break;
       tc_fence_after();
-      const Tile tl = tile_of<BN>(t, plan, U, NT, args);
       const bool slot_ok = tl.slot >= 0 && tl.slot < args.num_slots;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + ab * C::ACC_COLS;
       const int ocol = tl.m * BM + r;
 #pragma unroll 1
-      for (int j0 = 0; j0 < BN; j0 += 16) {
-        uint32_t g[16], u[16];
-        tmem_ld16(tbase + j0, g);
-        if (DUAL) tmem_ld16(tbase + BN + j0, u);
-        tmem_ld_wait();
+      for (int j0 = 0; j0 < BN; j0 += 32) {
+        // output rows of pairs j0 .. j0+31, one per lane, broadcast by shuffle
+        const int jl = j0 + lane;
+        int my_row = 0;
+        if (jl < tl.nvalid) {
+          const int pos = tl.goff + tl.n0 + jl;
+          my_row = args.out_by_pos ? pos : args.perm[pos];
+        }
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = j0 + jj;
-          if (j < tl.nvalid) {
-            const int pos = tl.goff + tl.n0 + j;
-            const int orow = args.out_by_pos ? pos : args.perm[pos];
-            uint16_t v;
-            if (!slot_ok) v = 0;
-            else if (DUAL) v = swiglu_bf16(__uint_as_float(g[jj]), __uint_as_float(u[jj]));
-            else v = f32_to_bf16(__uint_as_float(g[jj]));
-            args.out[(size_t)orow * args.OUT + ocol] = v;
+        for (int h = 0; h < 2; ++h) {
+          const int jb = j0 + 16 * h;
+          if (jb >= BN) break;
+          uint32_t g[16], u[16];
+          tmem_ld16(tbase + jb, g);
+          if (DUAL) tmem_ld16(tbase + BN + jb, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int orow = __shfl_sync(0xffffffffu, my_row, 16 * h + jj);
+            if (jb + jj < tl.nvalid) {
+              uint16_t v;
+              if (!slot_ok) v = 0;
+              else if (DUAL) v = swiglu_bf16(__uint_as_float(g[jj]), __uint_as_float(u[jj]));
+              else v = f32_to_bf16(__uint_as_float(g[jj]));
+              args.out[(size_t)orow * args.OUT + ocol] = v;
+            }
           }
         }
       }
@@ -637,10 +827,8 @@ static int launch_cfg(const sg_arena* A, const uint16_t* in, int in_rows, const 
          make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w1, K, rows_total, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
     const uint64_t words = (uint64_t)K * BITS / 32;
-    const uint32_t box = BK * BITS / 32;
-    const CUtensorMapSwizzle sw = BITS == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-    ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, box, BM, sw) &&
-         make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, box, BM, sw);
+    ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   }
   ok = ok && make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in, K, (uint64_t)in_rows, BK, 1,
                       CU_TENSOR_MAP_SWIZZLE_128B);
@@ -681,7 +869,9 @@ static int pick_bn(int P, int grid_groups) {
 bool tc_supported(const sg_arena* A, bool dual, int grid_groups) {
   const int K = dual ? A->hidden : A->inter;
   const int OUT = dual ? A->inter : A->hidden;
-  return K % tc::BK == 0 && OUT % tc::BM == 0 && grid_groups <= tc::PLAN_MAX_GROUPS;
+  // packed rows must fill one 128-byte TMA box
+  return K % tc::BK == 0 && OUT % tc::BM == 0 && grid_groups <= tc::PLAN_MAX_GROUPS &&
+         (A->bits == 16 || K * A->bits / 8 >= 128);
 }
 
 int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_by_pos,
