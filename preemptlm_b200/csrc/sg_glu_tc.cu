@@ -52,35 +52,57 @@ __host__ __device__ constexpr int pow2ceil(int v) {
   return p;
 }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 template <int BITS, bool DUAL, int BN>
 struct Cfg {
   static constexpr int NMAT = DUAL ? 2 : 1;
+  // ATM: dequantised A tiles live in tensor memory (tcgen05.st by the
+  // dequantisers, read by tcgen05.mma), sparing shared-memory bandwidth;
+  // used for quantised arenas at decode tile widths
+  static constexpr bool ATM = BITS != 16 && BN <= 64;
   static constexpr int A_MAT = BM * BK * 2;                       // one bf16 operand tile
-  static constexpr int A_BYTES = NMAT * A_MAT;
+  static constexpr int A_BYTES = ATM ? 0 : NMAT * A_MAT;          // shared-memory A stage
   // one packed tile: 128 rows x 128 bytes (KP operand stages of BK weights)
   static constexpr int KP = BITS == 16 ? 1 : 128 * 8 / (BK * BITS);
   static constexpr int P_MAT = BITS == 16 ? 0 : BM * 128;
   static constexpr int P_BYTES = NMAT * P_MAT;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int SB = cmin(8, 32768 / B_BYTES < 2 ? 2 : 32768 / B_BYTES);
-  static constexpr int SA = BITS == 16 ? cmin(8, (RING_BUDGET - SB * B_BYTES) / A_BYTES) : (DUAL ? 3 : 4);
-  static constexpr int SP = BITS == 16 ? 0 : cmin(6, (RING_BUDGET - SA * A_BYTES - SB * B_BYTES) / P_BYTES);
+  static constexpr int B_SUB = BN * BK * 2;  // one operand stage of B (BN rows x BK)
+  // B stages span KBB operand stages and run SB deep, so the row gathers are
+  // issued well ahead of the MMAs (they queue in the SM's TMA unit behind the
+  // weight loads)
+  static constexpr int KBB = BN <= 32 ? 4 : (BN <= 64 ? 2 : 1);
+  static constexpr int B_BYTES = B_SUB * KBB;
   static constexpr int ACC_COLS = NMAT * BN;
   static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;
-  static constexpr int TMEM_COLS = pow2ceil(NACC * ACC_COLS < 32 ? 32 : NACC * ACC_COLS);
+  static constexpr int ACC_TOTAL = NACC * ACC_COLS;
+  static constexpr int A_TCOLS = NMAT * BK / 2;  // TMEM columns of one A stage (two bf16 per column)
+  static constexpr int SB = cmin(6, cmax(2, 49152 / B_BYTES));
+  static constexpr int SA = ATM ? cmin(6, (512 - ACC_TOTAL) / A_TCOLS)
+                                : cmin(BITS == 16 ? 8 : 3, (RING_BUDGET - SB * B_BYTES -
+                                                            (BITS == 16 ? 0 : 2 * NMAT * BM * 128)) / A_BYTES);
+  // packed ring: deep enough to cover HBM latency (~1 us at 96 KB per SM in
+  // flight), shallow enough that the B gathers queued behind it in the SM's
+  // TMA unit still land ahead of the MMAs
+  static constexpr int SP = BITS == 16 ? 0
+                          : cmin(ATM ? (DUAL ? 3 : 4) : 6, (RING_BUDGET - SA * A_BYTES - SB * B_BYTES) / P_BYTES);
+  static constexpr int TMEM_USED = ACC_TOTAL + (ATM ? SA * A_TCOLS : 0);
+  // operand stages per MMA-side wait on a_full: TMA-filled stages may land out
+  // of order and are waited one by one
+  static constexpr int MG = (BITS != 16 && SA >= 4) ? 2 : 1;
+  static constexpr int TMEM_COLS = pow2ceil(TMEM_USED < 32 ? 32 : TMEM_USED);
   // shared memory carve-up (offsets from a 1024-aligned base)
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + SA * A_BYTES;
   static constexpr int OFF_P = OFF_B + SB * B_BYTES;
   static constexpr int OFF_PLAN = OFF_P + SP * P_BYTES;
-  static constexpr int OFF_ROWS = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
-  static constexpr int OFF_BAR = (OFF_ROWS + BN * 4 + 15) & ~15;
+  static constexpr int OFF_BAR = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
   static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC;
   static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
   static_assert(SA >= 2 && (BITS == 16 || SP >= 2), "pipeline too shallow");
+  static_assert(TMEM_COLS <= 512, "tensor memory budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
+  static_assert(B_SUB % 1024 == 0, "B tile must keep 1024-byte alignment");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -131,13 +153,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int r0, int r1, int r2, int r3,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
-      : "memory");
+// 16-byte LSU copy global -> shared (zero fill when src_bytes == 0); completion
+// is tracked per thread and reported to an mbarrier by cp_async_arrive.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// One arrival on `bar` once every cp.async this thread issued so far has landed
+// (the arrival counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Bring [p, p + bytes) into L2 (16-byte aligned address and size).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
@@ -164,6 +194,22 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t 
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+// A from tensor memory (K-major, row m in lane m, two bf16 of consecutive k per column)
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                             uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -187,16 +233,22 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 //   2^15 (one PRMT / LOP3; the field must end below bit 23, the exponent);
 //   fma(v, s_p, -2^15 * s_p) = q * scale exactly (s_p = scale * 2^(8 - p), a
 //   power-of-two rescale); then one add of bias.
+// Fused form: when c_p = bias - 2^15 * s_p is exact in fp32 (checked per group
+// with an error-free two-sum), fma(v, s_p, c_p) rounds the exact scale*q + bias
+// once -- the same value as fp32(scale * q) + bias, since scale * q (8 + 8
+// significant bits) is exact -- in one instruction instead of two.
 // Two weights at a time with packed fma.rn.f32x2 / add.rn.f32x2.
 __device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
   return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
 }
+template <bool FUSED>
 __device__ __forceinline__ uint32_t dq_pair(uint32_t v_lo, uint32_t v_hi, unsigned long long s2,
                                             unsigned long long c2, unsigned long long b2) {
   const unsigned long long v = (static_cast<unsigned long long>(v_hi) << 32) | v_lo;
   unsigned long long t, w;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(t) : "l"(v), "l"(s2), "l"(c2));
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(w) : "l"(t), "l"(b2));
+  if (FUSED) w = t;
+  else asm("add.rn.f32x2 %0, %1, %2;" : "=l"(w) : "l"(t), "l"(b2));
   __nv_bfloat162 r = __floats2bfloat162_rn(__uint_as_float(static_cast<uint32_t>(w)),
                                            __uint_as_float(static_cast<uint32_t>(w >> 32)));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -204,29 +256,53 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t v_lo, uint32_t v_hi, unsign
 
 struct GroupScale {  // one (scale, bias) group in the forms the converters use
   // q8: p1 = (s, s).  q4: p1 = (s8, s12), p2 = (s16, s8), p3 = (s12, s16) with
-  // s_p = scale * 2^(8 - p); c* = -2^15 * s*; b = (bias, bias)
+  // s_p = scale * 2^(8 - p); c* = k - 2^15 * s* with k = bias when the warp
+  // runs fused, else 0; b = (bias, bias)
   unsigned long long p1, c1, p2, c2, p3, c3, b;
+  bool fused;  // warp-uniform
 };
+// b - x, and whether that difference is exact in fp32 (Knuth's two-sum error is zero)
+__device__ __forceinline__ float sub_exact(float b, float x, bool& exact) {
+  const float d = __fsub_rn(b, x);
+  const float bv = __fsub_rn(d, b);
+  const float err = __fadd_rn(__fsub_rn(b, __fsub_rn(d, bv)), __fsub_rn(-x, bv));
+  exact = exact && err == 0.0f;
+  return d;
+}
 template <int BITS>
 __device__ __forceinline__ GroupScale make_scale(float s, float b) {
   GroupScale g;
   g.b = f2pack(b, b);
+  bool ex = true;
   if (BITS == 8) {
+    const float x = 32768.0f * s;
+    const float cf = sub_exact(b, x, ex);
+    g.fused = __all_sync(0xffffffffu, ex);
     g.p1 = f2pack(s, s);
-    g.c1 = f2pack(-32768.0f * s, -32768.0f * s);
+    g.c1 = g.fused ? f2pack(cf, cf) : f2pack(-x, -x);
   } else {
     const float s8 = s, s12 = s * 0.0625f, s16 = s * 0.00390625f;
+    const float x8 = 32768.0f * s8, x12 = 32768.0f * s12, x16 = 32768.0f * s16;
+    const float f8 = sub_exact(b, x8, ex), f12 = sub_exact(b, x12, ex), f16 = sub_exact(b, x16, ex);
+    g.fused = __all_sync(0xffffffffu, ex);
     g.p1 = f2pack(s8, s12);
-    g.c1 = f2pack(-32768.0f * s8, -32768.0f * s12);
     g.p2 = f2pack(s16, s8);
-    g.c2 = f2pack(-32768.0f * s16, -32768.0f * s8);
     g.p3 = f2pack(s12, s16);
-    g.c3 = f2pack(-32768.0f * s12, -32768.0f * s16);
+    if (g.fused) {
+      g.c1 = f2pack(f8, f12);
+      g.c2 = f2pack(f16, f8);
+      g.c3 = f2pack(f12, f16);
+    } else {
+      g.c1 = f2pack(-x8, -x12);
+      g.c2 = f2pack(-x16, -x8);
+      g.c3 = f2pack(-x12, -x16);
+    }
   }
   return g;
 }
 
 // q8: 16-byte packed chunk (16 weights) -> two 16-byte bf16 chunks
+template <bool FUSED>
 __device__ __forceinline__ void dq8_chunk(uint4 v, const GroupScale& g, uint4& o0, uint4& o1) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t o[8];
@@ -236,8 +312,8 @@ __device__ __forceinline__ void dq8_chunk(uint4 v, const GroupScale& g, uint4& o
     const uint32_t a1 = __byte_perm(w[i], 0x47000000u, 0x7414);
     const uint32_t a2 = __byte_perm(w[i], 0x47000000u, 0x7424);
     const uint32_t a3 = __byte_perm(w[i], 0x47000000u, 0x7434);
-    o[2 * i] = dq_pair(a0, a1, g.p1, g.c1, g.b);
-    o[2 * i + 1] = dq_pair(a2, a3, g.p1, g.c1, g.b);
+    o[2 * i] = dq_pair<FUSED>(a0, a1, g.p1, g.c1, g.b);
+    o[2 * i + 1] = dq_pair<FUSED>(a2, a3, g.p1, g.c1, g.b);
   }
   o0 = make_uint4(o[0], o[1], o[2], o[3]);
   o1 = make_uint4(o[4], o[5], o[6], o[7]);
@@ -246,6 +322,7 @@ __device__ __forceinline__ void dq8_chunk(uint4 v, const GroupScale& g, uint4& o
 // q4: one packed word (8 weights, nibble m at bits 4m) -> one 16-byte bf16 chunk.
 // A nibble may sit at mantissa bit 8, 12 or 16 only (bits 20-23 would reach
 // the exponent), so three shifted copies of the word feed the eight weights.
+template <bool FUSED>
 __device__ __forceinline__ uint4 dq4_word(uint32_t w, const GroupScale& g) {
   const uint32_t a = w << 8, b = w >> 4, c = w >> 16;
   const uint32_t M = 0x47000000u;
@@ -253,37 +330,81 @@ __device__ __forceinline__ uint4 dq4_word(uint32_t w, const GroupScale& g) {
   const uint32_t v2 = (a & 0x000F0000u) | M, v3 = (b & 0x00000F00u) | M;  // nibbles 2,3 at bits 16,8
   const uint32_t v4 = (b & 0x0000F000u) | M, v5 = (b & 0x000F0000u) | M;  // nibbles 4,5 at bits 12,16
   const uint32_t v6 = (c & 0x00000F00u) | M, v7 = (c & 0x0000F000u) | M;  // nibbles 6,7 at bits 8,12
-  return make_uint4(dq_pair(v0, v1, g.p1, g.c1, g.b), dq_pair(v2, v3, g.p2, g.c2, g.b),
-                    dq_pair(v4, v5, g.p3, g.c3, g.b), dq_pair(v6, v7, g.p1, g.c1, g.b));
+  return make_uint4(dq_pair<FUSED>(v0, v1, g.p1, g.c1, g.b), dq_pair<FUSED>(v2, v3, g.p2, g.c2, g.b),
+                    dq_pair<FUSED>(v4, v5, g.p3, g.c3, g.b), dq_pair<FUSED>(v6, v7, g.p1, g.c1, g.b));
 }
 
-// Dequantise output chunks [oc0, oc0 + NOC) of row r (8 weights per chunk)
-// of operand sub-stage j (BK weights) from a packed stage tile (SW128: 128-byte
-// rows, 16-byte chunk c at c ^ (r & 7)) into the SW128 bf16 operand tile.
-template <int BITS, int NOC>
-__device__ __forceinline__ void dequant_part(const uint8_t* p_tile, uint8_t* a_tile, int r, int j, int oc0,
-                                             const GroupScale& g) {
-  uint8_t* arow = a_tile + r * 128;
+// A thread's share of one packed stage, held in registers: q8 DUAL 8 chunks
+// (its full 128-byte row), otherwise 4 chunks (its half of every sub-stage).
+// Packed tile layout: SW128, 128-byte rows, 16-byte chunk c of row r at c ^ (r & 7).
+template <int BITS, bool FULL>
+__device__ __forceinline__ void load_packed(const uint8_t* p_tile, int r, int part, uint4 (&v)[8]) {
   const uint8_t* prow = p_tile + r * 128;
-  if (BITS == 8) {
-    // sub-stage j = bytes [64 j, 64 j + 64) = packed chunks 4j .. 4j+3 (16 weights each)
 #pragma unroll
-    for (int c = oc0 / 2; c < (oc0 + NOC) / 2; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(prow + (((4 * j + c) ^ (r & 7)) << 4));
+  for (int i = 0; i < (FULL ? 8 : 4); ++i) {
+    // full row: chunk i.  Half rows: q8 sub-stage j = i / 2 uses chunks 4j + 2 part + (i & 1);
+    // q4 sub-stage j = i uses chunk 2j + part.
+    const int c = FULL ? i : (BITS == 8 ? 4 * (i >> 1) + 2 * part + (i & 1) : 2 * i + part);
+    v[i] = *reinterpret_cast<const uint4*>(prow + ((c ^ (r & 7)) << 4));
+  }
+}
+
+// Operand sub-stage j (BK weights of row r) from the register share into
+// registers: out[4 k .. 4 k + 3] = output chunk k of this thread (8 bf16 each;
+// FULL: the row's 8 chunks, half rows: chunks 4 part .. 4 part + 3).
+template <int BITS, bool FULL, bool FUSED>
+__device__ __forceinline__ void dequant_sub_regs(const uint4 (&v)[8], int j, const GroupScale& g,
+                                                 uint32_t (&out)[32]) {
+  if (BITS == 8) {
+#pragma unroll
+    for (int q = 0; q < (FULL ? 4 : 2); ++q) {
       uint4 o0, o1;
-      dq8_chunk(v, g, o0, o1);
-      *reinterpret_cast<uint4*>(arow + (((2 * c) ^ (r & 7)) << 4)) = o0;
-      *reinterpret_cast<uint4*>(arow + (((2 * c + 1) ^ (r & 7)) << 4)) = o1;
+      dq8_chunk<FUSED>(v[FULL ? 4 * j + q : 2 * j + q], g, o0, o1);
+      out[8 * q + 0] = o0.x; out[8 * q + 1] = o0.y; out[8 * q + 2] = o0.z; out[8 * q + 3] = o0.w;
+      out[8 * q + 4] = o1.x; out[8 * q + 5] = o1.y; out[8 * q + 6] = o1.z; out[8 * q + 7] = o1.w;
     }
   } else {
-    // sub-stage j = bytes [32 j, 32 j + 32) = packed chunks 2j, 2j+1 (32 weights each)
 #pragma unroll
-    for (int c = oc0 / 4; c < (oc0 + NOC) / 4; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(prow + (((2 * j + c) ^ (r & 7)) << 4));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int q = 0; q < (FULL ? 2 : 1); ++q) {
+      const uint4 pv = FULL ? v[2 * j + q] : v[j];
+      const uint32_t w[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint4 o = dq4_word<FUSED>(w[h], g);
+        out[16 * q + 4 * h + 0] = o.x; out[16 * q + 4 * h + 1] = o.y;
+        out[16 * q + 4 * h + 2] = o.z; out[16 * q + 4 * h + 3] = o.w;
+      }
+    }
+  }
+}
+
+// Operand sub-stage j (BK weights of row r) from the register share into the
+// SW128 bf16 tile.  FULL: all 8 output chunks; half rows: chunks 4 part .. +3.
+template <int BITS, bool FULL, bool FUSED>
+__device__ __forceinline__ void dequant_sub(const uint4 (&v)[8], int j, uint8_t* a_tile, int r, int part,
+                                            const GroupScale& g) {
+  uint8_t* arow = a_tile + r * 128;
+  if (BITS == 8) {
+    // q8: a packed chunk = 16 weights = 2 output chunks; sub-stage j = packed chunks 4j .. 4j+3
+#pragma unroll
+    for (int q = 0; q < (FULL ? 4 : 2); ++q) {
+      const int pc = FULL ? 4 * j + q : 2 * j + q;   // index into v
+      const int oc = FULL ? 2 * q : 4 * part + 2 * q;  // first output chunk
+      uint4 o0, o1;
+      dq8_chunk<FUSED>(v[pc], g, o0, o1);
+      *reinterpret_cast<uint4*>(arow + ((oc ^ (r & 7)) << 4)) = o0;
+      *reinterpret_cast<uint4*>(arow + (((oc + 1) ^ (r & 7)) << 4)) = o1;
+    }
+  } else {
+    // q4: a packed chunk = 32 weights = 4 output chunks; sub-stage j = packed chunks 2j, 2j+1
+#pragma unroll
+    for (int q = 0; q < (FULL ? 2 : 1); ++q) {
+      const uint4 pv = FULL ? v[2 * j + q] : v[j];
+      const uint32_t w[4] = {pv.x, pv.y, pv.z, pv.w};
+      const int oc0 = FULL ? 4 * q : 4 * part;
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        *reinterpret_cast<uint4*>(arow + (((4 * c + h) ^ (r & 7)) << 4)) = dq4_word(w[h], g);
+        *reinterpret_cast<uint4*>(arow + (((oc0 + h) ^ (r & 7)) << 4)) = dq4_word<FUSED>(w[h], g);
     }
   }
 }
@@ -291,6 +412,8 @@ __device__ __forceinline__ void dequant_part(const uint8_t* p_tile, uint8_t* a_t
 // ------------------------------------------------------------------ arguments
 struct Args {
   int num_slots, K, OUT;
+  const uint8_t* in;  // B rows: [in_rows, K] bf16
+  int in_rows;
   const uint16_t* s0;
   const uint16_t* b0;
   const uint16_t* s1;
@@ -366,13 +489,13 @@ struct ScaleVec<1> {
 template <int BITS, bool DUAL, int BN, int V>
 __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, int U, int NT, int total,
                                              uint8_t* sA, const uint8_t* sP, uint64_t* a_full, uint64_t* a_empty,
-                                             uint64_t* p_full, uint64_t* p_empty, Ctl ctl) {
+                                             uint64_t* p_full, uint64_t* p_empty, Ctl ctl, uint32_t tmem_a) {
   using C = Cfg<BITS, DUAL, BN>;
-  const int d = (threadIdx.x >> 5) * 32 - DQ_WARP0 * 32 + (threadIdx.x & 31);  // 0..255
-  const int r = d & 127;
-  const int part = d >> 7;               // DUAL: matrix (gate / up); single: half row
+  // row r = 32 (warp % 4) + lane: the TMEM lane quadrant this warp may write
+  const int warp = threadIdx.x >> 5;
+  const int r = 32 * (warp & 3) + (threadIdx.x & 31);
+  const int part = (warp - DQ_WARP0) >> 2;  // DUAL: matrix (gate / up); single: half row
   const int mat = DUAL ? part : 0;
-  const int oc0 = DUAL ? 0 : part * 4;   // first output chunk of this thread
   const int K = args.K, NKB = K / BK, groups = K / 64, nvec = groups / V;
   const uint16_t* sbase = mat ? args.s1 : args.s0;
   const uint16_t* bbase = mat ? args.b1 : args.b0;
@@ -411,41 +534,73 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
     bool sok;
     const uint16_t *tsp, *tbp;
     row_ptrs(t, tsp, tbp, sok);
-    for (int kb = 0; kb < NKB; ++kb) {
-      const int j = kb % V;
-      if (j == 0 && kb > 0) {  // next vector of this tile becomes current
-        cur = nxt;
-        int vn = kb / V + 1;
-        int tn = t;
-        if (vn >= nvec) {
-          vn = 0;
-          tn = t + gridDim.x;
-        }
-        if (tn < total) {
-          const uint16_t *ns, *nb;
-          bool nsok;
-          row_ptrs(tn, ns, nb, nsok);
-          nxt.load(ns, nb, vn);
-        }
-      }
-      const GroupScale g = make_scale<BITS>(sok ? cur.sc(j) : 0.f, sok ? cur.bi(j) : 0.f);
-      const int jp = kb % C::KP;  // operand sub-stage within the packed stage
-      ok = (jp != 0 || wait_bar(&p_full[sp_i], pp, ctl)) && wait_bar(&a_empty[sa], pa ^ 1, ctl);
-      ok = __all_sync(0xffffffffu, ok);  // keep the warp converged for __syncwarp
+    uint4 pk[8];
+    for (int kb0 = 0; kb0 < NKB && ok; kb0 += C::KP) {
+      // take this thread's share of the packed stage into registers and
+      // release the slot at once, so the producer can refill it
+      ok = wait_bar(&p_full[sp_i], pp, ctl);
+      ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const uint8_t* ptile = sP + sp_i * C::P_BYTES + mat * C::P_MAT;
-      uint8_t* atile = sA + sa * C::A_BYTES + mat * C::A_MAT;
-      if (DUAL) dequant_part<BITS, 8>(ptile, atile, r, jp, 0, g);
-      else dequant_part<BITS, 4>(ptile, atile, r, jp, oc0, g);
-      fence_async_smem();
+      load_packed<BITS, DUAL>(sP + sp_i * C::P_BYTES + mat * C::P_MAT, r, part, pk);
       __syncwarp();
-      const bool last_sub = jp == C::KP - 1 || kb == NKB - 1;
-      if ((threadIdx.x & 31) == 0) {
-        mbar_arrive(&a_full[sa]);
-        if (last_sub) mbar_arrive(&p_empty[sp_i]);
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&p_empty[sp_i]);
+      if (++sp_i == C::SP) { sp_i = 0; pp ^= 1; }
+      const int nsub = min(C::KP, NKB - kb0);
+#pragma unroll
+      for (int jp = 0; jp < C::KP; ++jp) {  // operand sub-stages (compile-time index into pk)
+        const int kb = kb0 + jp;
+        if (kb >= NKB) break;
+        if (jp % C::MG == 0) {
+          // the MMAs free operand slots in order: waiting for the last slot of
+          // the next MG sub-stages covers all of them
+          int sl = sa + min(C::MG, nsub - jp) - 1;
+          uint32_t ph = pa;
+          if (sl >= C::SA) { sl -= C::SA; ph ^= 1; }
+          ok = wait_bar(&a_empty[sl], ph ^ 1, ctl);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+        }
+        const int j = kb % V;
+        if (j == 0 && kb > 0) {  // next vector of this tile becomes current
+          cur = nxt;
+          int vn = kb / V + 1;
+          int tn = t;
+          if (vn >= nvec) {
+            vn = 0;
+            tn = t + gridDim.x;
+          }
+          if (tn < total) {
+            const uint16_t *ns, *nb;
+            bool nsok;
+            row_ptrs(tn, ns, nb, nsok);
+            nxt.load(ns, nb, vn);
+          }
+        }
+        const GroupScale g = make_scale<BITS>(sok ? cur.sc(j) : 0.f, sok ? cur.bi(j) : 0.f);
+        if (C::ATM) {
+          uint32_t out[32];
+          if (g.fused) dequant_sub_regs<BITS, DUAL, true>(pk, jp, g, out);
+          else dequant_sub_regs<BITS, DUAL, false>(pk, jp, g, out);
+          tc_fence_after();
+          const uint32_t ta = tmem_a + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
+                              C::ACC_TOTAL + (sa * C::NMAT + mat) * (BK / 2) + (DUAL ? 0 : 16 * part);
+          const uint32_t (&lo)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[0]);
+          tmem_st16(ta, lo);
+          if (DUAL) {
+            const uint32_t (&hi)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[16]);
+            tmem_st16(ta + 16, hi);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+        } else {
+          if (g.fused) dequant_sub<BITS, DUAL, true>(pk, jp, sA + sa * C::A_BYTES + mat * C::A_MAT, r, part, g);
+          else dequant_sub<BITS, DUAL, false>(pk, jp, sA + sa * C::A_BYTES + mat * C::A_MAT, r, part, g);
+          fence_async_smem();
+        }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&a_full[sa]);
+        if (++sa == C::SA) { sa = 0; pa ^= 1; }
       }
-      if (++sa == C::SA) { sa = 0; pa ^= 1; }
-      if (last_sub && ++sp_i == C::SP) { sp_i = 0; pp ^= 1; }
     }
     // the first vector of the next tile is already in nxt
     if (nvec > 1 || V == 1) {
@@ -480,7 +635,7 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
 template <int BITS, bool DUAL, int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-              const __grid_constant__ CUtensorMap tmB, const Args args) {
+              const Args args) {
   using C = Cfg<BITS, DUAL, BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -488,7 +643,6 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sP = smem + C::OFF_P;
   int* plan = reinterpret_cast<int*>(smem + C::OFF_PLAN);
-  int* rows = reinterpret_cast<int*>(smem + C::OFF_ROWS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* a_full = bars;                   // [SA] A stage ready (TMA tx or 8 dequant warps)
   uint64_t* a_empty = a_full + C::SA;        // [SA] A stage consumed (MMA commit)
@@ -513,7 +667,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SB; ++i) {
-      mbar_init(&b_full[i], 1);
+      mbar_init(&b_full[i], 32);  // one cp.async arrival per producer lane
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < C::SP; ++i) {
@@ -571,8 +725,26 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       constexpr int RING = BITS == 16 ? C::SA : C::SP;
       uint64_t* full = BITS == 16 ? a_full : p_full;
       uint64_t* empty = BITS == 16 ? a_empty : p_empty;
+      // scale/bias rows of a tile (contiguous, 128 rows x K/64 groups) go to
+      // L2 one tile ahead, so the dequantisers' loads of them hit L2
+      auto prefetch_scales = [&](int tt) {
+        if (BITS == 16 || tt >= total) return;
+        const Tile tn = tile_of<BN>(tt, plan, U, NT, args);
+        if (tn.slot < 0 || tn.slot >= args.num_slots) return;
+        const int groups = K / 64;
+        const size_t off = ((size_t)tn.slot * args.OUT + (size_t)tn.m * BM) * groups;
+        const uint32_t bytes = BM * groups * 2;
+        prefetch_l2(args.s0 + off, bytes);
+        prefetch_l2(args.b0 + off, bytes);
+        if (DUAL) {
+          prefetch_l2(args.s1 + off, bytes);
+          prefetch_l2(args.b1 + off, bytes);
+        }
+      };
+      prefetch_scales(blockIdx.x);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+        prefetch_scales(t + gridDim.x);
         const int row0 = tl.slot * args.OUT + tl.m * BM;
         const int nstage = BITS == 16 ? NKB : (NKB + C::KP - 1) / C::KP;
         for (int kb = 0; kb < nstage; ++kb) {
@@ -606,66 +778,50 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       }
     }
   } else if (warp == 2) {
-    // ---------------------------------------------------------------- B gather producer
-    // rows[] holds the current tile's B rows; every lane loads the next tile's
-    // row for its column before lane 0 issues the current tile, so the perm
-    // lookups overlap the issue loop.
+    // ---------------------------------------------------------------- B row producer
+    // The tile's pair rows, 16-byte LSU copies straight into the SW128 operand
+    // layout (row j of a stage at 128 j, chunk c at c ^ (j & 7)); lane l copies
+    // chunk l % 8 of rows l / 8 + 4 i.  Each lane reports its copies to the
+    // stage's full barrier (32 arrivals); rows past the tile's pairs are zero.
+    constexpr int RPL = BN / 4;  // rows per lane
+    const int c = lane & 7, r0 = lane >> 3;
+    const size_t row_bytes = static_cast<size_t>(K) * 2;
     int sb = 0;
     uint32_t pb = 0;
     bool ok = true;
-    int issued = 0;
-    auto row_of = [&](const Tile& tl, int j) {
-      const int pos = tl.goff + tl.n0 + (j < tl.nvalid ? j : 0);
-      return args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
-    };
-    constexpr int RPL = (BN + 31) / 32;  // rows per lane
-    int nxt[RPL];
-    int t = blockIdx.x;
-    if (t < total) {
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+      int row[RPL];  // source row of each of this lane's tile rows, -1: zero fill
 #pragma unroll
-      for (int i = 0; i < RPL; ++i)
-        if (lane + 32 * i < BN) nxt[i] = row_of(tl, lane + 32 * i);
-    }
-    for (; t < total && ok; t += gridDim.x) {
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < RPL; ++i)
-        if (lane + 32 * i < BN) rows[lane + 32 * i] = nxt[i];
-      __syncwarp();
-      const int tn = t + gridDim.x;
-      if (tn < total) {  // loads in flight while lane 0 issues tile t
-        const Tile tl = tile_of<BN>(tn, plan, U, NT, args);
-#pragma unroll
-        for (int i = 0; i < RPL; ++i)
-          if (lane + 32 * i < BN) nxt[i] = row_of(tl, lane + 32 * i);
-      }
-      if (lane == 0) {
-        for (int kb = 0; kb < NKB; ++kb) {
-          ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
-          if (!ok) break;
-          mbar_expect_tx(&b_full[sb], C::B_BYTES);
-          uint8_t* dst = sB + sb * C::B_BYTES;
-#pragma unroll 1
-          for (int g = 0; g < BN / 4; ++g)
-            tma_gather4(dst + g * 512, &tmB, kb * BK, rows[4 * g], rows[4 * g + 1], rows[4 * g + 2],
-                        rows[4 * g + 3], &b_full[sb]);
-          ++issued;
-          if (++sb == C::SB) { sb = 0; pb ^= 1; }
+      for (int i = 0; i < RPL; ++i) {
+        const int j = r0 + 4 * i;
+        int rw = -1;
+        if (j < tl.nvalid) {
+          const int pos = tl.goff + tl.n0 + j;
+          rw = args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
         }
+        row[i] = (rw >= 0 && rw < args.in_rows) ? rw : -1;
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    }
-    if (!ok && lane == 0) {
-      for (int i = 0; i < min(issued, C::SB); ++i) {
-        int s = sb - 1 - i;
-        uint32_t p = pb;
-        if (s < 0) { s += C::SB; p ^= 1; }
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&b_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
+      for (int kb0 = 0; kb0 < NKB; kb0 += C::KBB) {
+        ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const int nsub = min(C::KBB, NKB - kb0);
+        for (int j = 0; j < nsub; ++j) {
+          uint8_t* dst = sB + sb * C::B_BYTES + j * C::B_SUB;
+          const uint8_t* col = args.in + (kb0 + j) * (BK * 2) + c * 16;
+#pragma unroll
+          for (int i = 0; i < RPL; ++i) {
+            const int rt = r0 + 4 * i;  // row within the tile
+            const bool v = row[i] >= 0;
+            cp_async16(dst + rt * 128 + ((c ^ (rt & 7)) << 4), v ? col + row[i] * row_bytes : args.in, v ? 16u : 0u);
+          }
         }
+        cp_async_arrive(&b_full[sb]);
+        if (++sb == C::SB) { sb = 0; pb ^= 1; }
       }
     }
+    cp_async_wait_all();  // no copy of this warp outlives the kernel
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -682,22 +838,45 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         tc_fence_after();
         const uint32_t d0 = tmem + ab * C::ACC_COLS;
         for (int kb = 0; kb < NKB; ++kb) {
-          ok = wait_bar(&a_full[sa], pa, ctl) && wait_bar(&b_full[sb], pb, ctl);
+          const int jb = kb % C::KBB;  // operand stage within the B stage
+          if (jb == 0) ok = wait_bar(&b_full[sb], pb, ctl);
+          if (kb % C::MG == 0 && ok) {
+            // dequantised stages fill in order (every dequantiser arrives on
+            // them in turn), so the last stage of a group being full implies
+            // the rest are: one wait per MG stages
+            int sl = sa + min(C::MG, NKB - kb) - 1;
+            uint32_t ph = pa;
+            if (sl >= C::SA) { sl -= C::SA; ph ^= 1; }
+            ok = wait_bar(&a_full[sl], ph, ctl);
+          }
           if (!ok) break;
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + sa * C::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + sb * C::B_BYTES);
+          const uint32_t b_base = smem_u32(sB + sb * C::B_BYTES + jb * C::B_SUB);
+          if (C::ATM) {
+            const uint32_t a_t = tmem + C::ACC_TOTAL + sa * C::NMAT * (BK / 2);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t bd = desc_sw128(b_base + kk * 32);
-            const uint32_t acc = (kb | kk) != 0;
-            umma_bf16(d0, desc_sw128(a_base + kk * 32), bd, idesc, acc);
-            if (DUAL) umma_bf16(d0 + BN, desc_sw128(a_base + C::A_MAT + kk * 32), bd, idesc, acc);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t bd = desc_sw128(b_base + kk * 32);
+              const uint32_t acc = (kb | kk) != 0;
+              umma_bf16_ts(d0, a_t + kk * 8, bd, idesc, acc);
+              if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2 + kk * 8, bd, idesc, acc);
+            }
+          } else {
+            const uint32_t a_base = smem_u32(sA + sa * C::A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t bd = desc_sw128(b_base + kk * 32);
+              const uint32_t acc = (kb | kk) != 0;
+              umma_bf16(d0, desc_sw128(a_base + kk * 32), bd, idesc, acc);
+              if (DUAL) umma_bf16(d0 + BN, desc_sw128(a_base + C::A_MAT + kk * 32), bd, idesc, acc);
+            }
           }
           umma_commit(&a_empty[sa]);
-          umma_commit(&b_empty[sb]);
           if (++sa == C::SA) { sa = 0; pa ^= 1; }
-          if (++sb == C::SB) { sb = 0; pb ^= 1; }
+          if (jb == C::KBB - 1 || kb == NKB - 1) {
+            umma_commit(&b_empty[sb]);
+            if (++sb == C::SB) { sb = 0; pb ^= 1; }
+          }
         }
         if (ok) umma_commit(&acc_full[ab]);
       }
@@ -706,9 +885,11 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     // ---------------------------------------------------------------- dequantisers
     if (BITS != 16) {
       if ((K / 64) % 4 == 0)
-        dequant_role<BITS, DUAL, BN, 4>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl);
+        dequant_role<BITS, DUAL, BN, 4>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl,
+                                        tmem);
       else
-        dequant_role<BITS, DUAL, BN, 1>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl);
+        dequant_role<BITS, DUAL, BN, 1>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl,
+                                        tmem);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 11-14)
@@ -814,11 +995,11 @@ static int num_sms() {
 }
 
 template <int BITS, bool DUAL, int BN>
-static int launch_cfg(const sg_arena* A, const uint16_t* in, int in_rows, const Args& args, cudaStream_t s) {
+static int launch_cfg(const sg_arena* A, const Args& args, cudaStream_t s) {
   using C = Cfg<BITS, DUAL, BN>;
   const int K = args.K, OUT = args.OUT;
   const uint64_t rows_total = (uint64_t)A->num_slots * OUT;
-  CUtensorMap m0, m1, mb;
+  CUtensorMap m0, m1;
   const void* w0 = DUAL ? A->gate_w : A->down_w;
   const void* w1 = DUAL ? A->up_w : A->down_w;
   bool ok;
@@ -830,28 +1011,28 @@ static int launch_cfg(const sg_arena* A, const uint16_t* in, int in_rows, const 
     ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
          make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   }
-  ok = ok && make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, in, K, (uint64_t)in_rows, BK, 1,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return SG_ERR_CUDA;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static bool attr_done[64] = {};  // per device
+  int dev = 0;
+  SG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
+  if (!attr_done[dev]) {
     SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM));
-    attr_done = true;
+    attr_done[dev] = true;
   }
-  glu_tc_kernel<BITS, DUAL, BN><<<num_sms(), NUM_THREADS, C::SMEM, s>>>(m0, m1, mb, args);
+  glu_tc_kernel<BITS, DUAL, BN><<<num_sms(), NUM_THREADS, C::SMEM, s>>>(m0, m1, args);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
 template <int BITS, bool DUAL>
-static int launch_bits(const sg_arena* A, const uint16_t* in, int in_rows, int bn, const Args& args,
-                       cudaStream_t s) {
+static int launch_bits(const sg_arena* A, int bn, const Args& args, cudaStream_t s) {
   switch (bn) {
-    case 16: return launch_cfg<BITS, DUAL, 16>(A, in, in_rows, args, s);
-    case 32: return launch_cfg<BITS, DUAL, 32>(A, in, in_rows, args, s);
-    case 64: return launch_cfg<BITS, DUAL, 64>(A, in, in_rows, args, s);
-    default: return launch_cfg<BITS, DUAL, 128>(A, in, in_rows, args, s);
+    case 16: return launch_cfg<BITS, DUAL, 16>(A, args, s);
+    case 32: return launch_cfg<BITS, DUAL, 32>(A, args, s);
+    case 64: return launch_cfg<BITS, DUAL, 64>(A, args, s);
+    default: return launch_cfg<BITS, DUAL, 128>(A, args, s);
   }
 }
 
@@ -885,6 +1066,8 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   a.b0 = static_cast<const uint16_t*>(dual ? A->gate_b : A->down_b);
   a.s1 = static_cast<const uint16_t*>(dual ? A->up_s : A->down_s);
   a.b1 = static_cast<const uint16_t*>(dual ? A->up_b : A->down_b);
+  a.in = reinterpret_cast<const uint8_t*>(in);
+  a.in_rows = in_rows;
   a.counts = counts;
   a.slot_ids = slot_ids;
   a.group_off = group_off;
@@ -896,9 +1079,9 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   a.out = out;
   const int bn = pick_bn(P, grid_groups);
   switch (A->bits) {
-    case 16: return dual ? tc::launch_bits<16, true>(A, in, in_rows, bn, a, s) : tc::launch_bits<16, false>(A, in, in_rows, bn, a, s);
-    case 8: return dual ? tc::launch_bits<8, true>(A, in, in_rows, bn, a, s) : tc::launch_bits<8, false>(A, in, in_rows, bn, a, s);
-    default: return dual ? tc::launch_bits<4, true>(A, in, in_rows, bn, a, s) : tc::launch_bits<4, false>(A, in, in_rows, bn, a, s);
+    case 16: return dual ? tc::launch_bits<16, true>(A, bn, a, s) : tc::launch_bits<16, false>(A, bn, a, s);
+    case 8: return dual ? tc::launch_bits<8, true>(A, bn, a, s) : tc::launch_bits<8, false>(A, bn, a, s);
+    default: return dual ? tc::launch_bits<4, true>(A, bn, a, s) : tc::launch_bits<4, false>(A, bn, a, s);
   }
 }
 

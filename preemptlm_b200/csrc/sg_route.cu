@@ -39,13 +39,22 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
     for (int b = 0; b < RT_TOK; ++b) acc[a][b] = 0.0f;
 
   const int iters = H >> 8;
+  // router rows: this lane's 16-byte chunk of iteration i + 1 is in flight
+  // while iteration i computes
+  uint4 wn[RT_EXP];
+#pragma unroll
+  for (int a = 0; a < RT_EXP; ++a) {
+    const int e = e0 + a;
+    wn[a] = (e < E) ? ldg_nc_v4(w + (size_t)e * H + (size_t)lane * 8) : make_uint4(0, 0, 0, 0);
+  }
   for (int i = 0; i < iters; ++i) {
     const int cc = i * 32 + lane;  // this lane's 16-byte chunk of the row
     uint4 wv[RT_EXP];
 #pragma unroll
     for (int a = 0; a < RT_EXP; ++a) {
-      int e = e0 + a;
-      wv[a] = (e < E) ? ldg_nc_v4(w + (size_t)e * H + (size_t)cc * 8) : make_uint4(0, 0, 0, 0);
+      wv[a] = wn[a];
+      const int e = e0 + a;
+      if (i + 1 < iters && e < E) wn[a] = ldg_nc_v4(w + (size_t)e * H + (size_t)(cc + 32) * 8);
     }
 #pragma unroll
     for (int b = 0; b < RT_TOK; ++b) {
@@ -72,6 +81,35 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
       if (lane == ((a * RT_TOK + b) & 31) && e < E && t < T) logits[(size_t)t * E + e] = f32_to_bf16(s);
     }
   }
+}
+
+// Few experts (the shared expert's one-row gate): one warp per (token, expert)
+// with the same per-lane order and fold as the tiled kernel above, so the
+// logits are bit-identical to it.
+__global__ void __launch_bounds__(256)
+router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                           uint16_t* __restrict__ logits, int T, int H, int E) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= T * E) return;
+  const int t = gw / E, e = gw - t * E;
+  const uint16_t* xr = x + (size_t)t * H;
+  const uint16_t* wr = w + (size_t)e * H;
+  float acc = 0.0f;
+  for (int i = 0; i < (H >> 8); ++i) {
+    const int cc = i * 32 + lane;
+    const uint4 xv = ldg_nc_v4(xr + (size_t)cc * 8);
+    const uint4 wv = ldg_nc_v4(wr + (size_t)cc * 8);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc = __fmaf_rn(lo_bf16(xw[q]), lo_bf16(ww[q]), acc);
+      acc = __fmaf_rn(hi_bf16(xw[q]), hi_bf16(ww[q]), acc);
+    }
+  }
+  const float s = warp_fold_sum(acc);
+  if (lane == 0) logits[(size_t)t * E + e] = f32_to_bf16(s);
 }
 
 // ============================================================== routing
@@ -240,6 +278,14 @@ extern "C" int sg_router_logits(const uint16_t* x, const uint16_t* w, uint16_t* 
   if (H % 256 != 0) return SG_ERR_SHAPE;
   if (T == 0) return SG_OK;
   if (!x || !w || !logits) return SG_ERR_INVALID_ARG;
+  if (E < sg::RT_WARPS * sg::RT_EXP) {
+    const long long warps = (long long)T * E;
+    if (warps > (1LL << 30)) return SG_ERR_SHAPE;
+    sg::router_logits_small_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, (cudaStream_t)stream>>>(x, w, logits, T, H,
+                                                                                                    E);
+    SG_LAUNCH_CHECK();
+    return SG_OK;
+  }
   const size_t smem = (size_t)sg::RT_TOK * H * 2;
   if (smem > 200 * 1024) return SG_ERR_SHAPE;
   static bool attr_done = false;

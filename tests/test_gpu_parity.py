@@ -26,7 +26,8 @@ def _bf16(shape, seed, std=1.0):
 
 # ----------------------------------------------------------------------------- router / routing
 
-@pytest.mark.parametrize("T,H,E", [(1, 2048, 512), (7, 256, 128), (33, 4096, 64), (9, 2048, 1), (256, 2048, 512)])
+@pytest.mark.parametrize("T,H,E", [(1, 2048, 512), (7, 256, 128), (33, 4096, 64), (9, 2048, 1), (256, 2048, 512),
+                                   (256, 2048, 1), (5, 512, 31), (6, 512, 33)])
 def test_router_logits_bitexact(T, H, E):
     x = _bf16((T, H), 1)
     w = _bf16((E, H), 2, 0.02)
@@ -113,7 +114,11 @@ def glu_path(request):
 @pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
 @pytest.mark.parametrize("bits", [16, 8, 4])
 @pytest.mark.parametrize("H,I,E,T,k", [(256, 128, 8, 5, 2), (2048, 768, 16, 33, 4), (1024, 512, 6, 1, 6),
-                                       (512, 256, 4, 300, 2)])
+                                       (512, 256, 4, 300, 2),
+                                       # ~25 and ~50 pairs per expert: 32- and 64-wide pair tiles
+                                       (512, 256, 8, 100, 2), (512, 256, 4, 100, 2),
+                                       # K = 576 / 640: packed and row-gather stages end part-way
+                                       (576, 256, 8, 40, 2), (640, 384, 8, 24, 3)])
 def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
