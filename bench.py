@@ -40,6 +40,10 @@ sys.path.insert(0, str(ROOT))
 
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+# DRAM bytes (read + write) per routed gate/up launch from an ncu capture, by
+# (workload, tokens per GPU); see profiles/ for the capture and its scaling
+TRAFFIC: dict = {}
 QUEUE_AHEAD_CYCLES = 200_000_000  # ~0.1 s of device spin before the device-resident timed region
 METRIC = "SlottedGLU tokens/s at 1/2/4/8 B200; expert-GEMM HBM GB/s vs 8 TB/s peak"
 
@@ -67,6 +71,15 @@ def hbm_peak():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s of this pool's B200s (burst: a kernel timed alone)."""
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 # --------------------------------------------------------------------------- clocks
@@ -244,7 +257,7 @@ def _kernel_roofline(cfg, timing, rows_per_step, T_local):
     else:
         per_gu = 2 * (I * H * cfg.bits // 8 + (I * H // 64) * 4)
         per_dn = H * I * cfg.bits // 8 + (H * I // 64) * 4
-    gu_ms, dn_ms, gu_b, dn_b, us = [], [], 0, 0, []
+    gu_ms, dn_ms, gu_b, dn_b, us, gu_f, dn_f = [], [], 0, 0, [], 0, 0
     for i, (ev, d) in enumerate(zip(timing["events"], timing["dispatch"])):
         U = int(d.counts[0].item())
         P = rows_per_step[i] if rows_per_step else T_local * k
@@ -254,8 +267,12 @@ def _kernel_roofline(cfg, timing, rows_per_step, T_local):
         dn_ms.append(ev[1].elapsed_time(ev[2]))
         gu_b += U * per_gu + n_in * H * 2 + P * I * 2
         dn_b += U * per_dn + P * I * 2 + P * H * 2
+        gu_f += 4 * P * H * I  # gate and up, 2 flops per multiply-add
+        dn_f += 2 * P * H * I
     return {"gu_ms": gu_ms, "dn_ms": dn_ms, "gu_bytes": gu_b, "dn_bytes": dn_b, "unique": us,
             "gu_gbs": gu_b / (sum(gu_ms) * 1e-3) / 1e9, "dn_gbs": dn_b / (sum(dn_ms) * 1e-3) / 1e9,
+            "gu_tflops": gu_f / (sum(gu_ms) * 1e-3) / 1e12, "dn_tflops": dn_f / (sum(dn_ms) * 1e-3) / 1e12,
+            "pairs_per_expert": (gu_f / (4 * H * I)) / max(1, sum(us)),
             "mean_unique": st.mean(us)}
 
 
@@ -358,6 +375,7 @@ def run_ours(args, rank, world, local_rank):
         return
     rl = _kernel_roofline(cfg, timing, timing.get("rows"), T)
     peak, peak_kind = hbm_peak()
+    tpeak, tpeak_kind = tensor_peak()
     us_mean = rl["mean_unique"]
     step_bytes = (us_mean * cfg.expert_bytes() + cfg.shared_bytes() + cfg.num_experts * H * 2 + 2 * T * H * 2)
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
@@ -432,12 +450,16 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
             "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4), "peak_kind": peak_kind,
-            "traffic": None,
+            "traffic": TRAFFIC.get((cfg.name, T)),
             "bytes_per_launch": round(rl["gu_bytes"] / len(rl["gu_ms"])),
             "ms_per_launch": round(statistics.mean(rl["gu_ms"]), 5),
             "down": {"achieved": round(rl["dn_gbs"], 1), "frac": round(rl["dn_gbs"] / peak, 4),
                      "ms_per_launch": round(statistics.mean(rl["dn_ms"]), 5)},
             "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+            "tensor": {"achieved": round(rl["gu_tflops"], 1), "peak": tpeak, "unit": "TFLOP/s",
+                       "frac": round(rl["gu_tflops"] / tpeak, 4), "peak_kind": tpeak_kind,
+                       "down_achieved": round(rl["dn_tflops"], 1)},
+            "pairs_per_expert": round(rl["pairs_per_expert"], 1),
         },
         "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)},
@@ -446,6 +468,12 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "cpu_baseline": cpu,
     }
+    if rl["pairs_per_expert"] >= 64:
+        # prefill-sized expert groups: the gate/up launch is tensor-core bound
+        r = line["roofline"]
+        hbm = {k: r[k] for k in ("achieved", "peak", "unit", "frac", "peak_kind")}
+        r.update(bound="tensor", achieved=r["tensor"]["achieved"], peak=tpeak, unit="TFLOP/s",
+                 frac=r["tensor"]["frac"], peak_kind=tpeak_kind, hbm=hbm)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -482,6 +510,89 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_stream(args, rank, world, local_rank):
+    """Streaming miss path (config-2 layer shape: H2048 E128 k8 I768, affine
+    q4 g64, 64 slots): a seeded expert bank written to local disk, Zipf(1.1)
+    expert popularity, demand refills through DiskBackedExpertLoader (pread
+    into pinned host buffers, cudaMemcpyAsync into slots on a side stream while
+    the shared-expert-free step continues), end-to-end decode tokens/s at batch
+    1 and 16 (tokens host->device, output device->host every step)."""
+    import tempfile
+
+    import torch
+
+    from preemptlm_b200.bank import PreadExpertBank
+    from preemptlm_b200.cache_manager import ExpertCacheManager
+    from preemptlm_b200.layer import Qwen3_xMoEWrapper
+    from preemptlm_b200.loader import DiskBackedExpertLoader, HostExpertCache
+    from preemptlm_b200.synthetic import CONFIGS, make_layer, make_zipf_tokens, write_bank
+
+    if world > 1:
+        raise SystemExit("the streaming workload runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS["cfg2"].scaled(name="cfg5-stream-q4", num_slots=64)
+    block, tens = make_layer(cfg, device=dev)
+    tmp = Path(tempfile.mkdtemp(prefix="sg_bank_", dir=os.environ.get("SG_BANK_DIR")))
+    t0 = time.perf_counter()
+    write_bank(tmp, cfg, tens["experts"], block.switch_mlp.tensor_names())
+    os.sync()
+    write_s = time.perf_counter() - t0
+    results = {}
+    for batch in (1, 16):
+        bank = PreadExpertBank(tmp, bypass_page_cache=True)
+        nbytes = bank.manifest.expert_num_bytes()
+        cache = HostExpertCache(ExpertCacheManager(budget_bytes=32 * nbytes))
+        loader = DiskBackedExpertLoader(expert_bank=bank, cache=cache)
+
+        class Cand:
+            layer_path, block_idx = "model.layers.0.mlp", 0
+
+        moe = Qwen3_xMoEWrapper.make_wrapper_factory(model_fingerprint=bank.model_fingerprint, expert_loader=loader,
+                                                     expert_cache=cache, num_slots=cfg.num_slots, slot_size=nbytes,
+                                                     slot_policy="lfru")(block, Cand())
+        n = args.warmup + args.steps
+        xs = make_zipf_tokens(tens["router"], n * batch, cfg.top_k, seed=500 + batch, device=dev)
+        x_host = xs.cpu().pin_memory().view(n, batch, cfg.hidden)
+        out_host = torch.empty((batch, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+
+        def step(i):
+            xd = x_host[i].to(dev, non_blocking=True)
+            out_host.copy_(moe(xd.view(1, batch, cfg.hidden)).view(batch, cfg.hidden), non_blocking=True)
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        moe.admit_stats.update(steps=0, unique=0, missed=0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.warmup, n):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        st = moe.admit_stats
+        results[f"batch{batch}"] = {"tokens_per_s": round(batch * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                                    "hit_rate": round(1 - st["missed"] / max(1, st["unique"]), 4),
+                                    "refills_per_step": round(st["missed"] / max(1, st["steps"]), 2)}
+        loader.close()
+        bank.close()
+    import shutil
+
+    shutil.rmtree(tmp, ignore_errors=True)
+    if rank == 0:
+        b16 = results["batch16"]
+        print(json.dumps({
+            "metric": "streaming decode tokens/s (end to end, demand refills from disk)", "value": b16["tokens_per_s"],
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": b16["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4", "data": "synthetic (seeded bank on local disk, Zipf(1.1) routing)",
+            "config": {"workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
+                                   f"affine-q4 g64, {cfg.num_slots} slots, host cache 32 experts, lfru slots",
+                       "bank_write_s": round(write_s, 2), **results},
+        }))
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -491,6 +602,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "cfg5":
+        run_stream(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)
 

@@ -121,6 +121,16 @@ int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs,
                 const int32_t* group_off, const int32_t* perm,
                 int grid_groups, uint16_t* y, void* stream);
 
+/* Dense SwiGLU of one slot over every row: h[t, I] = swiglu(x @ gate^T, x @ up^T),
+ * y[t, H] = bf16(h @ down^T) for t < T, slot sid of the arena (the shared
+ * expert: one slot, all tokens).  h is caller-provided intermediate storage.
+ * Replaces `self.inner.shared_expert(x)`, qwen3_x_moe.py:258.  Needs the
+ * tensor-core shapes (H and I multiples of 128, packed rows of >= 128 bytes);
+ * returns SG_ERR_SHAPE otherwise (sg_glu_gate_up / sg_glu_down over a
+ * one-group dispatch serve those shapes). */
+int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint16_t* h, uint16_t* y,
+                 void* stream);
+
 /* Kernel choice for sg_glu_gate_up / sg_glu_down: 0 = automatic (tcgen05 when
  * the mean pairs per group is >= 2 and the shape allows: in-dim % 64, out-dim
  * % 128, <= 2048 groups), 1 = streaming GEMV always, 2 = tcgen05 whenever the

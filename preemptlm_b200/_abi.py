@@ -25,7 +25,7 @@ SG_ERR_TIMEOUT = -6
 # Every symbol include/sg_abi.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
     "sg_status_string", "sg_version", "sg_built_arch", "sg_router_logits", "sg_route_topk",
-    "sg_dispatch", "sg_glu_gate_up", "sg_glu_down", "sg_combine", "sg_refill_h2d",
+    "sg_dispatch", "sg_glu_gate_up", "sg_glu_down", "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
 )
 
@@ -76,6 +76,7 @@ def load() -> ctypes.CDLL:
         "sg_dispatch": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I32, P]),
         "sg_glu_gate_up": (I32, [A, P, I32, I32, P, P, P, P, I32, P, P]),
         "sg_glu_down": (I32, [A, P, I32, P, P, P, P, I32, P, P]),
+        "sg_dense_glu": (I32, [A, I32, P, I32, P, P, P]),
         "sg_set_glu_path": (I32, [I32]),
         "sg_device_status": (I32, [I32]),
         "sg_combine": (I32, [P, P, I32, I32, I32, P, P, P, P]),

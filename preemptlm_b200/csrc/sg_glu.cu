@@ -264,6 +264,8 @@ bool tc_supported(const sg_arena* A, bool dual, int grid_groups);
 int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_by_pos,
                   int out_by_pos, int P, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
                   const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
+int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
+                    cudaStream_t s);
 static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05
 
 // auto: the tensor-core path once the mean pairs per group reaches 2
@@ -320,4 +322,18 @@ extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pai
     case 8: return sg::launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
     default: return sg::launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
   }
+}
+
+extern "C" int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint16_t* h, uint16_t* y,
+                            void* stream) {
+  int st = sg::check_arena(arena);
+  if (st) return st;
+  if (T < 0 || sid < 0 || sid >= arena->num_slots) return SG_ERR_INVALID_ARG;
+  if (T == 0) return SG_OK;
+  if (!x || !h || !y) return SG_ERR_INVALID_ARG;
+  if (!sg::tc_supported(arena, true, 1) || !sg::tc_supported(arena, false, 1)) return SG_ERR_SHAPE;
+  cudaStream_t s = (cudaStream_t)stream;
+  st = sg::tc_dense_launch(arena, true, x, T, sid, h, s);
+  if (st) return st;
+  return sg::tc_dense_launch(arena, false, h, T, sid, y, s);
 }

@@ -27,6 +27,7 @@
 // copies it issued (bounded as well), frees its TMEM and returns.
 #include <cuda.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "sg_common.cuh"
@@ -39,9 +40,7 @@ namespace tc {
 
 constexpr int BM = 128;            // weight rows per tile (MMA M)
 constexpr int BK = 64;             // K per pipeline stage (one 128-byte swizzle atom of bf16)
-constexpr int NUM_WARPS = 15;
-constexpr int NUM_THREADS = NUM_WARPS * 32;
-constexpr int DQ_WARP0 = 3, DQ_WARPS = 8;  // epilogue warps follow: 11..14
+constexpr int DQ_WARP0 = 3;  // dequantiser warps start here; the 4 epilogue warps follow them
 constexpr int RING_BUDGET = 208 * 1024;
 constexpr int PLAN_MAX_GROUPS = 2048;
 constexpr long long WAIT_CYCLES = 2000000000LL;  // ~1 s
@@ -96,9 +95,24 @@ struct Cfg {
   static constexpr int OFF_B = OFF_A + SA * A_BYTES;
   static constexpr int OFF_P = OFF_B + SB * B_BYTES;
   static constexpr int OFF_PLAN = OFF_P + SP * P_BYTES;
-  static constexpr int OFF_BAR = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
-  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC;
+  // ATM configs also keep the groups' offsets and slots in shared memory, so
+  // that finding a tile's rows never waits on a global load
+  static constexpr bool TILE_SMEM = ATM;
+  static constexpr int OFF_TILE = OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4;
+  // ATM configs stage scale/bias rows by TMA (when the group count is a
+  // multiple of 8): a chunk is 8 groups (16 bytes) x 128 rows per array,
+  // arrays [matrix][scales, biases], SS chunks in flight
+  static constexpr int SS = ATM ? 3 : 0;
+  static constexpr int S_BYTES = NMAT * 2 * BM * 16;
+  static constexpr int OFF_S = (OFF_TILE + (TILE_SMEM ? (2 * PLAN_MAX_GROUPS + 1) * 4 : 0) + 127) & ~127;
+  static constexpr int OFF_BAR = (OFF_S + SS * S_BYTES + 15) & ~15;
+  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC + 2 * SS;
   static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
+  // dequantiser warps: 8, each thread one row of one matrix (gate / up), or
+  // half a row of the single matrix (down); one TMEM lane quadrant per warp
+  static constexpr int DQW = BITS == 16 ? 0 : 8;
+  static constexpr int EPI_WARP0 = DQ_WARP0 + DQW;
+  static constexpr int THREADS = (EPI_WARP0 + 4) * 32;
   static_assert(SA >= 2 && (BITS == 16 || SP >= 2), "pipeline too shallow");
   static_assert(TMEM_COLS <= 512, "tensor memory budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -128,6 +142,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As above, but a thread whose phase is not complete is suspended until it
+// completes or about `ns` nanoseconds pass, instead of spinning on issue slots
+// that the dequantising warps of its SM sub-partition need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.b32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 struct Ctl {
   volatile int* abort;  // shared flag: a wait in this CTA expired
 };
@@ -137,7 +164,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl ctl
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 200000)) return true;  // wakes on completion
     if (*ctl.abort) return false;
     if (clock64() - t0 > WAIT_CYCLES) {
       *ctl.abort = 1;
@@ -427,6 +454,10 @@ struct Args {
   int out_by_pos;  // output row: pos, or perm[pos]
   int max_groups;
   uint16_t* out;
+  // dense mode (dense_rows > 0): one group of dense_rows rows through slot
+  // dense_slot, B row = output row = position; counts / slot_ids / group_off /
+  // perm are not read.  B tiles are then contiguous rows, loaded by TMA.
+  int dense_rows, dense_slot;
 };
 
 struct Tile {
@@ -434,7 +465,8 @@ struct Tile {
 };
 
 template <int BN>
-__device__ __forceinline__ Tile tile_of(int t, const int* plan, int U, int NT, const Args& a) {
+__device__ __forceinline__ Tile tile_of(int t, const int* plan, int U, int NT, const Args& a, const int* goff_tab,
+                                       const int* slot_tab) {
   Tile tl;
   tl.m = t / NT;
   const int fn = t - tl.m * NT;
@@ -446,10 +478,16 @@ __device__ __forceinline__ Tile tile_of(int t, const int* plan, int U, int NT, c
   }
   tl.u = lo;
   tl.n0 = (fn - plan[lo]) * BN;
-  tl.goff = a.group_off[lo];
-  const int cnt = a.group_off[lo + 1] - tl.goff;
+  if (a.dense_rows > 0) {
+    tl.goff = 0;
+    tl.nvalid = min(BN, a.dense_rows - tl.n0);
+    tl.slot = a.dense_slot;
+    return tl;
+  }
+  tl.goff = goff_tab[lo];
+  const int cnt = goff_tab[lo + 1] - tl.goff;
   tl.nvalid = min(BN, cnt - tl.n0);
-  tl.slot = a.slot_ids[lo];
+  tl.slot = slot_tab[lo];
   return tl;
 }
 
@@ -486,10 +524,14 @@ struct ScaleVec<1> {
   __device__ __forceinline__ float bi(int) const { return bf16_to_f32(b); }
 };
 
-template <int BITS, bool DUAL, int BN, int V>
+// STMA: scales and biases come from the TMA-staged chunk ring in shared
+// memory (8 groups per chunk) instead of per-thread global loads.
+template <int BITS, bool DUAL, int BN, int V, bool STMA>
 __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, int U, int NT, int total,
                                              uint8_t* sA, const uint8_t* sP, uint64_t* a_full, uint64_t* a_empty,
-                                             uint64_t* p_full, uint64_t* p_empty, Ctl ctl, uint32_t tmem_a) {
+                                             uint64_t* p_full, uint64_t* p_empty, Ctl ctl, uint32_t tmem_a,
+                                             const int* gtab, const int* stab, const uint8_t* sS,
+                                             uint64_t* s_full, uint64_t* s_empty) {
   using C = Cfg<BITS, DUAL, BN>;
   // row r = 32 (warp % 4) + lane: the TMEM lane quadrant this warp may write
   const int warp = threadIdx.x >> 5;
@@ -503,37 +545,44 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
   // dequantises zeros: its A tile is the TMA's zero fill and the epilogue
   // writes zeros for it)
   auto row_ptrs = [&](int t, const uint16_t*& sp, const uint16_t*& bp, bool& sok) {
-    const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+    const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
     sok = tl.slot >= 0 && tl.slot < args.num_slots;
     const size_t row = sok ? (size_t)tl.slot * args.OUT + tl.m * BM + r : 0;
     sp = sbase + row * groups;
     bp = bbase + row * groups;
   };
-  int sa = 0, sp_i = 0;
-  uint32_t pa = 0, pp = 0;
+  int sa = 0, sp_i = 0, ss = 0;
+  uint32_t pa = 0, pp = 0, sph = 0;
   bool ok = true;
   int t = blockIdx.x;
   if (t >= total) return;
-  const uint16_t *cs, *cb;
-  bool csok;
-  row_ptrs(t, cs, cb, csok);
   ScaleVec<V> cur, nxt;
-  cur.load(cs, cb, 0);
-  int nxt_t = t, nxt_v = 1;  // (tile, vector) held in nxt
-  if (nvec == 1) {
-    nxt_t = t + gridDim.x;
-    nxt_v = 0;
-  }
-  if (nxt_t < total) {
-    const uint16_t *ns, *nb;
-    bool nsok;
-    row_ptrs(nxt_t, ns, nb, nsok);
-    nxt.load(ns, nb, nxt_v);
+  if constexpr (!STMA) {
+    const uint16_t *cs, *cb;
+    bool csok;
+    row_ptrs(t, cs, cb, csok);
+    cur.load(cs, cb, 0);
+    int nxt_t = t, nxt_v = 1;  // (tile, vector) held in nxt
+    if (nvec == 1) {
+      nxt_t = t + gridDim.x;
+      nxt_v = 0;
+    }
+    if (nxt_t < total) {
+      const uint16_t *ns, *nb;
+      bool nsok;
+      row_ptrs(nxt_t, ns, nb, nsok);
+      nxt.load(ns, nb, nxt_v);
+    }
   }
   for (; t < total && ok; t += gridDim.x) {
     bool sok;
-    const uint16_t *tsp, *tbp;
-    row_ptrs(t, tsp, tbp, sok);
+    if constexpr (STMA) {
+      const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
+      sok = tl.slot >= 0 && tl.slot < args.num_slots;
+    } else {
+      const uint16_t *tsp, *tbp;
+      row_ptrs(t, tsp, tbp, sok);
+    }
     uint4 pk[8];
     for (int kb0 = 0; kb0 < NKB && ok; kb0 += C::KP) {
       // take this thread's share of the packed stage into registers and
@@ -560,23 +609,42 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
         }
-        const int j = kb % V;
-        if (j == 0 && kb > 0) {  // next vector of this tile becomes current
-          cur = nxt;
-          int vn = kb / V + 1;
-          int tn = t;
-          if (vn >= nvec) {
-            vn = 0;
-            tn = t + gridDim.x;
+        float gs, gb;  // this sub-stage's scale and bias
+        if constexpr (STMA) {
+          if ((kb & 7) == 0) {
+            ok = wait_bar(&s_full[ss], sph, ctl);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
           }
-          if (tn < total) {
-            const uint16_t *ns, *nb;
-            bool nsok;
-            row_ptrs(tn, ns, nb, nsok);
-            nxt.load(ns, nb, vn);
+          const uint8_t* sc = sS + ss * C::S_BYTES + mat * (2 * BM * 16) + r * 16 + (kb & 7) * 2;
+          gs = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc));
+          gb = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc + BM * 16));
+          if ((kb & 7) == 7) {  // chunk done (group counts are multiples of 8 here)
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) mbar_arrive(&s_empty[ss]);
+            if (++ss == C::SS) { ss = 0; sph ^= 1; }
           }
+        } else {
+          const int j = kb % V;
+          if (j == 0 && kb > 0) {  // next vector of this tile becomes current
+            cur = nxt;
+            int vn = kb / V + 1;
+            int tn = t;
+            if (vn >= nvec) {
+              vn = 0;
+              tn = t + gridDim.x;
+            }
+            if (tn < total) {
+              const uint16_t *ns, *nb;
+              bool nsok;
+              row_ptrs(tn, ns, nb, nsok);
+              nxt.load(ns, nb, vn);
+            }
+          }
+          gs = cur.sc(j);
+          gb = cur.bi(j);
         }
-        const GroupScale g = make_scale<BITS>(sok ? cur.sc(j) : 0.f, sok ? cur.bi(j) : 0.f);
+        const GroupScale g = make_scale<BITS>(sok ? gs : 0.f, sok ? gb : 0.f);
         if (C::ATM) {
           uint32_t out[32];
           if (g.fused) dequant_sub_regs<BITS, DUAL, true>(pk, jp, g, out);
@@ -590,20 +658,30 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
             const uint32_t (&hi)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[16]);
             tmem_st16(ta + 16, hi);
           }
-          tmem_st_wait();
-          tc_fence_before();
+          // one store wait per group of MG stages (the MMA reads a group only
+          // once all of it is full): the first stage's stores complete while
+          // the next one is computed
+          if (jp % C::MG == C::MG - 1 || jp == nsub - 1) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) {
+              for (int q = jp % C::MG; q >= 0; --q) mbar_arrive(&a_full[sa >= q ? sa - q : sa - q + C::SA]);
+            }
+          }
         } else {
           if (g.fused) dequant_sub<BITS, DUAL, true>(pk, jp, sA + sa * C::A_BYTES + mat * C::A_MAT, r, part, g);
           else dequant_sub<BITS, DUAL, false>(pk, jp, sA + sa * C::A_BYTES + mat * C::A_MAT, r, part, g);
           fence_async_smem();
+          __syncwarp();
+          if ((threadIdx.x & 31) == 0) mbar_arrive(&a_full[sa]);
         }
-        __syncwarp();
-        if ((threadIdx.x & 31) == 0) mbar_arrive(&a_full[sa]);
         if (++sa == C::SA) { sa = 0; pa ^= 1; }
       }
     }
     // the first vector of the next tile is already in nxt
-    if (nvec > 1 || V == 1) {
+    if constexpr (STMA) {
+    } else if (nvec > 1 || V == 1) {
       cur = nxt;
       const int tn = t + gridDim.x;
       if (tn < total) {
@@ -632,10 +710,12 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
   }
 }
 
-template <int BITS, bool DUAL, int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BITS, bool DUAL, int BN, bool STMA>
+__global__ void __launch_bounds__(Cfg<BITS, DUAL, BN>::THREADS, 1)
 glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-              const Args args) {
+              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS0,
+              const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__ CUtensorMap tmS1,
+              const __grid_constant__ CUtensorMap tmQ1, const Args args) {
   using C = Cfg<BITS, DUAL, BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -643,6 +723,8 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sP = smem + C::OFF_P;
   int* plan = reinterpret_cast<int*>(smem + C::OFF_PLAN);
+  int* s_goff = reinterpret_cast<int*>(smem + C::OFF_TILE);
+  int* s_slot = s_goff + PLAN_MAX_GROUPS + 1;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* a_full = bars;                   // [SA] A stage ready (TMA tx or 8 dequant warps)
   uint64_t* a_empty = a_full + C::SA;        // [SA] A stage consumed (MMA commit)
@@ -652,6 +734,9 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   uint64_t* p_empty = p_full + C::SP;        // [SP] packed stage consumed (8 dequant warps)
   uint64_t* acc_full = p_empty + C::SP;      // [NACC] accumulator ready (MMA commit)
   uint64_t* acc_empty = acc_full + C::NACC;  // [NACC] accumulator drained (4 epilogue warps)
+  uint64_t* s_full = acc_empty + C::NACC;    // [SS] scale chunk landed (TMA tx)
+  uint64_t* s_empty = s_full + C::SS;        // [SS] scale chunk consumed (dequantiser warps)
+  const uint8_t* sS = smem + C::OFF_S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Ctl ctl{abort_flag};
@@ -663,30 +748,43 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::SA; ++i) {
-      mbar_init(&a_full[i], BITS == 16 ? 1 : DQ_WARPS);
+      mbar_init(&a_full[i], BITS == 16 ? 1 : C::DQW);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SB; ++i) {
-      mbar_init(&b_full[i], 32);  // one cp.async arrival per producer lane
+      mbar_init(&b_full[i], args.dense_rows > 0 ? 1 : 32);  // TMA tx, or one cp.async arrival per producer lane
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < C::SP; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], DQ_WARPS);
+      mbar_init(&p_empty[i], C::DQW);
     }
     for (int i = 0; i < C::NACC; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
+    for (int i = 0; i < C::SS; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], C::DQW);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // tile plan: plan[u] = first flat n-tile of group u (prefix of ceil(count / BN))
-  const int U = min(args.counts[0], args.max_groups);
+  const int U = args.dense_rows > 0 ? 1 : min(args.counts[0], args.max_groups);
+  const bool tab_smem = C::TILE_SMEM && args.dense_rows == 0;
   for (int u = threadIdx.x; u < U; u += blockDim.x) {
-    const int cnt = args.group_off[u + 1] - args.group_off[u];
+    const int g0 = args.dense_rows > 0 ? 0 : args.group_off[u], g1 = args.dense_rows > 0 ? 0 : args.group_off[u + 1];
+    const int cnt = args.dense_rows > 0 ? args.dense_rows : g1 - g0;
     plan[u + 1] = (cnt + BN - 1) / BN;
+    if (tab_smem) {
+      s_goff[u] = g0;
+      s_slot[u] = args.slot_ids[u];
+      if (u == U - 1) s_goff[U] = g1;
+    }
   }
+  const int* gtab = tab_smem ? s_goff : args.group_off;
+  const int* stab = tab_smem ? s_slot : args.slot_ids;
   if (threadIdx.x == 0) plan[0] = 0;
   __syncthreads();
   if (warp == 0) {  // inclusive scan of plan[1..U] by one warp, in 32-entry blocks
@@ -728,8 +826,8 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       // scale/bias rows of a tile (contiguous, 128 rows x K/64 groups) go to
       // L2 one tile ahead, so the dequantisers' loads of them hit L2
       auto prefetch_scales = [&](int tt) {
-        if (BITS == 16 || tt >= total) return;
-        const Tile tn = tile_of<BN>(tt, plan, U, NT, args);
+        if (BITS == 16 || STMA || tt >= total) return;
+        const Tile tn = tile_of<BN>(tt, plan, U, NT, args, gtab, stab);
         if (tn.slot < 0 || tn.slot >= args.num_slots) return;
         const int groups = K / 64;
         const size_t off = ((size_t)tn.slot * args.OUT + (size_t)tn.m * BM) * groups;
@@ -742,12 +840,30 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         }
       };
       prefetch_scales(blockIdx.x);
+      int ss = 0, s_issued = 0;  // scale chunk ring (TMA-staged scales)
+      uint32_t sph = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+        const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
         prefetch_scales(t + gridDim.x);
         const int row0 = tl.slot * args.OUT + tl.m * BM;
         const int nstage = BITS == 16 ? NKB : (NKB + C::KP - 1) / C::KP;
         for (int kb = 0; kb < nstage; ++kb) {
+          if (STMA && (kb * C::KP) % 8 == 0) {
+            // scales and biases of groups [kb*KP, kb*KP + 8) for the tile's
+            // rows, ahead of the packed stages that use them
+            ok = wait_bar(&s_empty[ss], sph ^ 1, ctl);
+            if (!ok) break;
+            uint8_t* dst = const_cast<uint8_t*>(sS) + ss * C::S_BYTES;
+            mbar_expect_tx(&s_full[ss], C::S_BYTES);
+            tma_load_2d(dst, &tmS0, kb * C::KP, row0, &s_full[ss]);
+            tma_load_2d(dst + BM * 16, &tmQ0, kb * C::KP, row0, &s_full[ss]);
+            if (DUAL) {
+              tma_load_2d(dst + 2 * BM * 16, &tmS1, kb * C::KP, row0, &s_full[ss]);
+              tma_load_2d(dst + 3 * BM * 16, &tmQ1, kb * C::KP, row0, &s_full[ss]);
+            }
+            ++s_issued;
+            if (++ss == C::SS) { ss = 0; sph ^= 1; }
+          }
           ok = wait_bar(&empty[s_i], ph ^ 1, ctl);
           if (!ok) break;
           if (BITS == 16) {
@@ -775,14 +891,54 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           while (!mbar_try_wait(&full[s], p) && clock64() - t0 < WAIT_CYCLES) {
           }
         }
+        for (int i = 0; i < min(s_issued, C::SS); ++i) {
+          int s = ss - 1 - i;
+          uint32_t p = sph;
+          if (s < 0) { s += C::SS; p ^= 1; }
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&s_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
+          }
+        }
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------------- B row producer
-    // The tile's pair rows, 16-byte LSU copies straight into the SW128 operand
-    // layout (row j of a stage at 128 j, chunk c at c ^ (j & 7)); lane l copies
-    // chunk l % 8 of rows l / 8 + 4 i.  Each lane reports its copies to the
-    // stage's full barrier (32 arrivals); rows past the tile's pairs are zero.
+    if (args.dense_rows > 0) {
+      // dense mode: the tile's rows are contiguous, one TMA box (BN rows x
+      // 128 bytes, SW128, zero fill past the last row) per operand stage
+      if (lane == 0) {
+        int sb = 0, issued = 0;
+        uint32_t pb = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+          const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
+          for (int kb0 = 0; kb0 < NKB; kb0 += C::KBB) {
+            ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
+            if (!ok) break;
+            const int nsub = min(C::KBB, NKB - kb0);
+            mbar_expect_tx(&b_full[sb], nsub * C::B_SUB);
+            for (int j = 0; j < nsub; ++j)
+              tma_load_2d(sB + sb * C::B_BYTES + j * C::B_SUB, &tmB, (kb0 + j) * BK, tl.n0, &b_full[sb]);
+            ++issued;
+            if (++sb == C::SB) { sb = 0; pb ^= 1; }
+          }
+        }
+        if (!ok) {  // drain the loads still in flight (bounded)
+          for (int i = 0; i < min(issued, C::SB); ++i) {
+            int st = sb - 1 - i;
+            uint32_t p = pb;
+            if (st < 0) { st += C::SB; p ^= 1; }
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&b_full[st], p) && clock64() - t0 < WAIT_CYCLES) {
+            }
+          }
+        }
+      }
+    } else {
+    // Gathered rows: 16-byte LSU copies straight into the SW128 operand layout
+    // (row j of a stage at 128 j, chunk c at c ^ (j & 7)); lane l copies chunk
+    // l % 8 of rows l / 8 + 4 i.  Each lane reports its copies to the stage's
+    // full barrier (32 arrivals); rows past the tile's pairs are zero.
     constexpr int RPL = BN / 4;  // rows per lane
     const int c = lane & 7, r0 = lane >> 3;
     const size_t row_bytes = static_cast<size_t>(K) * 2;
@@ -790,7 +946,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     uint32_t pb = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+      const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
       int row[RPL];  // source row of each of this lane's tile rows, -1: zero fill
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
@@ -822,6 +978,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       }
     }
     cp_async_wait_all();  // no copy of this warp outlives the kernel
+    }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -854,12 +1011,13 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           const uint32_t b_base = smem_u32(sB + sb * C::B_BYTES + jb * C::B_SUB);
           if (C::ATM) {
             const uint32_t a_t = tmem + C::ACC_TOTAL + sa * C::NMAT * (BK / 2);
+            const uint64_t bd0 = desc_sw128(b_base);  // +2 per 32-byte K step (address field is addr >> 4)
+            umma_bf16_ts(d0, a_t, bd0, idesc, kb != 0);
+            if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2, bd0, idesc, kb != 0);
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t bd = desc_sw128(b_base + kk * 32);
-              const uint32_t acc = (kb | kk) != 0;
-              umma_bf16_ts(d0, a_t + kk * 8, bd, idesc, acc);
-              if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2 + kk * 8, bd, idesc, acc);
+            for (int kk = 1; kk < BK / 16; ++kk) {
+              umma_bf16_ts(d0, a_t + kk * 8, bd0 + 2 * kk, idesc, 1u);
+              if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2 + kk * 8, bd0 + 2 * kk, idesc, 1u);
             }
           } else {
             const uint32_t a_base = smem_u32(sA + sa * C::A_BYTES);
@@ -881,18 +1039,21 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         if (ok) umma_commit(&acc_full[ab]);
       }
     }
-  } else if (warp >= DQ_WARP0 && warp < DQ_WARP0 + DQ_WARPS) {
+  } else if (warp >= DQ_WARP0 && warp < C::EPI_WARP0) {
     // ---------------------------------------------------------------- dequantisers
     if (BITS != 16) {
-      if ((K / 64) % 4 == 0)
-        dequant_role<BITS, DUAL, BN, 4>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl,
-                                        tmem);
+      if constexpr (STMA)
+        dequant_role<BITS, DUAL, BN, 1, true>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+                                              ctl, tmem, gtab, stab, sS, s_full, s_empty);
+      else if ((K / 64) % 4 == 0)
+        dequant_role<BITS, DUAL, BN, 4, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+                                               ctl, tmem, gtab, stab, sS, s_full, s_empty);
       else
-        dequant_role<BITS, DUAL, BN, 1>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty, ctl,
-                                        tmem);
+        dequant_role<BITS, DUAL, BN, 1, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+                                               ctl, tmem, gtab, stab, sS, s_full, s_empty);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 11-14)
+    // ---------------------------------------------------------------- epilogue (last 4 warps)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     int it = 0;
@@ -900,7 +1061,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
       const int ab = it % C::NACC;
       const uint32_t accp = static_cast<uint32_t>((it / C::NACC) & 1);
-      const Tile tl = tile_of<BN>(t, plan, U, NT, args);
+      const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
       ok = wait_bar(&acc_full[ab], accp, ctl);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
       if (!ok) break;
@@ -995,11 +1156,12 @@ static int num_sms() {
 }
 
 template <int BITS, bool DUAL, int BN>
-static int launch_cfg(const sg_arena* A, const Args& args, cudaStream_t s) {
+static int launch_cfg(const sg_arena* A, const Args& args_in, cudaStream_t s) {
   using C = Cfg<BITS, DUAL, BN>;
+  Args args = args_in;
   const int K = args.K, OUT = args.OUT;
   const uint64_t rows_total = (uint64_t)A->num_slots * OUT;
-  CUtensorMap m0, m1;
+  CUtensorMap m0, m1, mb, ms0, mq0, ms1, mq1;
   const void* w0 = DUAL ? A->gate_w : A->down_w;
   const void* w1 = DUAL ? A->up_w : A->down_w;
   bool ok;
@@ -1011,17 +1173,51 @@ static int launch_cfg(const sg_arena* A, const Args& args, cudaStream_t s) {
     ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
          make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   }
+  // B rows (dense mode): [in_rows, K] bf16, box BN rows x 64 columns
+  if (args.dense_rows > 0)
+    ok = ok && make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.in, K, (uint64_t)args.in_rows, BK, BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    memset(&mb, 0, sizeof(mb));
+  // scale/bias chunks by TMA: [rows_total, K/64] bf16, box 8 groups x 128 rows
+  // (needs 16-byte row strides: group counts that are multiples of 8)
+  const int groups = K / 64;
+  const bool scale_tma = C::SS > 0 && groups % 8 == 0;
+  memset(&ms0, 0, sizeof(ms0));
+  memset(&mq0, 0, sizeof(mq0));
+  memset(&ms1, 0, sizeof(ms1));
+  memset(&mq1, 0, sizeof(mq1));
+  if (scale_tma)
+    ok = ok &&
+         make_map(&ms0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.s0, groups, rows_total, 8, BM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         make_map(&mq0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.b0, groups, rows_total, 8, BM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         make_map(&ms1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.s1, groups, rows_total, 8, BM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         make_map(&mq1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.b1, groups, rows_total, 8, BM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) return SG_ERR_CUDA;
   static bool attr_done[64] = {};  // per device
   int dev = 0;
   SG_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
   if (!attr_done[dev]) {
-    SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C::SMEM));
+    SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    if constexpr (C::SS > 0)
+      SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done[dev] = true;
   }
-  glu_tc_kernel<BITS, DUAL, BN><<<num_sms(), NUM_THREADS, C::SMEM, s>>>(m0, m1, args);
+  if constexpr (C::SS > 0) {
+    if (scale_tma) {
+      glu_tc_kernel<BITS, DUAL, BN, true><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
+      SG_LAUNCH_CHECK();
+      return SG_OK;
+    }
+  }
+  glu_tc_kernel<BITS, DUAL, BN, false><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -1077,7 +1273,42 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   a.out_by_pos = out_by_pos;
   a.max_groups = grid_groups;
   a.out = out;
+  a.dense_rows = 0;
+  a.dense_slot = 0;
   const int bn = pick_bn(P, grid_groups);
+  switch (A->bits) {
+    case 16: return dual ? tc::launch_bits<16, true>(A, bn, a, s) : tc::launch_bits<16, false>(A, bn, a, s);
+    case 8: return dual ? tc::launch_bits<8, true>(A, bn, a, s) : tc::launch_bits<8, false>(A, bn, a, s);
+    default: return dual ? tc::launch_bits<4, true>(A, bn, a, s) : tc::launch_bits<4, false>(A, bn, a, s);
+  }
+}
+
+// Dense mode: all `rows` rows of `in` through slot `sid` (the shared expert).
+// Pair tiles of 64 keep the tensor-memory operand path while the tiles fit in
+// one wave of CTAs; wider problems take 128-wide tiles (less re-dequantisation).
+int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
+                    cudaStream_t s) {
+  tc::Args a;
+  memset(&a, 0, sizeof(a));
+  a.num_slots = A->num_slots;
+  a.K = dual ? A->hidden : A->inter;
+  a.OUT = dual ? A->inter : A->hidden;
+  a.s0 = static_cast<const uint16_t*>(dual ? A->gate_s : A->down_s);
+  a.b0 = static_cast<const uint16_t*>(dual ? A->gate_b : A->down_b);
+  a.s1 = static_cast<const uint16_t*>(dual ? A->up_s : A->down_s);
+  a.b1 = static_cast<const uint16_t*>(dual ? A->up_b : A->down_b);
+  a.in = reinterpret_cast<const uint8_t*>(in);
+  a.in_rows = rows;
+  a.pair_div = 1;
+  a.in_by_pos = 1;
+  a.out_by_pos = 1;
+  a.max_groups = 1;
+  a.out = out;
+  a.dense_rows = rows;
+  a.dense_slot = sid;
+  const int mt = a.OUT / tc::BM;
+  int bn = rows > 32 ? 64 : (rows > 16 ? 32 : 16);
+  if ((long long)mt * ((rows + 63) / 64) > tc::num_sms()) bn = 128;
   switch (A->bits) {
     case 16: return dual ? tc::launch_bits<16, true>(A, bn, a, s) : tc::launch_bits<16, false>(A, bn, a, s);
     case 8: return dual ? tc::launch_bits<8, true>(A, bn, a, s) : tc::launch_bits<8, false>(A, bn, a, s);

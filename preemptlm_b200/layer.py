@@ -90,7 +90,13 @@ def _combine_shared(y, scores, shared_y, shared_gate):
 
 
 def shared_expert_forward(arena: SlottedGLU, x2: torch.Tensor) -> torch.Tensor:
-    """Dense SwiGLU of the shared expert (mlx_lm Qwen3NextMLP) on every token."""
+    """Dense SwiGLU of the shared expert (mlx_lm Qwen3NextMLP) on every token:
+    the dense tensor-core kernel from two tokens on (its B rows are contiguous
+    and load by TMA), else the one-group gathered path."""
+    if x2.shape[0] >= 2 and ops.glu_path() != "gemv":
+        y = ops.dense_glu(arena, x2)
+        if y is not None:
+            return y
     d = ops.token_dispatch(x2.shape[0], x2.device)
     h = ops.glu_gate_up(arena, x2, d, pair_div=1)
     return ops.glu_down(arena, h, d)
@@ -122,6 +128,9 @@ class Qwen3_xMoEWrapper(SlotTable):
         self.slot_size = slot_size or 0
         self._quants = inner.quant
         self._pending: list = []  # (event, pinned blobs) kept alive until their copies finish
+        self._copy_stream: torch.cuda.Stream | None = None  # slot refills, overlapped with compute
+        self._refill_event: torch.cuda.Event | None = None  # the last step's refills, for the GLU to wait on
+        self.admit_stats = {"steps": 0, "unique": 0, "missed": 0}  # streaming: routed experts seen / refilled
         self._weight_slots: SlottedGLU | None = None
         if expert_loader is not None or expert_cache is not None:
             H, I = inner.hidden_size, inner.moe_intermediate_size
@@ -162,6 +171,9 @@ class Qwen3_xMoEWrapper(SlotTable):
         d = ops.dispatch(routed_eids, self.num_experts, self.eid2sid_device)
         counts = d.counts.cpu()  # the one host read of a hit-only step
         n_unique, n_missed = int(counts[0]), int(counts[1])
+        self.admit_stats["steps"] += 1
+        self.admit_stats["unique"] += n_unique
+        self.admit_stats["missed"] += n_missed
         if n_unique > self.num_slots:
             raise RuntimeError(
                 f"MoE block {self.block_idx}: total slots available ({self.num_slots}) "
@@ -179,14 +191,22 @@ class Qwen3_xMoEWrapper(SlotTable):
         self._eid_lookup_table[evicted] = EMPTY
         self._sid_lookup_table[acquired] = EMPTY
         blobs = self.expert_loader.load_sync(glob_eids.tolist())
-        stream = torch.cuda.current_stream(self._device)
+        # refills run on a side stream: they start once earlier work on the
+        # compute stream (the previous steps' reads of the replaced slots) is
+        # done, and the shared expert runs meanwhile; the GLU waits on them
+        compute = torch.cuda.current_stream(self._device)
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self._device)
+        copy = self._copy_stream
+        copy.wait_stream(compute)
         for eid, sid, payload in zip(missed, acquired, blobs):
-            self._weight_slots.refill_from_blob(int(sid), payload.as_tensor(), stream)
+            self._weight_slots.refill_from_blob(int(sid), payload.as_tensor(), copy)
             self._eid_lookup_table[eid] = sid
             self._sid_lookup_table[sid] = eid
         ev = torch.cuda.Event()
-        ev.record(stream)
+        ev.record(copy)
         self._pending.append((ev, blobs))
+        self._refill_event = ev
         self.sync_device()
         d.slot_ids[:n_unique] = self.eid2sid_device[d.unique[:n_unique].long()]
         return unique, d.inverse, d
@@ -219,6 +239,9 @@ class Qwen3_xMoEWrapper(SlotTable):
         x2 = x.reshape(B * S, H).contiguous()
         logits = ops.router_linear(x2, self.inner.gate)
         inds, scores = _get_routings(logits, self.inner.top_k, self.inner.norm_topk_prob)
+        admitted = None
+        if self.expert_cache is not None:
+            admitted = self._maybe_admit(inds)  # slot refills start on the side stream
         shared_y = shared_gate = None
         if self.inner.shared_expert is not None:
             shared_y = shared_expert_forward(self.inner.shared_expert, x2)
@@ -231,8 +254,11 @@ class Qwen3_xMoEWrapper(SlotTable):
             d = ops.dispatch(inds, self.num_experts, self._identity)
             y = self._gather_forward_dispatched(x2, d, self.inner.switch_mlp)
         else:
-            unique, _inverse, d = self._maybe_admit(inds)
+            unique, _inverse, d = admitted
             slot_ids = self._eid_lookup_table[unique]
+            if self._refill_event is not None:
+                torch.cuda.current_stream(self._device).wait_event(self._refill_event)
+                self._refill_event = None
             y = self._gather_forward_dispatched(x2, d, self._weight_slots)
             self._touch(slot_ids)
         out = _combine_shared(y.reshape(B * S, self.inner.top_k, H), scores, shared_y, shared_gate)

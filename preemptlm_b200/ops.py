@@ -150,13 +150,42 @@ def glu_down(arena, h: torch.Tensor, d: Dispatch) -> torch.Tensor:
     return y
 
 
+def dense_glu(arena, x: torch.Tensor, sid: int = 0) -> torch.Tensor | None:
+    """y = down(swiglu(gate(x), up(x))) of slot ``sid`` over every row of x
+    (``sg_dense_glu``, the shared expert).  Returns None for shapes the dense
+    tensor-core kernel does not take (the caller then runs the one-group
+    gathered path)."""
+    x = _bf16_2d(x, "x")
+    T = x.shape[0]
+    y = torch.empty((T, arena.hidden), dtype=torch.bfloat16, device=x.device)
+    if T == 0:
+        return y
+    h = torch.empty((T, arena.inter), dtype=torch.bfloat16, device=x.device)
+    lib = _abi.load()
+    st = lib.sg_dense_glu(ctypes.byref(arena.desc()), int(sid), x.data_ptr(), T, h.data_ptr(), y.data_ptr(),
+                          _stream())
+    if st == _abi.SG_ERR_SHAPE:
+        return None
+    _abi.check(st, "sg_dense_glu")
+    LAUNCHES[0] += 2
+    return y
+
+
 GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2}
+
+
+_GLU_PATH = ["auto"]
 
 
 def set_glu_path(mode: str) -> None:
     """Pick the gathered-GLU kernel: "auto", "gemv" (streaming CUDA-core
     GEMV) or "tc" (tcgen05 tensor cores)."""
     _abi.call("sg_set_glu_path", GLU_PATHS[mode])
+    _GLU_PATH[0] = mode
+
+
+def glu_path() -> str:
+    return _GLU_PATH[0]
 
 
 def device_status(reset: bool = True) -> int:

@@ -118,3 +118,44 @@ def make_layer(cfg: LayerConfig, device="cuda", gen_device=None, experts: dict |
 
 def make_tokens(cfg: LayerConfig, T: int, device="cuda", step: int = 0) -> torch.Tensor:
     return _randn((T, cfg.hidden), _gen(1000 * cfg.cfg_id + 100 + step, device), device, 1.0)
+
+
+def write_bank(path, cfg: LayerConfig, experts: dict[str, torch.Tensor], tensor_names, block_idx: int = 0):
+    """Write ``experts`` (blob-name tensors, [E, ...]) as an expert bank of one
+    MoE block with ExpertBankWriter: the seeded synthetic bank of the streaming
+    workload."""
+    from .bank import ExpertBankWriter, ModelMoESpec, assemble_expert_blob, derive_tensor_specs, make_encoding_tag
+
+    names = tuple(tensor_names)
+    specs = derive_tensor_specs({n: experts[n][0] for n in names}, names)
+    spec = ModelMoESpec(moe_block_idxs=(block_idx,), num_routed_experts=cfg.num_experts, top_k=cfg.top_k)
+    enc = make_encoding_tag(None if cfg.bits == 16 else cfg.bits, 64)
+    with ExpertBankWriter(path, model_id=cfg.name, model_fingerprint=f"synthetic-{cfg.cfg_id}", encoding=enc,
+                          tensor_specs=specs, model_moe_spec=spec, overwrite=True) as w:
+        for e in range(cfg.num_experts):
+            w.add_expert(block_idx, e, assemble_expert_blob({n: experts[n][e] for n in names}, specs))
+    return None
+
+
+def make_zipf_tokens(router: torch.Tensor, T: int, top_k: int, seed: int, s: float = 1.1, device="cuda",
+                     noise: float = 0.1) -> torch.Tensor:
+    """Tokens whose routing follows a Zipf(s) expert popularity: each token is
+    a sum of the (normalised) router rows of top_k experts drawn by Zipf rank
+    over a seeded random ranking of the experts, plus N(0, noise) -- so the
+    real router sends it (almost always) to those experts."""
+    import numpy as np
+
+    E, H = router.shape
+    rng = np.random.default_rng(seed)
+    rank = rng.permutation(E)
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p /= p.sum()
+    w = router.float().to(device)
+    wn = w / (w * w).sum(1, keepdim=True)
+    picks = np.stack([rank[rng.choice(E, size=top_k, replace=False, p=p)] for _ in range(T)])
+    idx = torch.from_numpy(picks).to(device)
+    x = 3.0 * wn[idx].sum(1)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = x + noise * torch.randn((T, H), generator=g, device=device)
+    return x.to(torch.bfloat16)

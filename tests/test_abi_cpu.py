@@ -68,6 +68,13 @@ def test_host_side_argument_checks(lib):
     a.bits, a.group_size, a.hidden = 16, 64, 100
     assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_set_glu_path(3) == _abi.SG_ERR_INVALID_ARG
+    a = _abi.sg_arena(num_slots=2, hidden=1024, inter=512, bits=8, group_size=64, gate_w=1, up_w=1, down_w=1,
+                      gate_s=1, gate_b=1, up_s=1, up_b=1, down_s=1, down_b=1)
+    assert lib.sg_dense_glu(ctypes.byref(a), 2, 1, 4, 1, 1, None) == _abi.SG_ERR_INVALID_ARG  # slot out of range
+    assert lib.sg_dense_glu(ctypes.byref(a), 0, None, 4, 1, 1, None) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_dense_glu(ctypes.byref(a), 0, None, 0, None, None, None) == _abi.SG_OK  # empty: no pointer read
+    a.inter = 192  # I % 128 != 0: not a dense tensor-core shape
+    assert lib.sg_dense_glu(ctypes.byref(a), 0, 1, 4, 1, 1, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_combine(1, 1, 1, 2, 12, None, None, 1, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_combine(1, 1, 1, 2, 16, 1, None, 1, None) == _abi.SG_ERR_INVALID_ARG
     a = _abi.sg_arena(num_slots=4, hidden=256, inter=128, bits=16, group_size=64, gate_w=1, up_w=1, down_w=1)

@@ -150,6 +150,23 @@ def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what="y|h")
 
 
+@pytest.mark.parametrize("bits", [16, 8, 4])
+@pytest.mark.parametrize("T", [2, 37, 256, 1100])
+def test_dense_glu_matches_oracle(bits, T):
+    """The shared expert's dense path (sg_dense_glu): 16/32/64-wide pair tiles
+    with TMA row loads, and 128-wide ones once the tiles overflow one wave."""
+    H, I = 1024, 512
+    cfg = LayerConfig("t", 9, H, 3, 1, I, None, bits, 3)
+    block, tens = make_layer(cfg, device=DEV)
+    x = _bf16((T, H), 13)
+    y = ops.dense_glu(block.switch_mlp, x, sid=2)
+    assert y is not None
+    ew = LazyExperts(tens["experts"], bits)[2]
+    ref = orc.expert_forward(f32(x), ew)
+    assert_close(f32(y), ref, max_abs=2e-2 * max(1.0, float(np.abs(ref).max())), what="dense y")
+    assert ops.device_status(reset=True) == 0
+
+
 def test_glu_skips_missing_slots():
     cfg = LayerConfig("t", 9, 256, 4, 1, 128, None, 8, 4)
     block, _ = make_layer(cfg, device=DEV)
