@@ -37,6 +37,14 @@ enum sg_status {
   SG_ERR_TIMEOUT = -6,       /* a bounded wait gave up */
 };
 
+/* Row order flags of sg_glu_gate_up / sg_glu_down.  Pair order: row p of the
+ * pair index p = t * k + j (h, y; x is indexed by p / pair_div).  Dispatch
+ * order: row pos of the sg_dispatch permutation (pairs grouped by expert). */
+enum sg_glu_flags {
+  SG_IN_DISPATCH_ORDER = 1,   /* input rows are in dispatch order (num_pairs rows) */
+  SG_OUT_DISPATCH_ORDER = 2,  /* write output rows in dispatch order */
+};
+
 /* Human-readable text of a status code (static storage). */
 const char* sg_status_string(int status);
 
@@ -98,28 +106,48 @@ int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
                 int32_t* perm, int max_unique, void* stream);
 
 /* ------------------------------------------------- gathered SwiGLU (a9/a10)
- * h[p, I] = swiglu(x[p / pair_div] @ gate^T, ... @ up^T) for every pair p of
- * every group u < counts[0], against arena slot slot_ids[u]; pairs listed by
- * perm/group_off (sg_dispatch layout); num_pairs = P (length of perm, rows of
- * h; x has ceil(P / pair_div) rows).  Runs on the tcgen05 tensor-core kernel
- * or the streaming GEMV (see sg_set_glu_path).  Rounds x_up, x_gate, sigmoid, silu and
- * the product to bf16 (experts.py:26-28).  pair_div = k for routed experts,
- * 1 when pairs are tokens (the shared expert).  grid_groups is a host-side
- * upper bound on counts[0].
- * Replaces the up/gate `gather_mm` calls and `swiglu_activation` in
- * `_gather_forward`, qwen3_x_moe.py:225-242.
+ * y[p, H] = bf16(swiglu(x[p / pair_div] @ gate^T, ... @ up^T) @ down^T) for
+ * every pair p of every group u < counts[0], against arena slot slot_ids[u];
+ * pairs listed by perm/group_off (sg_dispatch layout); num_pairs = P (length
+ * of perm, rows of y; x has ceil(P / pair_div) rows); y in pair order.
+ * xs [P, H] and h [P, I] are caller-provided intermediate storage (xs is
+ * written only when sg_glu_use_permute says so: the pairs' token rows are
+ * first copied into dispatch order, so that every tile's rows load as one
+ * TMA box; h is kept in dispatch order).  pair_div = k for routed experts.
+ * grid_groups is a host-side upper bound on counts[0].
+ * Replaces `_gather_forward`, qwen3_x_moe.py:210-248 (the `mx.take` of the
+ * arena, two `gather_mm` + `swiglu_activation`, the down `gather_mm`). */
+int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                   const int32_t* counts, const int32_t* slot_ids,
+                   const int32_t* group_off, const int32_t* perm,
+                   int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y, void* stream);
+
+/* 1 when sg_glu_forward permutes the token rows for this problem size. */
+int sg_glu_use_permute(const sg_arena* arena, int num_pairs, int grid_groups);
+
+/* xs[pos, :] = x[perm[pos] / pair_div, :] for pos < num_pairs (H % 8 == 0). */
+int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_div, int num_pairs, int H,
+                    uint16_t* xs, void* stream);
+
+/* The two halves of sg_glu_forward.  h[., I] = swiglu(x @ gate^T, x @ up^T)
+ * per pair; rows in pair or dispatch order per `flags` (sg_glu_flags; input
+ * in dispatch order means x has num_pairs rows and pair_div is not used).
+ * Rounds x_up, x_gate, sigmoid, silu and the product to bf16
+ * (experts.py:26-28).  Replaces the up/gate `gather_mm` calls and
+ * `swiglu_activation` in `_gather_forward`, qwen3_x_moe.py:225-242.
  * Requires H % 64 == 0 and I % 64 == 0. */
 int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                    const int32_t* counts, const int32_t* slot_ids,
                    const int32_t* group_off, const int32_t* perm,
-                   int grid_groups, uint16_t* h, void* stream);
+                   int grid_groups, uint16_t* h, int flags, void* stream);
 
-/* y[p, H] = bf16(h[p, I] @ down^T) for every listed pair (num_pairs rows).
- * Replaces the down `gather_mm` in `_gather_forward`, qwen3_x_moe.py:243-248. */
+/* y[., H] = bf16(h[., I] @ down^T) for every listed pair (num_pairs rows),
+ * orders per `flags`.  Replaces the down `gather_mm` in `_gather_forward`,
+ * qwen3_x_moe.py:243-248. */
 int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs,
                 const int32_t* counts, const int32_t* slot_ids,
                 const int32_t* group_off, const int32_t* perm,
-                int grid_groups, uint16_t* y, void* stream);
+                int grid_groups, uint16_t* y, int flags, void* stream);
 
 /* Dense SwiGLU of one slot over every row: h[t, I] = swiglu(x @ gate^T, x @ up^T),
  * y[t, H] = bf16(h @ down^T) for t < T, slot sid of the arena (the shared
@@ -131,10 +159,12 @@ int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs,
 int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint16_t* h, uint16_t* y,
                  void* stream);
 
-/* Kernel choice for sg_glu_gate_up / sg_glu_down: 0 = automatic (tcgen05 when
- * the mean pairs per group is >= 2 and the shape allows: in-dim % 64, out-dim
- * % 128, <= 2048 groups), 1 = streaming GEMV always, 2 = tcgen05 whenever the
- * shape allows.  Process-wide.  No counterpart in the reference (MLX picks
+/* Kernel choice for sg_glu_forward / sg_glu_gate_up / sg_glu_down: 0 =
+ * automatic (tcgen05 when the mean pairs per group is >= 2 and the shape
+ * allows: in-dim % 64, out-dim % 128, <= 2048 groups; token rows permuted
+ * once the mean reaches 32), 1 = streaming GEMV always, 2 = tcgen05 whenever
+ * the shape allows, 3 = as 2 with the token rows always permuted.
+ * Process-wide.  No counterpart in the reference (MLX picks
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);
 

@@ -140,7 +140,7 @@ template <int BITS, bool DUAL>
 __global__ void __launch_bounds__(GW_WARPS * 32)
 gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, const int32_t* __restrict__ counts,
                 const int32_t* __restrict__ slot_ids, const int32_t* __restrict__ group_off,
-                const int32_t* __restrict__ perm, uint16_t* __restrict__ out) {
+                const int32_t* __restrict__ perm, uint16_t* __restrict__ out, int in_by_pos, int out_by_pos) {
   constexpr int WROWS = 4;                        // weight rows per warp
   constexpr int OROWS = DUAL ? WROWS / 2 : WROWS;  // output rows per warp
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -180,7 +180,7 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
       int b = c / cpr, cc = c - b * cpr;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (b < nb) {
-        int row = perm[p0 + b] / pair_div;
+        int row = in_by_pos ? p0 + b : perm[p0 + b] / pair_div;
         v = reinterpret_cast<const uint4*>(xin + (size_t)row * K)[cc];
       }
       reinterpret_cast<uint4*>(xs)[c] = v;
@@ -209,13 +209,13 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
           float g = warp_fold_sum(acc[o][b]);
           float up = warp_fold_sum(acc[o + OROWS][b]);
           if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
-            const int p = perm[p0 + b];
+            const int p = out_by_pos ? p0 + b : perm[p0 + b];
             out[(size_t)p * OUT + r] = slot_ok ? swiglu_bf16(g, up) : (uint16_t)0;
           }
         } else {
           float y = warp_fold_sum(acc[o][b]);
           if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
-            const int p = perm[p0 + b];
+            const int p = out_by_pos ? p0 + b : perm[p0 + b];
             out[(size_t)p * OUT + r] = slot_ok ? f32_to_bf16(y) : (uint16_t)0;
           }
         }
@@ -227,7 +227,7 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
 template <int BITS, bool DUAL>
 static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
                        const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
-                       uint16_t* out, cudaStream_t s) {
+                       uint16_t* out, int in_by_pos, int out_by_pos, cudaStream_t s) {
   const int K = DUAL ? A->hidden : A->inter;
   const int OUT = DUAL ? A->inter : A->hidden;
   const int orows_cta = GW_WARPS * (DUAL ? 2 : 4);
@@ -240,7 +240,7 @@ static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, con
   }
   dim3 grid((OUT + orows_cta - 1) / orows_cta, grid_groups);
   gemv_glu_kernel<BITS, DUAL><<<grid, GW_WARPS * 32, smem, s>>>(*A, xin, pair_div, counts, slot_ids, group_off,
-                                                                 perm, out);
+                                                                 perm, out, in_by_pos, out_by_pos);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -266,62 +266,142 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
                   const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
 int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
                     cudaStream_t s);
-static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05
+static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05, 3 tcgen05 over permuted rows
 
 // auto: the tensor-core path once the mean pairs per group reaches 2
 static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || !tc_supported(A, dual, grid_groups)) return false;
-  if (g_glu_path == 2) return true;
+  if (g_glu_path >= 2) return true;
   return P >= 2 * grid_groups;
+}
+
+// Whether sg_glu_forward first copies the pairs' token rows into dispatch
+// order: worth it once a group's pairs fill 64-wide tiles (a contiguous
+// tile of rows then loads with one TMA box per stage).
+static bool use_permute(const sg_arena* A, int P, int grid_groups) {
+  if (!use_tc(A, true, P, grid_groups) || !use_tc(A, false, P, grid_groups)) return false;
+  if (g_glu_path == 3) return true;
+  return P >= 32 * grid_groups;
+}
+
+// xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
+__global__ void __launch_bounds__(256)
+permute_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int pair_div, int P, int H,
+                    uint16_t* __restrict__ xs) {
+  const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pos >= P) return;
+  const int row = perm[pos] / pair_div;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)pos * H);
+  for (int c = threadIdx.x & 31; c < H / 8; c += 32) dst[c] = ldg_nc_v4(src + c);
+}
+
+static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div, const int32_t* counts,
+                    const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                    uint16_t* h, int flags, cudaStream_t s) {
+  const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
+  const int div = in_pos ? 1 : pair_div;
+  if (use_tc(arena, true, num_pairs, grid_groups)) {
+    const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
+    return tc_glu_launch(arena, true, x, in_rows, div, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
+                         grid_groups, h, s);
+  }
+  switch (arena->bits) {
+    case 16: return launch_gemv<16, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
+    case 8: return launch_gemv<8, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
+    default: return launch_gemv<4, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
+  }
+}
+
+static int glu_single(const sg_arena* arena, const uint16_t* h, int num_pairs, const int32_t* counts,
+                      const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                      uint16_t* y, int flags, cudaStream_t s) {
+  const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
+  if (use_tc(arena, false, num_pairs, grid_groups))
+    return tc_glu_launch(arena, false, h, num_pairs, 1, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
+                         grid_groups, y, s);
+  switch (arena->bits) {
+    case 16: return launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
+    case 8: return launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
+    default: return launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
+  }
+}
+
+static int check_glu_args(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups, int flags) {
+  int st = check_arena(arena);
+  if (st) return st;
+  if (num_pairs < 0 || pair_div < 1 || grid_groups < 0) return SG_ERR_INVALID_ARG;
+  if (flags & ~(SG_IN_DISPATCH_ORDER | SG_OUT_DISPATCH_ORDER)) return SG_ERR_INVALID_ARG;
+  if (grid_groups > 65535) return SG_ERR_SHAPE;
+  return SG_OK;
 }
 }  // namespace sg
 
 extern "C" int sg_set_glu_path(int mode) {
-  if (mode < 0 || mode > 2) return SG_ERR_INVALID_ARG;
+  if (mode < 0 || mode > 3) return SG_ERR_INVALID_ARG;
   sg::g_glu_path = mode;
+  return SG_OK;
+}
+
+extern "C" int sg_glu_use_permute(const sg_arena* arena, int num_pairs, int grid_groups) {
+  if (sg::check_arena(arena) || num_pairs <= 0 || grid_groups <= 0) return 0;
+  return sg::use_permute(arena, num_pairs, grid_groups) ? 1 : 0;
+}
+
+extern "C" int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_div, int num_pairs, int H,
+                               uint16_t* xs, void* stream) {
+  if (num_pairs < 0 || pair_div < 1 || H < 8 || H % 8) return num_pairs < 0 || pair_div < 1 ? SG_ERR_INVALID_ARG
+                                                                                            : SG_ERR_SHAPE;
+  if (num_pairs == 0) return SG_OK;
+  if (!x || !perm || !xs) return SG_ERR_INVALID_ARG;
+  sg::permute_rows_kernel<<<(num_pairs + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, perm, pair_div, num_pairs, H, xs);
+  SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
 extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                               const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                              const int32_t* perm, int grid_groups, uint16_t* h, void* stream) {
-  int st = sg::check_arena(arena);
+                              const int32_t* perm, int grid_groups, uint16_t* h, int flags, void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, flags);
   if (st) return st;
-  if (num_pairs < 0 || pair_div < 1 || grid_groups < 0) return SG_ERR_INVALID_ARG;
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!x || !counts || !slot_ids || !group_off || !perm || !h) return SG_ERR_INVALID_ARG;
-  if (grid_groups > 65535) return SG_ERR_SHAPE;
-  cudaStream_t s = (cudaStream_t)stream;
-  if (sg::use_tc(arena, true, num_pairs, grid_groups)) {
-    const int in_rows = (num_pairs + pair_div - 1) / pair_div;
-    return sg::tc_glu_launch(arena, true, x, in_rows, pair_div, 0, 0, num_pairs, counts, slot_ids, group_off, perm,
-                             grid_groups, h, s);
-  }
-  switch (arena->bits) {
-    case 16: return sg::launch_gemv<16, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
-    case 8: return sg::launch_gemv<8, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
-    default: return sg::launch_gemv<4, true>(arena, x, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, s);
-  }
+  return sg::glu_dual(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, flags,
+                      (cudaStream_t)stream);
 }
 
 extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs, const int32_t* counts,
                            const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
-                           uint16_t* y, void* stream) {
-  int st = sg::check_arena(arena);
+                           uint16_t* y, int flags, void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, 1, grid_groups, flags);
   if (st) return st;
-  if (num_pairs < 0 || grid_groups < 0) return SG_ERR_INVALID_ARG;
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!h || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
-  if (grid_groups > 65535) return SG_ERR_SHAPE;
+  return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, flags,
+                        (cudaStream_t)stream);
+}
+
+extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                              const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                              const int32_t* perm, int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y,
+                              void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
+  if (st) return st;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!x || !counts || !slot_ids || !group_off || !perm || !h || !y) return SG_ERR_INVALID_ARG;
   cudaStream_t s = (cudaStream_t)stream;
-  if (sg::use_tc(arena, false, num_pairs, grid_groups))
-    return sg::tc_glu_launch(arena, false, h, num_pairs, 1, 0, 0, num_pairs, counts, slot_ids, group_off, perm,
-                             grid_groups, y, s);
-  switch (arena->bits) {
-    case 16: return sg::launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
-    case 8: return sg::launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
-    default: return sg::launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, s);
+  const bool permute = sg::use_permute(arena, num_pairs, grid_groups);
+  if (permute) {
+    if (!xs) return SG_ERR_INVALID_ARG;
+    st = sg_permute_rows(x, perm, pair_div, num_pairs, arena->hidden, xs, stream);
+    if (st) return st;
   }
+  // h in dispatch order, so that the down projection's rows are contiguous
+  st = sg::glu_dual(arena, permute ? xs : x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h,
+                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s);
+  if (st) return st;
+  return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, SG_IN_DISPATCH_ORDER,
+                        s);
 }
 
 extern "C" int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint16_t* h, uint16_t* y,

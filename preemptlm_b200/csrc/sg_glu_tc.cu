@@ -752,7 +752,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < C::SB; ++i) {
-      mbar_init(&b_full[i], args.dense_rows > 0 ? 1 : 32);  // TMA tx, or one cp.async arrival per producer lane
+      mbar_init(&b_full[i], args.in_by_pos ? 1 : 32);  // TMA tx, or one cp.async arrival per producer lane
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < C::SP; ++i) {
@@ -903,9 +903,11 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------------- B row producer
-    if (args.dense_rows > 0) {
-      // dense mode: the tile's rows are contiguous, one TMA box (BN rows x
-      // 128 bytes, SW128, zero fill past the last row) per operand stage
+    if (args.in_by_pos) {
+      // B rows in dispatch order (dense mode, or rows permuted beforehand):
+      // a tile's rows are contiguous, one TMA box (BN rows x 128 bytes, SW128,
+      // zero fill past the last row) per operand stage; rows past the group's
+      // pairs are read but their results are never written
       if (lane == 0) {
         int sb = 0, issued = 0;
         uint32_t pb = 0;
@@ -918,7 +920,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             const int nsub = min(C::KBB, NKB - kb0);
             mbar_expect_tx(&b_full[sb], nsub * C::B_SUB);
             for (int j = 0; j < nsub; ++j)
-              tma_load_2d(sB + sb * C::B_BYTES + j * C::B_SUB, &tmB, (kb0 + j) * BK, tl.n0, &b_full[sb]);
+              tma_load_2d(sB + sb * C::B_BYTES + j * C::B_SUB, &tmB, (kb0 + j) * BK, tl.goff + tl.n0, &b_full[sb]);
             ++issued;
             if (++sb == C::SB) { sb = 0; pb ^= 1; }
           }
@@ -1173,8 +1175,8 @@ static int launch_cfg(const sg_arena* A, const Args& args_in, cudaStream_t s) {
     ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
          make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   }
-  // B rows (dense mode): [in_rows, K] bf16, box BN rows x 64 columns
-  if (args.dense_rows > 0)
+  // B rows in dispatch order: [in_rows, K] bf16, box BN rows x 64 columns
+  if (args.in_by_pos)
     ok = ok && make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.in, K, (uint64_t)args.in_rows, BK, BN,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   else

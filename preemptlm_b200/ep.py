@@ -69,18 +69,9 @@ class CudaBackend:
 
     def experts(self, rows: torch.Tensor, local_eids: torch.Tensor) -> torch.Tensor:
         d = ops.dispatch(local_eids, self.arena.num_slots, self.ident)
-        if self.timing is None:
-            h = ops.glu_gate_up(self.arena, rows, d, pair_div=1)
-            return ops.glu_down(self.arena, h, d)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        ev[0].record()
-        h = ops.glu_gate_up(self.arena, rows, d, pair_div=1)
-        ev[1].record()
-        y = ops.glu_down(self.arena, h, d)
-        ev[2].record()
-        self.timing.setdefault("events", []).append(ev)
-        self.timing.setdefault("dispatch", []).append(d)
-        self.timing.setdefault("rows", []).append(rows.shape[0])
+        y = ops.gather_forward(self.arena, rows, d, 1, timing=self.timing)
+        if self.timing is not None:
+            self.timing.setdefault("rows", []).append(rows.shape[0])
         return y
 
     def shared_terms(self, x: torch.Tensor):

@@ -213,8 +213,7 @@ class Qwen3_xMoEWrapper(SlotTable):
 
     # ------------------------------------------------------------------ forward
     def _gather_forward_dispatched(self, x2: torch.Tensor, d: ops.Dispatch, arena: SlottedGLU) -> torch.Tensor:
-        h = ops.glu_gate_up(arena, x2, d, pair_div=self.inner.top_k)
-        return ops.glu_down(arena, h, d)
+        return ops.gather_forward(arena, x2, d, self.inner.top_k)
 
     def _gather_forward(self, x, gate_proj, up_proj, down_proj, slot_idxs, inverse_map):
         """qwen3_x_moe.py:210-248: pair p = t*k + j runs expert slot
@@ -279,17 +278,7 @@ class Qwen3_xMoEWrapper(SlotTable):
             shared_gate = ops.router_linear(x2, self.inner.shared_expert_gate)
         d = ops.dispatch(inds, self.num_experts, self._identity)
         arena = self.inner.switch_mlp
-        if timing is None:
-            y = self._gather_forward_dispatched(x2, d, arena)
-        else:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-            ev[0].record()
-            h = ops.glu_gate_up(arena, x2, d, pair_div=self.inner.top_k)
-            ev[1].record()
-            y = ops.glu_down(arena, h, d)
-            ev[2].record()
-            timing.setdefault("events", []).append(ev)
-            timing.setdefault("dispatch", []).append(d)
+        y = ops.gather_forward(arena, x2, d, self.inner.top_k, timing=timing)
         return ops.combine(y, scores, shared_y, None if shared_gate is None else shared_gate.reshape(-1))
 
     # ------------------------------------------------------------------ factory

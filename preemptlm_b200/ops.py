@@ -120,8 +120,9 @@ def _make_token_dispatch(T: int, dev) -> Dispatch:
     )
 
 
-def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
-    """h[p] = swiglu over the arena (``sg_glu_gate_up``)."""
+def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int = 0) -> torch.Tensor:
+    """h = swiglu over the arena (``sg_glu_gate_up``); rows in pair order
+    unless ``flags`` (SG_IN/OUT_DISPATCH_ORDER) say otherwise."""
     x = _bf16_2d(x, "x")
     P = d.perm.numel()
     h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
@@ -131,12 +132,12 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Ten
     lib = _abi.load()
     _abi.check(lib.sg_glu_gate_up(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                   d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
-                                  h.data_ptr(), _stream()), "sg_glu_gate_up")
+                                  h.data_ptr(), int(flags), _stream()), "sg_glu_gate_up")
     return h
 
 
-def glu_down(arena, h: torch.Tensor, d: Dispatch) -> torch.Tensor:
-    """y[p] = h[p] @ down^T over the arena (``sg_glu_down``)."""
+def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0) -> torch.Tensor:
+    """y = h @ down^T over the arena (``sg_glu_down``)."""
     h = _bf16_2d(h, "h")
     P = d.perm.numel()
     y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=h.device)
@@ -145,8 +146,54 @@ def glu_down(arena, h: torch.Tensor, d: Dispatch) -> torch.Tensor:
     LAUNCHES[0] += 1
     lib = _abi.load()
     _abi.check(lib.sg_glu_down(ctypes.byref(arena.desc()), h.data_ptr(), P, d.counts.data_ptr(), d.slot_ids.data_ptr(),
-                               d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),
-               "sg_glu_down")
+                               d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(), int(flags),
+                               _stream()), "sg_glu_down")
+    return y
+
+
+def permute_rows(x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
+    """xs[pos] = x[perm[pos] // pair_div] (``sg_permute_rows``)."""
+    x = _bf16_2d(x, "x")
+    P = d.perm.numel()
+    xs = torch.empty((P, x.shape[1]), dtype=torch.bfloat16, device=x.device)
+    if P:
+        LAUNCHES[0] += 1
+        _abi.check(_abi.load().sg_permute_rows(x.data_ptr(), d.perm.data_ptr(), int(pair_div), P, x.shape[1],
+                                               xs.data_ptr(), _stream()), "sg_permute_rows")
+    return xs
+
+
+def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: dict | None = None) -> torch.Tensor:
+    """y[p] = down(swiglu(gate(x[p // pair_div]), up(...))) for every pair, in
+    pair order: the reference's ``_gather_forward`` (``sg_glu_forward``).
+    With ``timing``, the same kernels run as separate calls with CUDA events
+    around the gate/up and down launches (per-kernel timing)."""
+    x = _bf16_2d(x, "x")
+    P = d.perm.numel()
+    lib = _abi.load()
+    if timing is None:
+        y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device)
+        if P == 0:
+            return y
+        h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
+        permute = lib.sg_glu_use_permute(ctypes.byref(arena.desc()), P, d.grid_groups) == 1
+        xs = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device) if permute else None
+        LAUNCHES[0] += 3 if permute else 2
+        _abi.check(lib.sg_glu_forward(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
+                                      d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
+                                      None if xs is None else xs.data_ptr(), h.data_ptr(), y.data_ptr(), _stream()),
+                   "sg_glu_forward")
+        return y
+    permute = P > 0 and lib.sg_glu_use_permute(ctypes.byref(arena.desc()), P, d.grid_groups) == 1
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    src, fl = (permute_rows(x, d, pair_div), _abi.SG_IN_DISPATCH_ORDER) if permute else (x, 0)
+    ev[0].record()
+    h = glu_gate_up(arena, src, d, pair_div, fl | _abi.SG_OUT_DISPATCH_ORDER)
+    ev[1].record()
+    y = glu_down(arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
+    ev[2].record()
+    timing.setdefault("events", []).append(ev)
+    timing.setdefault("dispatch", []).append(d)
     return y
 
 
@@ -171,7 +218,7 @@ def dense_glu(arena, x: torch.Tensor, sid: int = 0) -> torch.Tensor | None:
     return y
 
 
-GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2}
+GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2, "tc-perm": 3}
 
 
 _GLU_PATH = ["auto"]

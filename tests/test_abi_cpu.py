@@ -61,13 +61,19 @@ def test_host_side_argument_checks(lib):
     assert lib.sg_dispatch(1, 8, 9000, 1, 1, 1, 1, 1, 1, 1, 1, 100, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_dispatch(1, 8, 64, 1, 1, 1, 1, 1, 1, 1, 1, 4, None) == _abi.SG_ERR_CAPACITY
     a = _abi.sg_arena(num_slots=4, hidden=2048, inter=512, bits=5, group_size=64, gate_w=1, up_w=1, down_w=1)
-    assert lib.sg_glu_gate_up(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_FORMAT
+    assert lib.sg_glu_gate_up(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 1, 0, None) == _abi.SG_ERR_FORMAT
     a.bits = 8
     a.group_size = 32
-    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_FORMAT
+    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 0, None) == _abi.SG_ERR_FORMAT
     a.bits, a.group_size, a.hidden = 16, 64, 100
-    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, None) == _abi.SG_ERR_SHAPE
-    assert lib.sg_set_glu_path(3) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 0, None) == _abi.SG_ERR_SHAPE
+    a.hidden = 2048
+    assert lib.sg_glu_down(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 4, None) == _abi.SG_ERR_INVALID_ARG  # flag
+    assert lib.sg_glu_forward(ctypes.byref(a), None, 0, 1, None, None, None, None, 1, None, None, None,
+                              None) == _abi.SG_OK  # empty
+    assert lib.sg_permute_rows(1, 1, 1, 4, 12, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_permute_rows(1, 1, 0, 4, 16, 1, None) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_set_glu_path(4) == _abi.SG_ERR_INVALID_ARG
     a = _abi.sg_arena(num_slots=2, hidden=1024, inter=512, bits=8, group_size=64, gate_w=1, up_w=1, down_w=1,
                       gate_s=1, gate_b=1, up_s=1, up_b=1, down_s=1, down_b=1)
     assert lib.sg_dense_glu(ctypes.byref(a), 2, 1, 4, 1, 1, None) == _abi.SG_ERR_INVALID_ARG  # slot out of range

@@ -111,7 +111,7 @@ def glu_path(request):
     assert ops.device_status(reset=True) == 0  # no kernel gave up on a bounded wait
 
 
-@pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
+@pytest.mark.parametrize("glu_path", ["gemv", "tc", "tc-perm"], indirect=True)
 @pytest.mark.parametrize("bits", [16, 8, 4])
 @pytest.mark.parametrize("H,I,E,T,k", [(256, 128, 8, 5, 2), (2048, 768, 16, 33, 4), (1024, 512, 6, 1, 6),
                                        (512, 256, 4, 300, 2),
@@ -148,6 +148,9 @@ def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     hdev = f32(h)
     ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
     assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what="y|h")
+    # the fused call (h kept in dispatch order, token rows permuted first under
+    # "tc-perm"): the same kernels' arithmetic, so the same bits
+    assert torch.equal(ops.gather_forward(block.switch_mlp, x, d, k), y)
 
 
 @pytest.mark.parametrize("bits", [16, 8, 4])
