@@ -718,7 +718,10 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
               const __grid_constant__ CUtensorMap tmQ1, const Args args) {
   using C = Cfg<BITS, DUAL, BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the shared array, so that
+  // every derived pointer stays a shared-memory pointer (ld/st.shared rather
+  // than generic accesses)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem + C::OFF_A;
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sP = smem + C::OFF_P;
