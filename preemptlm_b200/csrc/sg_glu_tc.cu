@@ -53,8 +53,13 @@ __host__ __device__ constexpr int pow2ceil(int v) {
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
-template <int BITS, bool DUAL, int BN>
+// MODE 0: down projection, one 128-row weight tile; 1: gate/up, two matrices
+// and the SwiGLU epilogue; 2: down projection, two 128-row halves of a 256-row
+// weight tile sharing the B rows (twice the bytes per pipeline stage).
+template <int BITS, int MODE, int BN>
 struct Cfg {
+  static constexpr bool DUAL = MODE != 0;  // two A matrices per stage
+  static constexpr int ROWS = MODE == 2 ? 2 * BM : BM;  // weight rows per tile
   static constexpr int NMAT = DUAL ? 2 : 1;
   // ATM: dequantised A tiles live in tensor memory (tcgen05.st by the
   // dequantisers, read by tcgen05.mma), sparing shared-memory bandwidth;
@@ -526,13 +531,14 @@ struct ScaleVec<1> {
 
 // STMA: scales and biases come from the TMA-staged chunk ring in shared
 // memory (8 groups per chunk) instead of per-thread global loads.
-template <int BITS, bool DUAL, int BN, int V, bool STMA>
+template <int BITS, int MODE, int BN, int V, bool STMA>
 __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, int U, int NT, int total,
                                              uint8_t* sA, const uint8_t* sP, uint64_t* a_full, uint64_t* a_empty,
                                              uint64_t* p_full, uint64_t* p_empty, Ctl ctl, uint32_t tmem_a,
                                              const int* gtab, const int* stab, const uint8_t* sS,
                                              uint64_t* s_full, uint64_t* s_empty) {
-  using C = Cfg<BITS, DUAL, BN>;
+  using C = Cfg<BITS, MODE, BN>;
+  constexpr bool DUAL = C::DUAL;
   // row r = 32 (warp % 4) + lane: the TMEM lane quadrant this warp may write
   const int warp = threadIdx.x >> 5;
   const int r = 32 * (warp & 3) + (threadIdx.x & 31);
@@ -547,7 +553,7 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
   auto row_ptrs = [&](int t, const uint16_t*& sp, const uint16_t*& bp, bool& sok) {
     const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
     sok = tl.slot >= 0 && tl.slot < args.num_slots;
-    const size_t row = sok ? (size_t)tl.slot * args.OUT + tl.m * BM + r : 0;
+    const size_t row = sok ? (size_t)tl.slot * args.OUT + tl.m * C::ROWS + (MODE == 2 ? mat * BM : 0) + r : 0;
     sp = sbase + row * groups;
     bp = bbase + row * groups;
   };
@@ -710,13 +716,15 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
   }
 }
 
-template <int BITS, bool DUAL, int BN, bool STMA>
-__global__ void __launch_bounds__(Cfg<BITS, DUAL, BN>::THREADS, 1)
+template <int BITS, int MODE, int BN, bool STMA>
+__global__ void __launch_bounds__(Cfg<BITS, MODE, BN>::THREADS, 1)
 glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS0,
               const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__ CUtensorMap tmS1,
               const __grid_constant__ CUtensorMap tmQ1, const Args args) {
-  using C = Cfg<BITS, DUAL, BN>;
+  using C = Cfg<BITS, MODE, BN>;
+  constexpr bool DUAL = C::DUAL;
+  constexpr int RO1 = MODE == 2 ? BM : 0;  // row offset of the second matrix
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base by pointer arithmetic on the shared array, so that
   // every derived pointer stays a shared-memory pointer (ld/st.shared rather
@@ -747,7 +755,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = args.K;
   const int NKB = K / BK;
-  const int MT = args.OUT / BM;
+  const int MT = args.OUT / C::ROWS;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::SA; ++i) {
@@ -833,13 +841,14 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         const Tile tn = tile_of<BN>(tt, plan, U, NT, args, gtab, stab);
         if (tn.slot < 0 || tn.slot >= args.num_slots) return;
         const int groups = K / 64;
-        const size_t off = ((size_t)tn.slot * args.OUT + (size_t)tn.m * BM) * groups;
+        const size_t off = ((size_t)tn.slot * args.OUT + (size_t)tn.m * C::ROWS) * groups;
+        const size_t off1 = off + (size_t)RO1 * groups;
         const uint32_t bytes = BM * groups * 2;
         prefetch_l2(args.s0 + off, bytes);
         prefetch_l2(args.b0 + off, bytes);
         if (DUAL) {
-          prefetch_l2(args.s1 + off, bytes);
-          prefetch_l2(args.b1 + off, bytes);
+          prefetch_l2(args.s1 + off1, bytes);
+          prefetch_l2(args.b1 + off1, bytes);
         }
       };
       prefetch_scales(blockIdx.x);
@@ -848,7 +857,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
         prefetch_scales(t + gridDim.x);
-        const int row0 = tl.slot * args.OUT + tl.m * BM;
+        const int row0 = tl.slot * args.OUT + tl.m * C::ROWS;
         const int nstage = BITS == 16 ? NKB : (NKB + C::KP - 1) / C::KP;
         for (int kb = 0; kb < nstage; ++kb) {
           if (STMA && (kb * C::KP) % 8 == 0) {
@@ -861,8 +870,8 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             tma_load_2d(dst, &tmS0, kb * C::KP, row0, &s_full[ss]);
             tma_load_2d(dst + BM * 16, &tmQ0, kb * C::KP, row0, &s_full[ss]);
             if (DUAL) {
-              tma_load_2d(dst + 2 * BM * 16, &tmS1, kb * C::KP, row0, &s_full[ss]);
-              tma_load_2d(dst + 3 * BM * 16, &tmQ1, kb * C::KP, row0, &s_full[ss]);
+              tma_load_2d(dst + 2 * BM * 16, &tmS1, kb * C::KP, row0 + RO1, &s_full[ss]);
+              tma_load_2d(dst + 3 * BM * 16, &tmQ1, kb * C::KP, row0 + RO1, &s_full[ss]);
             }
             ++s_issued;
             if (++ss == C::SS) { ss = 0; sph ^= 1; }
@@ -872,14 +881,14 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           if (BITS == 16) {
             mbar_expect_tx(&full[s_i], C::A_BYTES);
             tma_load_2d(sA + s_i * C::A_BYTES, &tmA0, kb * BK, row0, &full[s_i]);
-            if (DUAL) tma_load_2d(sA + s_i * C::A_BYTES + C::A_MAT, &tmA1, kb * BK, row0, &full[s_i]);
+            if (DUAL) tma_load_2d(sA + s_i * C::A_BYTES + C::A_MAT, &tmA1, kb * BK, row0 + RO1, &full[s_i]);
           } else {
             // 128 bytes of every row: columns beyond the row end are the TMA's
             // zero fill and are never dequantised
             mbar_expect_tx(&full[s_i], C::P_BYTES);
             const int col = kb * 32;  // packed uint32 column (32 words = 128 bytes)
             tma_load_2d(sP + s_i * C::P_BYTES, &tmA0, col, row0, &full[s_i]);
-            if (DUAL) tma_load_2d(sP + s_i * C::P_BYTES + C::P_MAT, &tmA1, col, row0, &full[s_i]);
+            if (DUAL) tma_load_2d(sP + s_i * C::P_BYTES + C::P_MAT, &tmA1, col, row0 + RO1, &full[s_i]);
           }
           ++issued;
           if (++s_i == RING) { s_i = 0; ph ^= 1; }
@@ -1048,13 +1057,13 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     // ---------------------------------------------------------------- dequantisers
     if (BITS != 16) {
       if constexpr (STMA)
-        dequant_role<BITS, DUAL, BN, 1, true>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+        dequant_role<BITS, MODE, BN, 1, true>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
                                               ctl, tmem, gtab, stab, sS, s_full, s_empty);
       else if ((K / 64) % 4 == 0)
-        dequant_role<BITS, DUAL, BN, 4, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+        dequant_role<BITS, MODE, BN, 4, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
                                                ctl, tmem, gtab, stab, sS, s_full, s_empty);
       else
-        dequant_role<BITS, DUAL, BN, 1, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+        dequant_role<BITS, MODE, BN, 1, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
                                                ctl, tmem, gtab, stab, sS, s_full, s_empty);
     }
   } else {
@@ -1073,7 +1082,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       tc_fence_after();
       const bool slot_ok = tl.slot >= 0 && tl.slot < args.num_slots;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + ab * C::ACC_COLS;
-      const int ocol = tl.m * BM + r;
+      const int ocol = tl.m * C::ROWS + r;
 #pragma unroll 1
       for (int j0 = 0; j0 < BN; j0 += 32) {
         // output rows of pairs j0 .. j0+31, one per lane, broadcast by shuffle
@@ -1097,9 +1106,11 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             if (jb + jj < tl.nvalid) {
               uint16_t v;
               if (!slot_ok) v = 0;
-              else if (DUAL) v = swiglu_bf16(__uint_as_float(g[jj]), __uint_as_float(u[jj]));
+              else if (MODE == 1) v = swiglu_bf16(__uint_as_float(g[jj]), __uint_as_float(u[jj]));
               else v = f32_to_bf16(__uint_as_float(g[jj]));
               args.out[(size_t)orow * args.OUT + ocol] = v;
+              if (MODE == 2)  // the second 128-row half of the tile
+                args.out[(size_t)orow * args.OUT + ocol + BM] = slot_ok ? f32_to_bf16(__uint_as_float(u[jj])) : 0;
             }
           }
         }
@@ -1160,15 +1171,16 @@ static int num_sms() {
   return n;
 }
 
-template <int BITS, bool DUAL, int BN>
+template <int BITS, int MODE, int BN>
 static int launch_cfg(const sg_arena* A, const Args& args_in, cudaStream_t s) {
-  using C = Cfg<BITS, DUAL, BN>;
+  using C = Cfg<BITS, MODE, BN>;
+  constexpr bool DUAL = C::DUAL;
   Args args = args_in;
   const int K = args.K, OUT = args.OUT;
   const uint64_t rows_total = (uint64_t)A->num_slots * OUT;
   CUtensorMap m0, m1, mb, ms0, mq0, ms1, mq1;
-  const void* w0 = DUAL ? A->gate_w : A->down_w;
-  const void* w1 = DUAL ? A->up_w : A->down_w;
+  const void* w0 = MODE == 1 ? A->gate_w : A->down_w;
+  const void* w1 = MODE == 1 ? A->up_w : A->down_w;
   bool ok;
   if (BITS == 16) {
     ok = make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w0, K, rows_total, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
@@ -1208,32 +1220,50 @@ static int launch_cfg(const sg_arena* A, const Args& args_in, cudaStream_t s) {
   SG_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
   if (!attr_done[dev]) {
-    SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN, false>,
+    SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, MODE, BN, false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     if constexpr (C::SS > 0)
-      SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, DUAL, BN, true>,
+      SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, MODE, BN, true>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done[dev] = true;
   }
+  int grid = num_sms();
+  if (args.dense_rows > 0) {  // the tile count is known on the host: no idle CTAs
+    const int tiles = (args.OUT / C::ROWS) * ((args.dense_rows + BN - 1) / BN);
+    grid = tiles < grid ? tiles : grid;
+  }
   if constexpr (C::SS > 0) {
     if (scale_tma) {
-      glu_tc_kernel<BITS, DUAL, BN, true><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
+      glu_tc_kernel<BITS, MODE, BN, true><<<grid, C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
       SG_LAUNCH_CHECK();
       return SG_OK;
     }
   }
-  glu_tc_kernel<BITS, DUAL, BN, false><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
+  glu_tc_kernel<BITS, MODE, BN, false><<<grid, C::THREADS, C::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1, args);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
-template <int BITS, bool DUAL>
+template <int BITS, int MODE>
 static int launch_bits(const sg_arena* A, int bn, const Args& args, cudaStream_t s) {
   switch (bn) {
-    case 16: return launch_cfg<BITS, DUAL, 16>(A, args, s);
-    case 32: return launch_cfg<BITS, DUAL, 32>(A, args, s);
-    case 64: return launch_cfg<BITS, DUAL, 64>(A, args, s);
-    default: return launch_cfg<BITS, DUAL, 128>(A, args, s);
+    case 16: return launch_cfg<BITS, MODE, 16>(A, args, s);
+    case 32: return launch_cfg<BITS, MODE, 32>(A, args, s);
+    case 64: return launch_cfg<BITS, MODE, 64>(A, args, s);
+    default: return launch_cfg<BITS, MODE, 128>(A, args, s);
+  }
+}
+
+// gate/up: mode 1; down: 256-row paired tiles (mode 2) when the output
+// dimension allows, else 128-row tiles (mode 0)
+static int mode_of(bool dual, int OUT) { return dual ? 1 : (OUT % (2 * BM) == 0 ? 2 : 0); }
+
+template <int BITS>
+static int launch_mode(const sg_arena* A, int mode, int bn, const Args& args, cudaStream_t s) {
+  switch (mode) {
+    case 1: return launch_bits<BITS, 1>(A, bn, args, s);
+    case 2: return launch_bits<BITS, 2>(A, bn, args, s);
+    default: return launch_bits<BITS, 0>(A, bn, args, s);
   }
 }
 
@@ -1282,9 +1312,9 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   a.dense_slot = 0;
   const int bn = pick_bn(P, grid_groups);
   switch (A->bits) {
-    case 16: return dual ? tc::launch_bits<16, true>(A, bn, a, s) : tc::launch_bits<16, false>(A, bn, a, s);
-    case 8: return dual ? tc::launch_bits<8, true>(A, bn, a, s) : tc::launch_bits<8, false>(A, bn, a, s);
-    default: return dual ? tc::launch_bits<4, true>(A, bn, a, s) : tc::launch_bits<4, false>(A, bn, a, s);
+    case 16: return tc::launch_mode<16>(A, tc::mode_of(dual, a.OUT), bn, a, s);
+    case 8: return tc::launch_mode<8>(A, tc::mode_of(dual, a.OUT), bn, a, s);
+    default: return tc::launch_mode<4>(A, tc::mode_of(dual, a.OUT), bn, a, s);
   }
 }
 
@@ -1311,13 +1341,13 @@ int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, 
   a.out = out;
   a.dense_rows = rows;
   a.dense_slot = sid;
-  const int mt = a.OUT / tc::BM;
+  const int mt = a.OUT / (tc::mode_of(dual, a.OUT) == 2 ? 2 * tc::BM : tc::BM);
   int bn = rows > 32 ? 64 : (rows > 16 ? 32 : 16);
   if ((long long)mt * ((rows + 63) / 64) > tc::num_sms()) bn = 128;
   switch (A->bits) {
-    case 16: return dual ? tc::launch_bits<16, true>(A, bn, a, s) : tc::launch_bits<16, false>(A, bn, a, s);
-    case 8: return dual ? tc::launch_bits<8, true>(A, bn, a, s) : tc::launch_bits<8, false>(A, bn, a, s);
-    default: return dual ? tc::launch_bits<4, true>(A, bn, a, s) : tc::launch_bits<4, false>(A, bn, a, s);
+    case 16: return tc::launch_mode<16>(A, tc::mode_of(dual, a.OUT), bn, a, s);
+    case 8: return tc::launch_mode<8>(A, tc::mode_of(dual, a.OUT), bn, a, s);
+    default: return tc::launch_mode<4>(A, tc::mode_of(dual, a.OUT), bn, a, s);
   }
 }
 

@@ -6,13 +6,14 @@ Rank r of R owns experts [r*E/R, (r+1)*E/R) in its arena (slot = expert id -
 r*E/R); the router and the shared expert are replicated; every rank routes its
 own tokens.  Per layer:
 
-  1. route the local tokens (router GEMV + softmax/top-k);
+  1. route the local tokens (router GEMV + softmax/top-k) and queue the local
+     shared expert;
   2. order the T*k (token, expert) pairs by owning rank; exchange the per-rank
      pair counts (all-to-all of R ints, the one host read of the step);
   3. all-to-all the pairs' hidden rows and their local expert ids;
   4. run the gathered SwiGLU on the received rows against the local arena;
   5. all-to-all the expert outputs back, restore pair order, combine with the
-     routing scores and the local shared expert.
+     routing scores and the shared expert's output.
 
 The math of steps 1, 4, 5 goes through a ``backend`` object so that the same
 exchange logic runs with the CUDA kernels (``CudaBackend``) on GPUs and with a
@@ -109,6 +110,9 @@ class ExpertParallelMoE:
         T, H = x.shape
         k, R, per = self.top_k, self.world, self.shard.count
         inds, scores = self.backend.route(x)
+        # the shared expert is queued before the host waits on the pair counts,
+        # so the GPU runs it during that wait
+        shared_y, shared_gate = self.backend.shared_terms(x)
         flat = inds.reshape(-1).to(torch.int64)
         dest = torch.div(flat, per, rounding_mode="floor")
         order = torch.argsort(dest, stable=True)            # pair ids in send order
@@ -132,7 +136,6 @@ class ExpertParallelMoE:
         self._a2a(y_back, y_local, send, recv)
         y = torch.empty_like(y_back)
         y.index_copy_(0, order, y_back)
-        shared_y, shared_gate = self.backend.shared_terms(x)
         return self.backend.combine(y, scores, shared_y, shared_gate)
 
     __call__ = forward

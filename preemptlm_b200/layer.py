@@ -131,6 +131,7 @@ class Qwen3_xMoEWrapper(SlotTable):
         self._copy_stream: torch.cuda.Stream | None = None  # slot refills, overlapped with compute
         self._refill_event: torch.cuda.Event | None = None  # the last step's refills, for the GLU to wait on
         self.admit_stats = {"steps": 0, "unique": 0, "missed": 0}  # streaming: routed experts seen / refilled
+        self._side_stream: torch.cuda.Stream | None = None  # the shared expert, beside the routed path
         self._weight_slots: SlottedGLU | None = None
         if expert_loader is not None or expert_cache is not None:
             H, I = inner.hidden_size, inner.moe_intermediate_size
@@ -212,6 +213,34 @@ class Qwen3_xMoEWrapper(SlotTable):
         return unique, d.inverse, d
 
     # ------------------------------------------------------------------ forward
+    def _shared_begin(self, x2: torch.Tensor):
+        """Queue the shared expert and its gate on a side stream (they only
+        need x); returns the pending (y, gate) for _shared_end."""
+        if self.inner.shared_expert is None:
+            return None
+        main = torch.cuda.current_stream(x2.device)
+        if self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(x2.device)
+        side = self._side_stream
+        side.wait_stream(main)
+        x2.record_stream(side)  # read on the side stream after the caller may drop it
+        with torch.cuda.stream(side):
+            sy = shared_expert_forward(self.inner.shared_expert, x2)
+            sg = ops.router_linear(x2, self.inner.shared_expert_gate)
+        return sy, sg
+
+    def _shared_end(self, pending):
+        """Join the side stream; the shared results become usable on the
+        current stream."""
+        if pending is None:
+            return None, None
+        sy, sg = pending
+        main = torch.cuda.current_stream(sy.device)
+        main.wait_stream(self._side_stream)
+        sy.record_stream(main)
+        sg.record_stream(main)
+        return sy, sg
+
     def _gather_forward_dispatched(self, x2: torch.Tensor, d: ops.Dispatch, arena: SlottedGLU) -> torch.Tensor:
         return ops.gather_forward(arena, x2, d, self.inner.top_k)
 
@@ -241,10 +270,7 @@ class Qwen3_xMoEWrapper(SlotTable):
         admitted = None
         if self.expert_cache is not None:
             admitted = self._maybe_admit(inds)  # slot refills start on the side stream
-        shared_y = shared_gate = None
-        if self.inner.shared_expert is not None:
-            shared_y = shared_expert_forward(self.inner.shared_expert, x2)
-            shared_gate = ops.router_linear(x2, self.inner.shared_expert_gate)
+        pending = self._shared_begin(x2)
         if self.should_capture_traces:
             self.recorder.capture(layer_path=self.layer_path, layer_class="Qwen3NextSparseMoeBlock",
                                   block_idx=self.block_idx, expert_ids=inds, softmax_weights=scores,
@@ -260,6 +286,7 @@ class Qwen3_xMoEWrapper(SlotTable):
                 self._refill_event = None
             y = self._gather_forward_dispatched(x2, d, self._weight_slots)
             self._touch(slot_ids)
+        shared_y, shared_gate = self._shared_end(pending)
         out = _combine_shared(y.reshape(B * S, self.inner.top_k, H), scores, shared_y, shared_gate)
         return out.reshape(B, S, H)
 
@@ -270,15 +297,13 @@ class Qwen3_xMoEWrapper(SlotTable):
         kernels plus the step's Dispatch, for per-kernel timing."""
         if self._identity is None:
             raise RuntimeError("forward_resident needs the non-streaming (all-resident) wrapper")
+        pending = self._shared_begin(x2)
         logits = ops.router_linear(x2, self.inner.gate)
         inds, scores = ops.route_topk(logits, self.inner.top_k, self.inner.norm_topk_prob)
-        shared_y = shared_gate = None
-        if self.inner.shared_expert is not None:
-            shared_y = shared_expert_forward(self.inner.shared_expert, x2)
-            shared_gate = ops.router_linear(x2, self.inner.shared_expert_gate)
         d = ops.dispatch(inds, self.num_experts, self._identity)
         arena = self.inner.switch_mlp
         y = ops.gather_forward(arena, x2, d, self.inner.top_k, timing=timing)
+        shared_y, shared_gate = self._shared_end(pending)
         return ops.combine(y, scores, shared_y, None if shared_gate is None else shared_gate.reshape(-1))
 
     # ------------------------------------------------------------------ factory
