@@ -59,7 +59,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=None, help="override the expert count (profiling cases)")
     ap.add_argument("--no-shared", action="store_true", help="drop the shared expert (profiling cases)")
-    ap.add_argument("--glu-path", choices=("auto", "gemv", "tc"), default="auto")
+    ap.add_argument("--glu-path", choices=("auto", "gemv", "tc", "tc-perm"), default="auto")
+    ap.add_argument("--microbatches", type=int, default=None,
+                    help="expert-parallel micro-batches per step (default 2 when N > 1)")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed device-resident steps (for ncu captures); prints ms/step")
     return ap.parse_args()
@@ -301,7 +303,12 @@ def run_ours(args, rank, world, local_rank):
 
         backend, _ = shard_layer(cfg, rank, world, dev)
         ep = ExpertParallelMoE(backend, cfg.num_experts, H, cfg.top_k)
-        step = ep.forward
+        mb = args.microbatches or 2
+
+        def step(x):
+            # the step's tokens in mb micro-batches, every count exchange queued
+            # before the host waits on the first
+            return torch.cat(ep.forward_many(x.chunk(mb))) if mb > 1 else ep.forward(x)
         tens = None
     else:
         block, tens = make_layer(cfg, device=dev)
@@ -446,6 +453,7 @@ def run_ours(args, rank, world, local_rank):
             "l2": "no flush: each step streams >126 MB (L2) of expert weights per GPU",
             "queue": "device-resident steps are queued behind a bounded device spin (not timed); e2e is not",
             "parallelism": f"ep{world}",
+            "microbatches": (args.microbatches or 2) if world > 1 else 1,
         },
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),

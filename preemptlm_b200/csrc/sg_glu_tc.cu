@@ -44,6 +44,7 @@ constexpr int DQ_WARP0 = 3;  // dequantiser warps start here; the 4 epilogue war
 constexpr int RING_BUDGET = 208 * 1024;
 constexpr int PLAN_MAX_GROUPS = 2048;
 constexpr long long WAIT_CYCLES = 2000000000LL;  // ~1 s
+constexpr uint32_t BACKOFF_NS = 512;
 
 __host__ __device__ constexpr int pow2ceil(int v) {
   int p = 1;
@@ -165,11 +166,15 @@ struct Ctl {
 };
 
 // Bounded wait for the phase of parity `parity` to complete.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl ctl) {
+// Roles off the critical path (producers, epilogue) back off with a short
+// nanosleep between polls, leaving issue slots to the dequantising warps that
+// share their SM sub-partition.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl ctl, uint32_t backoff_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 200000)) return true;  // wakes on completion
+    if (backoff_ns) __nanosleep(backoff_ns);
     if (*ctl.abort) return false;
     if (clock64() - t0 > WAIT_CYCLES) {
       *ctl.abort = 1;
@@ -863,7 +868,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           if (STMA && (kb * C::KP) % 8 == 0) {
             // scales and biases of groups [kb*KP, kb*KP + 8) for the tile's
             // rows, ahead of the packed stages that use them
-            ok = wait_bar(&s_empty[ss], sph ^ 1, ctl);
+            ok = wait_bar(&s_empty[ss], sph ^ 1, ctl, BACKOFF_NS);
             if (!ok) break;
             uint8_t* dst = const_cast<uint8_t*>(sS) + ss * C::S_BYTES;
             mbar_expect_tx(&s_full[ss], C::S_BYTES);
@@ -876,7 +881,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             ++s_issued;
             if (++ss == C::SS) { ss = 0; sph ^= 1; }
           }
-          ok = wait_bar(&empty[s_i], ph ^ 1, ctl);
+          ok = wait_bar(&empty[s_i], ph ^ 1, ctl, BACKOFF_NS);
           if (!ok) break;
           if (BITS == 16) {
             mbar_expect_tx(&full[s_i], C::A_BYTES);
@@ -927,7 +932,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
           const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
           for (int kb0 = 0; kb0 < NKB; kb0 += C::KBB) {
-            ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
+            ok = wait_bar(&b_empty[sb], pb ^ 1, ctl, BACKOFF_NS);
             if (!ok) break;
             const int nsub = min(C::KBB, NKB - kb0);
             mbar_expect_tx(&b_full[sb], nsub * C::B_SUB);
@@ -973,7 +978,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         row[i] = (rw >= 0 && rw < args.in_rows) ? rw : -1;
       }
       for (int kb0 = 0; kb0 < NKB; kb0 += C::KBB) {
-        ok = wait_bar(&b_empty[sb], pb ^ 1, ctl);
+        ok = wait_bar(&b_empty[sb], pb ^ 1, ctl, BACKOFF_NS);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         const int nsub = min(C::KBB, NKB - kb0);
@@ -1076,7 +1081,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       const int ab = it % C::NACC;
       const uint32_t accp = static_cast<uint32_t>((it / C::NACC) & 1);
       const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
-      ok = wait_bar(&acc_full[ab], accp, ctl);
+      ok = wait_bar(&acc_full[ab], accp, ctl, BACKOFF_NS);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
       if (!ok) break;
       tc_fence_after();

@@ -105,13 +105,14 @@ class ExpertParallelMoE:
         dist.all_to_all_single(out, inp.contiguous(), output_split_sizes=out_splits, input_split_sizes=in_splits,
                                group=self.group)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """x [T, H] bf16 (this rank's tokens) -> [T, H] bf16."""
+    def begin(self, x: torch.Tensor) -> dict:
+        """Everything of a step that does not need the pair counts on the
+        host: routing, the shared expert, the send order and rows, and the
+        count exchange, whose result is copied to pinned host memory without
+        blocking.  ``end`` finishes the step."""
         T, H = x.shape
         k, R, per = self.top_k, self.world, self.shard.count
         inds, scores = self.backend.route(x)
-        # the shared expert is queued before the host waits on the pair counts,
-        # so the GPU runs it during that wait
         shared_y, shared_gate = self.backend.shared_terms(x)
         flat = inds.reshape(-1).to(torch.int64)
         dest = torch.div(flat, per, rounding_mode="floor")
@@ -119,24 +120,49 @@ class ExpertParallelMoE:
         send_counts = torch.bincount(dest, minlength=R)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        counts = torch.stack([send_counts, recv_counts]).cpu()
-        send, recv = counts[0].tolist(), counts[1].tolist()
-        self.last_counts = (send, recv)
-        n_recv = sum(recv)
-
         send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
         send_eid = (flat.index_select(0, order) - dest.index_select(0, order) * per).to(torch.int32)
-        recv_rows = torch.empty((n_recv, H), dtype=x.dtype, device=x.device)
-        recv_eid = torch.empty((n_recv,), dtype=torch.int32, device=x.device)
-        self._a2a(recv_rows, send_rows, recv, send)
-        self._a2a(recv_eid, send_eid, recv, send)
+        counts = torch.stack([send_counts, recv_counts])
+        if counts.is_cuda:
+            host = torch.empty(counts.shape, dtype=counts.dtype).pin_memory()
+            host.copy_(counts, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record()
+        else:
+            host, ready = counts, None
+        return {"T": T, "H": H, "dtype": x.dtype, "device": x.device, "scores": scores, "shared_y": shared_y,
+                "shared_gate": shared_gate, "order": order, "send_rows": send_rows, "send_eid": send_eid,
+                "counts": host, "ready": ready}
 
+    def end(self, st: dict) -> torch.Tensor:
+        """The exchange, the local experts and the combine of a begun step
+        (the one host wait: the pair counts)."""
+        if st["ready"] is not None:
+            st["ready"].synchronize()
+        send, recv = st["counts"][0].tolist(), st["counts"][1].tolist()
+        self.last_counts = (send, recv)
+        n_recv, T, H, k = sum(recv), st["T"], st["H"], self.top_k
+        recv_rows = torch.empty((n_recv, H), dtype=st["dtype"], device=st["device"])
+        recv_eid = torch.empty((n_recv,), dtype=torch.int32, device=st["device"])
+        self._a2a(recv_rows, st["send_rows"], recv, send)
+        self._a2a(recv_eid, st["send_eid"], recv, send)
         y_local = self.backend.experts(recv_rows, recv_eid)
-        y_back = torch.empty((T * k, H), dtype=x.dtype, device=x.device)
+        y_back = torch.empty((T * k, H), dtype=st["dtype"], device=st["device"])
         self._a2a(y_back, y_local, send, recv)
         y = torch.empty_like(y_back)
-        y.index_copy_(0, order, y_back)
-        return self.backend.combine(y, scores, shared_y, shared_gate)
+        y.index_copy_(0, st["order"], y_back)
+        return self.backend.combine(y, st["scores"], st["shared_y"], st["shared_gate"])
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x [T, H] bf16 (this rank's tokens) -> [T, H] bf16."""
+        return self.end(self.begin(x))
+
+    def forward_many(self, xs) -> list:
+        """Several independent token batches (micro-batches of one step):
+        every batch's count exchange is queued before the host waits on the
+        first, so the GPU stays busy while the host issues the rest."""
+        states = [self.begin(x) for x in xs]
+        return [self.end(s) for s in states]
 
     __call__ = forward
 
