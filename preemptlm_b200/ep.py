@@ -117,7 +117,10 @@ class ExpertParallelMoE:
         flat = inds.reshape(-1).to(torch.int64)
         dest = torch.div(flat, per, rounding_mode="floor")
         order = torch.argsort(dest, stable=True)            # pair ids in send order
-        send_counts = torch.bincount(dest, minlength=R)
+        # scatter-add rather than bincount: bincount sizes its output from the
+        # data, a device-to-host wait in the middle of the step
+        send_counts = torch.zeros(R, dtype=torch.int64, device=dest.device).scatter_add_(0, dest,
+                                                                                      torch.ones_like(dest))
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
