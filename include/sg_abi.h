@@ -122,6 +122,20 @@ int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int 
                    const int32_t* group_off, const int32_t* perm,
                    int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y, void* stream);
 
+/* sg_glu_forward without caller scratch: h (and the permuted token rows when
+ * sg_glu_use_permute returns 1) live in a fixed 32 MiB device-resident scratch
+ * area of the library (a file-scope __device__ array, its address looked up
+ * once per device), so the call allocates nothing.  Returns SG_ERR_CAPACITY
+ * when num_pairs * inter * 2 bytes (rounded up to 256), plus num_pairs *
+ * hidden * 2 when permuting, exceed 32 MiB.  Nothing in the scratch area needs
+ * to start at zero.  Calls that overlap in time on one device (different
+ * streams or host threads) share the area and race; calls on one stream are
+ * ordered.  No counterpart in the reference. */
+int sg_glu_forward_noalloc(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                           const int32_t* counts, const int32_t* slot_ids,
+                           const int32_t* group_off, const int32_t* perm,
+                           int grid_groups, uint16_t* y, void* stream);
+
 /* 1 when sg_glu_forward permutes the token rows for this problem size. */
 int sg_glu_use_permute(const sg_arena* arena, int num_pairs, int grid_groups);
 

@@ -8,6 +8,8 @@
 // shared memory NT at a time.  Affine weights are never expanded: per chunk a
 // lane forms dot = sum(q * x) and xs = sum(x) and adds scale*dot + bias*xs,
 // which equals sum((scale*q + bias) * x) without the bf16 rounding of w.
+#include <mutex>
+
 #include "sg_common.cuh"
 
 namespace sg {
@@ -416,4 +418,55 @@ extern "C" int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, i
   st = sg::tc_dense_launch(arena, true, x, T, sid, h, s);
   if (st) return st;
   return sg::tc_dense_launch(arena, false, h, T, sid, y, s);
+}
+
+// ---------------------------------------------------------------- no-alloc variant
+// sg_glu_forward with its intermediate rows (h, and the permuted token rows
+// when sg_glu_use_permute says so) in a fixed scratch area of this library's
+// device memory instead of caller buffers.  The area is a file-scope device
+// array, so the call allocates nothing; its address is looked up once per
+// device.  No part of it needs to start at zero: every row the down projection
+// reads was written by the gate/up launch of the same call.  Calls that overlap
+// in time on one device (other streams, other host threads) share the area and
+// race; calls on one stream are ordered and safe.
+namespace sg {
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64] = {};
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  SG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    SG_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return SG_OK;
+}
+}  // namespace sg
+
+extern "C" int sg_glu_forward_noalloc(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                                      const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                                      const int32_t* perm, int grid_groups, uint16_t* y, void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
+  if (st) return st;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!x || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
+  const size_t h_bytes = ((size_t)num_pairs * arena->inter * 2 + 255) & ~size_t(255);
+  const size_t xs_bytes =
+      sg::use_permute(arena, num_pairs, grid_groups) ? (size_t)num_pairs * arena->hidden * 2 : 0;
+  if (h_bytes + xs_bytes > sg::NOALLOC_SCRATCH_BYTES) return SG_ERR_CAPACITY;
+  void* base = nullptr;
+  st = sg::noalloc_scratch(&base);
+  if (st) return st;
+  uint16_t* h = static_cast<uint16_t*>(base);
+  uint16_t* xs = xs_bytes ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(base) + h_bytes) : nullptr;
+  return sg_glu_forward(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, xs, h, y,
+                        stream);
 }

@@ -197,6 +197,23 @@ def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: d
     return y
 
 
+def gather_forward_noalloc(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
+    """``gather_forward`` with the intermediate rows in the library's fixed
+    device scratch area (``sg_glu_forward_noalloc``): no scratch tensors are
+    allocated.  Calls overlapping in time on one device race on that area."""
+    x = _bf16_2d(x, "x")
+    P = d.perm.numel()
+    y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device)
+    if P == 0:
+        return y
+    LAUNCHES[0] += 2
+    _abi.check(_abi.load().sg_glu_forward_noalloc(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div),
+                                                  d.counts.data_ptr(), d.slot_ids.data_ptr(), d.group_off.data_ptr(),
+                                                  d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),
+               "sg_glu_forward_noalloc")
+    return y
+
+
 def dense_glu(arena, x: torch.Tensor, sid: int = 0) -> torch.Tensor | None:
     """y = down(swiglu(gate(x), up(x))) of slot ``sid`` over every row of x
     (``sg_dense_glu``, the shared expert).  Returns None for shapes the dense
