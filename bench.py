@@ -41,9 +41,11 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# DRAM bytes (read + write) per routed gate/up launch from an ncu capture, by
-# (workload, tokens per GPU); see profiles/ for the capture and its scaling
-TRAFFIC: dict = {}
+# DRAM bytes (read + write) of the routed gate/up launch per unique expert, from
+# an ncu capture of the same kernel on a smaller case of the workload (128
+# experts, 64 tokens: 291.59 MB for 128 unique experts); the launch streams
+# each unique expert's weights once, so traffic scales with the unique count
+TRAFFIC_PER_EXPERT = {"cfg3-q8-decode-shared": 291.59e6 / 128}
 QUEUE_AHEAD_CYCLES = 200_000_000  # ~0.1 s of device spin before the device-resident timed region
 METRIC = "SlottedGLU tokens/s at 1/2/4/8 B200; expert-GEMM HBM GB/s vs 8 TB/s peak"
 
@@ -458,7 +460,8 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
             "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4), "peak_kind": peak_kind,
-            "traffic": TRAFFIC.get((cfg.name, T)),
+            "traffic": (round(TRAFFIC_PER_EXPERT[cfg.name] * us_mean) if cfg.name in TRAFFIC_PER_EXPERT
+                        and world == 1 and not args.experts else None),
             "bytes_per_launch": round(rl["gu_bytes"] / len(rl["gu_ms"])),
             "ms_per_launch": round(statistics.mean(rl["gu_ms"]), 5),
             "down": {"achieved": round(rl["dn_gbs"], 1), "frac": round(rl["dn_gbs"] / peak, 4),
