@@ -43,7 +43,6 @@ enum sg_status {
 enum sg_glu_flags {
   SG_IN_DISPATCH_ORDER = 1,   /* input rows are in dispatch order (num_pairs rows) */
   SG_OUT_DISPATCH_ORDER = 2,  /* write output rows in dispatch order */
-  SG_IN_PREPARED = 4,         /* input is sg_glu_prep's scratch (gate/up only) */
 };
 
 /* Human-readable text of a status code (static storage). */
@@ -111,45 +110,24 @@ int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
  * every pair p of every group u < counts[0], against arena slot slot_ids[u];
  * pairs listed by perm/group_off (sg_dispatch layout); num_pairs = P (length
  * of perm, rows of y; x has ceil(P / pair_div) rows); y in pair order.
- * xs (sg_glu_scratch_bytes bytes, 16-byte aligned; NULL when that is 0) and
- * h [P, I] are caller-provided intermediate storage: xs takes sg_glu_prep's
- * rows, h is kept in dispatch order.  pair_div = k for routed experts.
+ * xs [P, H] and h [P, I] are caller-provided intermediate storage (xs is
+ * written only when sg_glu_use_permute says so: the pairs' token rows are
+ * first copied into dispatch order, so that every tile's rows load as one
+ * TMA box; h is kept in dispatch order).  pair_div = k for routed experts.
  * grid_groups is a host-side upper bound on counts[0].
  * Replaces `_gather_forward`, qwen3_x_moe.py:210-248 (the `mx.take` of the
  * arena, two `gather_mm` + `swiglu_activation`, the down `gather_mm`). */
 int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                    const int32_t* counts, const int32_t* slot_ids,
                    const int32_t* group_off, const int32_t* perm,
-                   int grid_groups, void* xs, uint16_t* h, uint16_t* y, void* stream);
+                   int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y, void* stream);
 
-/* Bytes of the xs scratch sg_glu_forward / sg_glu_prep need for this problem
- * (0: none, xs may be NULL), or a negative status.  No counterpart in the
- * reference (MLX allocates its own temporaries). */
-long long sg_glu_scratch_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups);
-
-/* The input preparation of sg_glu_forward, into `scratch`
- * (sg_glu_scratch_bytes bytes).  Decode-sized groups of a quantised arena
- * (16-wide pair tiles, hidden/64 a multiple of 8 and at most 64): each token
- * row is scaled by a power of two 2^-e that brings its largest magnitude
- * into [2^14, 2^15) and stored as f16 (exact for every value within 2^28 of
- * that maximum), with the fp32 sums of its 64-column groups and 2^e; gate/up
- * then runs on the raw quantised integers as f16 (1024 + q) and applies each
- * group's scale and bias to that group's accumulator,
- * y = sum_g s_g * A_g + (b_g - 1024 s_g) * X_g, the reference's
- * sum of (s q + b) x without its bf16 rounding of the dequantised weights.
- * Prefill-sized groups: the pairs' token rows copied into dispatch order.
- * Otherwise nothing.  Returns the sg_glu_gate_up input flags for the result
- * (SG_IN_PREPARED and/or SG_IN_DISPATCH_ORDER; 0 = use x itself), or a
- * negative status.  Replaces nothing in the reference (its `mx.take` of the
- * token rows, qwen3_x_moe.py:225, is the permuted case). */
-int sg_glu_prep(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
-                const int32_t* perm, int grid_groups, void* scratch, void* stream);
-
-/* sg_glu_forward without caller scratch: h and the prepared rows live in a
- * fixed 32 MiB device-resident scratch area of the library (a file-scope
- * __device__ array, its address looked up once per device), so the call
- * allocates nothing.  Returns SG_ERR_CAPACITY when num_pairs * inter * 2
- * bytes (rounded up to 256) plus sg_glu_scratch_bytes exceed 32 MiB.  Nothing in the scratch area needs
+/* sg_glu_forward without caller scratch: h (and the permuted token rows when
+ * sg_glu_use_permute returns 1) live in a fixed 32 MiB device-resident scratch
+ * area of the library (a file-scope __device__ array, its address looked up
+ * once per device), so the call allocates nothing.  Returns SG_ERR_CAPACITY
+ * when num_pairs * inter * 2 bytes (rounded up to 256), plus num_pairs *
+ * hidden * 2 when permuting, exceed 32 MiB.  Nothing in the scratch area needs
  * to start at zero.  Calls that overlap in time on one device (different
  * streams or host threads) share the area and race; calls on one stream are
  * ordered.  No counterpart in the reference. */
@@ -167,8 +145,7 @@ int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_div, int nu
 
 /* The two halves of sg_glu_forward.  h[., I] = swiglu(x @ gate^T, x @ up^T)
  * per pair; rows in pair or dispatch order per `flags` (sg_glu_flags; input
- * in dispatch order means x has num_pairs rows and pair_div is not used;
- * SG_IN_PREPARED: x is the scratch sg_glu_prep wrote for the same problem).
+ * in dispatch order means x has num_pairs rows and pair_div is not used).
  * Rounds x_up, x_gate, sigmoid, silu and the product to bf16
  * (experts.py:26-28).  Replaces the up/gate `gather_mm` calls and
  * `swiglu_activation` in `_gather_forward`, qwen3_x_moe.py:225-242.
@@ -200,9 +177,7 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
  * automatic (tcgen05 when the mean pairs per group is >= 2 and the shape
  * allows: in-dim % 64, out-dim % 128, <= 2048 groups; token rows permuted
  * once the mean reaches 32), 1 = streaming GEMV always, 2 = tcgen05 whenever
- * the shape allows, 3 = as 2 with the token rows always permuted, 4 = as 0
- * but gate/up always on exactly dequantised bf16 weights (no sg_glu_prep
- * factored scales).
+ * the shape allows, 3 = as 2 with the token rows always permuted.
  * Process-wide.  No counterpart in the reference (MLX picks
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);

@@ -24,13 +24,11 @@ SG_ERR_TIMEOUT = -6
 
 SG_IN_DISPATCH_ORDER = 1
 SG_OUT_DISPATCH_ORDER = 2
-SG_IN_PREPARED = 4
 
 # Every symbol include/sg_abi.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
     "sg_status_string", "sg_version", "sg_built_arch", "sg_router_logits", "sg_route_topk",
-    "sg_dispatch", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_scratch_bytes", "sg_glu_prep",
-    "sg_glu_use_permute", "sg_permute_rows", "sg_glu_gate_up", "sg_glu_down",
+    "sg_dispatch", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_use_permute", "sg_permute_rows", "sg_glu_gate_up", "sg_glu_down",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
 )
@@ -82,8 +80,6 @@ def load() -> ctypes.CDLL:
         "sg_dispatch": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I32, P]),
         "sg_glu_forward": (I32, [A, P, I32, I32, P, P, P, P, I32, P, P, P, P]),
         "sg_glu_forward_noalloc": (I32, [A, P, I32, I32, P, P, P, P, I32, P, P]),
-        "sg_glu_scratch_bytes": (ctypes.c_longlong, [A, I32, I32, I32]),
-        "sg_glu_prep": (I32, [A, P, I32, I32, P, I32, P, P]),
         "sg_glu_use_permute": (I32, [A, I32, I32]),
         "sg_permute_rows": (I32, [P, P, I32, I32, I32, P, P]),
         "sg_glu_gate_up": (I32, [A, P, I32, I32, P, P, P, P, I32, P, I32, P]),

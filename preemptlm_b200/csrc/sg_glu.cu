@@ -8,8 +8,6 @@
 // shared memory NT at a time.  Affine weights are never expanded: per chunk a
 // lane forms dot = sum(q * x) and xs = sum(x) and adds scale*dot + bias*xs,
 // which equals sum((scale*q + bias) * x) without the bf16 rounding of w.
-#include <cuda_fp16.h>
-
 #include <mutex>
 
 #include "sg_common.cuh"
@@ -267,14 +265,10 @@ namespace sg {
 bool tc_supported(const sg_arena* A, bool dual, int grid_groups);
 int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_by_pos,
                   int out_by_pos, int P, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                  const int32_t* perm, int grid_groups, uint16_t* out, const float* xsum, const float* xscale,
-                  cudaStream_t s);
-bool tc_fq_supported(const sg_arena* A, int P, int grid_groups);
+                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
 int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
                     cudaStream_t s);
-// 0 auto, 1 streaming GEMV, 2 tcgen05, 3 tcgen05 over permuted rows, 4 tcgen05
-// with the exact dequantised weights (no factored scales)
-static int g_glu_path = 0;
+static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05, 3 tcgen05 over permuted rows
 
 // auto: the tensor-core path once the mean pairs per group reaches 2
 static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
@@ -290,88 +284,6 @@ static bool use_permute(const sg_arena* A, int P, int grid_groups) {
   if (!use_tc(A, true, P, grid_groups) || !use_tc(A, false, P, grid_groups)) return false;
   if (g_glu_path == 3) return true;
   return P >= 32 * grid_groups;
-}
-
-// Whether sg_glu_forward's gate/up takes factored scales over prepared f16
-// rows (decode-sized groups of a quantised arena).
-static bool use_fq(const sg_arena* A, int P, int grid_groups) {
-  return g_glu_path != 4 && use_tc(A, true, P, grid_groups) && tc_fq_supported(A, P, grid_groups);
-}
-
-// Prepared-row scratch of sg_glu_prep: R rows of x16 [R][K] f16, then
-// xsum [R][K/64] fp32, then xscale [R] fp32, each part 256-byte aligned.
-static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-struct PrepLayout {
-  size_t x16, xsum, xscale, bytes;
-};
-static PrepLayout prep_layout(int R, int K) {
-  PrepLayout l;
-  l.x16 = 0;
-  l.xsum = align256((size_t)R * K * 2);
-  l.xscale = l.xsum + align256((size_t)R * (K / 64) * 4);
-  l.bytes = l.xscale + align256((size_t)R * 4);
-  return l;
-}
-
-// FQ row preparation, one warp per prepared row i (source row perm[i] /
-// pair_div when permuted, else i): e = the power of two that brings the row's
-// largest magnitude into [2^14, 2^15); x16 = f16(x * 2^-e), exact for every
-// value within 2^28 of that maximum; xsum[i][g] = fp32 sum of the 64 f16
-// values of group g (8 in a lane, then 8 lanes); xscale[i] = 2^e.  Rows
-// without a source (a permutation entry out of range) are zero.
-__global__ void __launch_bounds__(256)
-fq_prep_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int pair_div, int permuted, int R,
-               int src_rows, int K, uint16_t* __restrict__ x16, float* __restrict__ xsum,
-               float* __restrict__ xscale) {
-  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (i >= R) return;
-  const int src = permuted ? perm[i] / pair_div : i;
-  const bool valid = src >= 0 && src < src_rows;
-  const uint16_t* row = x + (size_t)(valid ? src : 0) * K;
-  const int chunks = K >> 3, G = K >> 6;
-  uint32_t m = 0;  // largest |x| as bf16 magnitude bits
-  for (int c = lane; c < chunks && valid; c += 32) {
-    const uint4 v = ldg_nc_v4(row + (size_t)c * 8);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) m = max(m, max(w[q] & 0x7FFFu, (w[q] >> 16) & 0x7FFFu));
-  }
-  m = __reduce_max_sync(0xffffffffu, m);
-  const int ebits = static_cast<int>(m >> 7);  // bf16 exponent field (fp32's)
-  const int e = ebits == 0 ? 0 : max(ebits - 141, -126);
-  const float down = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
-  uint4* orow = reinterpret_cast<uint4*>(x16 + (size_t)i * K);
-  for (int base = 0; base < chunks; base += 32) {
-    const int c = base + lane;
-    const bool act = c < chunks;  // uniform across each 8-lane group (chunks % 8 == 0)
-    float sum = 0.f;
-    if (act) {
-      const uint4 v = valid ? ldg_nc_v4(row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const __half2 h = __floats2half2_rn(__fmul_rn(__uint_as_float(w[q] << 16), down),
-                                            __fmul_rn(__uint_as_float(w[q] & 0xFFFF0000u), down));
-        const float2 f = __half22float2(h);
-        sum = __fadd_rn(__fadd_rn(sum, f.x), f.y);
-        o[q] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
-    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
-    if (act && (lane & 7) == 0) xsum[(size_t)i * G + (c >> 3)] = sum;
-  }
-  if (lane == 0) xscale[i] = valid ? __uint_as_float(static_cast<uint32_t>(127 + e) << 23) : 0.f;
-}
-
-// Rows of the prepared scratch: every pair in dispatch order when permuted,
-// else the token rows.
-static int prep_rows(const sg_arena* A, int P, int pair_div, int grid_groups) {
-  return use_permute(A, P, grid_groups) ? P : (P + pair_div - 1) / pair_div;
 }
 
 // xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
@@ -391,19 +303,10 @@ static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int
                     uint16_t* h, int flags, cudaStream_t s) {
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
   const int div = in_pos ? 1 : pair_div;
-  const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
-  if (flags & SG_IN_PREPARED) {
-    // x is sg_glu_prep's scratch: f16 rows, group sums, row scales
-    if (!use_fq(arena, num_pairs, grid_groups)) return SG_ERR_SHAPE;
-    const PrepLayout l = prep_layout(in_rows, arena->hidden);
-    const uint8_t* base = reinterpret_cast<const uint8_t*>(x);
-    return tc_glu_launch(arena, true, x, in_rows, div, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
-                         grid_groups, h, reinterpret_cast<const float*>(base + l.xsum),
-                         reinterpret_cast<const float*>(base + l.xscale), s);
-  }
   if (use_tc(arena, true, num_pairs, grid_groups)) {
+    const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
     return tc_glu_launch(arena, true, x, in_rows, div, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
-                         grid_groups, h, nullptr, nullptr, s);
+                         grid_groups, h, s);
   }
   switch (arena->bits) {
     case 16: return launch_gemv<16, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
@@ -418,7 +321,7 @@ static int glu_single(const sg_arena* arena, const uint16_t* h, int num_pairs, c
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
   if (use_tc(arena, false, num_pairs, grid_groups))
     return tc_glu_launch(arena, false, h, num_pairs, 1, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
-                         grid_groups, y, nullptr, nullptr, s);
+                         grid_groups, y, s);
   switch (arena->bits) {
     case 16: return launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
     case 8: return launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
@@ -430,14 +333,14 @@ static int check_glu_args(const sg_arena* arena, int num_pairs, int pair_div, in
   int st = check_arena(arena);
   if (st) return st;
   if (num_pairs < 0 || pair_div < 1 || grid_groups < 0) return SG_ERR_INVALID_ARG;
-  if (flags & ~(SG_IN_DISPATCH_ORDER | SG_OUT_DISPATCH_ORDER | SG_IN_PREPARED)) return SG_ERR_INVALID_ARG;
+  if (flags & ~(SG_IN_DISPATCH_ORDER | SG_OUT_DISPATCH_ORDER)) return SG_ERR_INVALID_ARG;
   if (grid_groups > 65535) return SG_ERR_SHAPE;
   return SG_OK;
 }
 }  // namespace sg
 
 extern "C" int sg_set_glu_path(int mode) {
-  if (mode < 0 || mode > 4) return SG_ERR_INVALID_ARG;
+  if (mode < 0 || mode > 3) return SG_ERR_INVALID_ARG;
   sg::g_glu_path = mode;
   return SG_OK;
 }
@@ -458,43 +361,6 @@ extern "C" int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_
   return SG_OK;
 }
 
-extern "C" long long sg_glu_scratch_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups) {
-  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
-  if (st) return st;
-  if (num_pairs == 0 || grid_groups == 0) return 0;
-  if (sg::use_fq(arena, num_pairs, grid_groups))
-    return (long long)sg::prep_layout(sg::prep_rows(arena, num_pairs, pair_div, grid_groups), arena->hidden).bytes;
-  if (sg::use_permute(arena, num_pairs, grid_groups)) return (long long)num_pairs * arena->hidden * 2;
-  return 0;
-}
-
-extern "C" int sg_glu_prep(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
-                           const int32_t* perm, int grid_groups, void* scratch, void* stream) {
-  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
-  if (st) return st;
-  if (num_pairs == 0 || grid_groups == 0) return 0;
-  if (!x || !perm) return SG_ERR_INVALID_ARG;
-  const bool permute = sg::use_permute(arena, num_pairs, grid_groups);
-  if (sg::use_fq(arena, num_pairs, grid_groups)) {
-    if (!scratch) return SG_ERR_INVALID_ARG;
-    const int R = sg::prep_rows(arena, num_pairs, pair_div, grid_groups);
-    const int src_rows = (num_pairs + pair_div - 1) / pair_div;
-    const sg::PrepLayout l = sg::prep_layout(R, arena->hidden);
-    uint8_t* base = static_cast<uint8_t*>(scratch);
-    sg::fq_prep_kernel<<<(R + 7) / 8, 256, 0, (cudaStream_t)stream>>>(
-        x, perm, pair_div, permute ? 1 : 0, R, src_rows, arena->hidden, reinterpret_cast<uint16_t*>(base + l.x16),
-        reinterpret_cast<float*>(base + l.xsum), reinterpret_cast<float*>(base + l.xscale));
-    SG_LAUNCH_CHECK();
-    return SG_IN_PREPARED | (permute ? SG_IN_DISPATCH_ORDER : 0);
-  }
-  if (permute) {
-    if (!scratch) return SG_ERR_INVALID_ARG;
-    st = sg_permute_rows(x, perm, pair_div, num_pairs, arena->hidden, static_cast<uint16_t*>(scratch), stream);
-    return st ? st : SG_IN_DISPATCH_ORDER;
-  }
-  return 0;
-}
-
 extern "C" int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                               const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
                               const int32_t* perm, int grid_groups, uint16_t* h, int flags, void* stream) {
@@ -511,7 +377,6 @@ extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pai
                            uint16_t* y, int flags, void* stream) {
   int st = sg::check_glu_args(arena, num_pairs, 1, grid_groups, flags);
   if (st) return st;
-  if (flags & SG_IN_PREPARED) return SG_ERR_INVALID_ARG;  // gate/up input only
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!h || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
   return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, flags,
@@ -520,18 +385,22 @@ extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pai
 
 extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                               const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                              const int32_t* perm, int grid_groups, void* xs, uint16_t* h, uint16_t* y,
+                              const int32_t* perm, int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y,
                               void* stream) {
   int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
   if (st) return st;
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!x || !counts || !slot_ids || !group_off || !perm || !h || !y) return SG_ERR_INVALID_ARG;
   cudaStream_t s = (cudaStream_t)stream;
-  const int in_flags = sg_glu_prep(arena, x, num_pairs, pair_div, perm, grid_groups, xs, stream);
-  if (in_flags < 0) return in_flags;
+  const bool permute = sg::use_permute(arena, num_pairs, grid_groups);
+  if (permute) {
+    if (!xs) return SG_ERR_INVALID_ARG;
+    st = sg_permute_rows(x, perm, pair_div, num_pairs, arena->hidden, xs, stream);
+    if (st) return st;
+  }
   // h in dispatch order, so that the down projection's rows are contiguous
-  st = sg::glu_dual(arena, in_flags ? static_cast<const uint16_t*>(xs) : x, num_pairs, pair_div, counts, slot_ids,
-                    group_off, perm, grid_groups, h, in_flags | SG_OUT_DISPATCH_ORDER, s);
+  st = sg::glu_dual(arena, permute ? xs : x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h,
+                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s);
   if (st) return st;
   return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, SG_IN_DISPATCH_ORDER,
                         s);
@@ -552,8 +421,8 @@ extern "C" int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, i
 }
 
 // ---------------------------------------------------------------- no-alloc variant
-// sg_glu_forward with its intermediate rows (h, and the prepared token rows
-// when sg_glu_scratch_bytes asks for them) in a fixed scratch area of this library's
+// sg_glu_forward with its intermediate rows (h, and the permuted token rows
+// when sg_glu_use_permute says so) in a fixed scratch area of this library's
 // device memory instead of caller buffers.  The area is a file-scope device
 // array, so the call allocates nothing; its address is looked up once per
 // device.  No part of it needs to start at zero: every row the down projection
@@ -590,15 +459,14 @@ extern "C" int sg_glu_forward_noalloc(const sg_arena* arena, const uint16_t* x, 
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!x || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
   const size_t h_bytes = ((size_t)num_pairs * arena->inter * 2 + 255) & ~size_t(255);
-  const long long xs_need = sg_glu_scratch_bytes(arena, num_pairs, pair_div, grid_groups);
-  if (xs_need < 0) return (int)xs_need;
-  const size_t xs_bytes = (size_t)xs_need;
+  const size_t xs_bytes =
+      sg::use_permute(arena, num_pairs, grid_groups) ? (size_t)num_pairs * arena->hidden * 2 : 0;
   if (h_bytes + xs_bytes > sg::NOALLOC_SCRATCH_BYTES) return SG_ERR_CAPACITY;
   void* base = nullptr;
   st = sg::noalloc_scratch(&base);
   if (st) return st;
   uint16_t* h = static_cast<uint16_t*>(base);
-  void* xs = xs_bytes ? static_cast<void*>(static_cast<uint8_t*>(base) + h_bytes) : nullptr;
+  uint16_t* xs = xs_bytes ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(base) + h_bytes) : nullptr;
   return sg_glu_forward(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, xs, h, y,
                         stream);
 }

@@ -57,11 +57,7 @@ __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // MODE 0: down projection, one 128-row weight tile; 1: gate/up, two matrices
 // and the SwiGLU epilogue; 2: down projection, two 128-row halves of a 256-row
 // weight tile sharing the B rows (twice the bytes per pipeline stage).
-// FQ (factored quantised gate/up, decode tiles): the A operand is the raw
-// quantised integer as f16 (1024 + q, exact), B the token rows as prepared f16
-// rows, and every 64-weight group accumulates into its own TMEM accumulator;
-// the epilogue applies that group's scale and bias (see epilogue_fq).
-template <int BITS, int MODE, int BN, bool FQ = false>
+template <int BITS, int MODE, int BN>
 struct Cfg {
   static constexpr bool DUAL = MODE != 0;  // two A matrices per stage
   static constexpr int ROWS = MODE == 2 ? 2 * BM : BM;  // weight rows per tile
@@ -83,8 +79,7 @@ struct Cfg {
   static constexpr int KBB = BN <= 32 ? 4 : (BN <= 64 ? 2 : 1);
   static constexpr int B_BYTES = B_SUB * KBB;
   static constexpr int ACC_COLS = NMAT * BN;
-  // FQ: a ring of NACC per-group accumulators; otherwise per-tile ones
-  static constexpr int NACC = FQ ? 4 : (2 * ACC_COLS <= 512 ? 2 : 1);
+  static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;
   static constexpr int ACC_TOTAL = NACC * ACC_COLS;
   static constexpr int A_TCOLS = NMAT * BK / 2;  // TMEM columns of one A stage (two bf16 per column)
   static constexpr int SB = cmin(6, cmax(2, 49152 / B_BYTES));
@@ -113,18 +108,11 @@ struct Cfg {
   // ATM configs stage scale/bias rows by TMA (when the group count is a
   // multiple of 8): a chunk is 8 groups (16 bytes) x 128 rows per array,
   // arrays [matrix][scales, biases], SS chunks in flight
-  // (FQ: the epilogue reads the scales, a few groups further behind the
-  // producer than the dequantisers, so one more chunk)
-  static constexpr int SS = ATM ? (FQ ? 4 : 3) : 0;
+  static constexpr int SS = ATM ? 3 : 0;
   static constexpr int S_BYTES = NMAT * 2 * BM * 16;
   static constexpr int OFF_S = (OFF_TILE + (TILE_SMEM ? (2 * PLAN_MAX_GROUPS + 1) * 4 : 0) + 127) & ~127;
-  // FQ: the tile's per-pair group sums [FQ_GMAX][BN] and row scales [BN],
-  // double buffered by tile
-  static constexpr int FQ_GMAX = 64;
-  static constexpr int X_FLOATS = FQ_GMAX * BN + BN;
-  static constexpr int OFF_X = (OFF_S + SS * S_BYTES + 15) & ~15;
-  static constexpr int OFF_BAR = (OFF_X + (FQ ? 2 * X_FLOATS * 4 : 0) + 15) & ~15;
-  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC + 2 * SS + (FQ ? 2 : 0);
+  static constexpr int OFF_BAR = (OFF_S + SS * S_BYTES + 15) & ~15;
+  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * SP + 2 * NACC + 2 * SS;
   static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot/abort flag + align slack
   // dequantiser warps: 8, each thread one row of one matrix (gate / up), or
   // half a row of the single matrix (down); one TMEM lane quadrant per warp
@@ -135,7 +123,6 @@ struct Cfg {
   static_assert(TMEM_COLS <= 512, "tensor memory budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(B_SUB % 1024 == 0, "B tile must keep 1024-byte alignment");
-  static_assert(!FQ || (BITS != 16 && MODE == 1 && BN == 16 && ATM), "FQ: quantised gate/up at 16-wide tiles");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -238,12 +225,6 @@ __device__ __forceinline__ uint32_t idesc_bf16() {
          (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
-// The same with A and B f16 (the FQ operands).
-template <int BN>
-__device__ __forceinline__ uint32_t idesc_f16() {
-  return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
-}
-
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -279,16 +260,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -444,41 +415,6 @@ __device__ __forceinline__ void dequant_sub_regs(const uint4 (&v)[8], int j, con
   }
 }
 
-// FQ operand sub-stage j of a full row share: 64 weights as f16 (1024 + q),
-// exact, in K order (two per 32-bit word).  q8: the byte goes under the f16
-// exponent byte 0x64 (one PRMT per two weights).  q4: PRMT puts byte i of the
-// word and of the word >> 4 in the two halves, LOP3 keeps one nibble of each
-// and adds the exponent bits.
-template <int BITS>
-__device__ __forceinline__ void fq_sub_regs(const uint4 (&v)[8], int j, uint32_t (&out)[32]) {
-  if (BITS == 8) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 c = v[4 * j + q];
-      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        out[8 * q + 2 * i] = __byte_perm(w[i], 0x64u, 0x4140);
-        out[8 * q + 2 * i + 1] = __byte_perm(w[i], 0x64u, 0x4342);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const uint4 pv = v[2 * j + q];
-      const uint32_t w[4] = {pv.x, pv.y, pv.z, pv.w};
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const uint32_t w4 = w[h] >> 4;
-        out[16 * q + 4 * h + 0] = (__byte_perm(w[h], w4, 0x4400) & 0x000F000Fu) | 0x64006400u;
-        out[16 * q + 4 * h + 1] = (__byte_perm(w[h], w4, 0x5511) & 0x000F000Fu) | 0x64006400u;
-        out[16 * q + 4 * h + 2] = (__byte_perm(w[h], w4, 0x6622) & 0x000F000Fu) | 0x64006400u;
-        out[16 * q + 4 * h + 3] = (__byte_perm(w[h], w4, 0x7733) & 0x000F000Fu) | 0x64006400u;
-      }
-    }
-  }
-}
-
 // Operand sub-stage j (BK weights of row r) from the register share into the
 // SW128 bf16 tile.  FULL: all 8 output chunks; half rows: chunks 4 part .. +3.
 template <int BITS, bool FULL, bool FUSED>
@@ -532,10 +468,6 @@ struct Args {
   // dense_slot, B row = output row = position; counts / slot_ids / group_off /
   // perm are not read.  B tiles are then contiguous rows, loaded by TMA.
   int dense_rows, dense_slot;
-  // FQ: per B row, the sums of its prepared f16 values over each 64-column
-  // group ([in_rows][K/64]) and the power of two that undoes their scaling
-  const float* xsum;
-  const float* xscale;
 };
 
 struct Tile {
@@ -604,13 +536,13 @@ struct ScaleVec<1> {
 
 // STMA: scales and biases come from the TMA-staged chunk ring in shared
 // memory (8 groups per chunk) instead of per-thread global loads.
-template <int BITS, int MODE, int BN, int V, bool STMA, bool FQ = false>
+template <int BITS, int MODE, int BN, int V, bool STMA>
 __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, int U, int NT, int total,
                                              uint8_t* sA, const uint8_t* sP, uint64_t* a_full, uint64_t* a_empty,
                                              uint64_t* p_full, uint64_t* p_empty, Ctl ctl, uint32_t tmem_a,
                                              const int* gtab, const int* stab, const uint8_t* sS,
                                              uint64_t* s_full, uint64_t* s_empty) {
-  using C = Cfg<BITS, MODE, BN, FQ>;
+  using C = Cfg<BITS, MODE, BN>;
   constexpr bool DUAL = C::DUAL;
   // row r = 32 (warp % 4) + lane: the TMEM lane quadrant this warp may write
   const int warp = threadIdx.x >> 5;
@@ -688,9 +620,8 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
         }
-        float gs = 0.f, gb = 0.f;  // this sub-stage's scale and bias (FQ: applied by the epilogue)
-        if constexpr (FQ) {
-        } else if constexpr (STMA) {
+        float gs, gb;  // this sub-stage's scale and bias
+        if constexpr (STMA) {
           if ((kb & 7) == 0) {
             ok = wait_bar(&s_full[ss], sph, ctl);
             ok = __all_sync(0xffffffffu, ok);
@@ -724,12 +655,10 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
           gs = cur.sc(j);
           gb = cur.bi(j);
         }
-        GroupScale g{};
-        if constexpr (!FQ) g = make_scale<BITS>(sok ? gs : 0.f, sok ? gb : 0.f);
+        const GroupScale g = make_scale<BITS>(sok ? gs : 0.f, sok ? gb : 0.f);
         if (C::ATM) {
           uint32_t out[32];
-          if constexpr (FQ) fq_sub_regs<BITS>(pk, jp, out);
-          else if (g.fused) dequant_sub_regs<BITS, DUAL, true>(pk, jp, g, out);
+          if (g.fused) dequant_sub_regs<BITS, DUAL, true>(pk, jp, g, out);
           else dequant_sub_regs<BITS, DUAL, false>(pk, jp, g, out);
           tc_fence_after();
           const uint32_t ta = tmem_a + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
@@ -792,139 +721,13 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
   }
 }
 
-// FQ epilogue: 4 warps, thread = TMEM lane = weight row r of the tile.  For
-// each 64-weight group g of the tile the MMAs left
-//   A_g[r][t] = sum_{k in g} (1024 + q[r][k]) * x'[t][k]
-// in the group's accumulator (x' = the B row's prepared f16 values, exact
-// products, fp32 sums).  With the group's scale s and bias b (the TMA-staged
-// chunk) and X_g[t] = sum_{k in g} x'[t][k]:
-//   y[r][t] += s * A_g + (b - 1024 s) * X_g   (= sum_{k in g} (s q + b) x')
-// and y * 2^e[t] undoes the row's power-of-two prescale before SwiGLU.
-template <int BITS, int BN>
-__device__ __forceinline__ void epilogue_fq(const Args& args, const int* plan, int U, int NT, int total,
-                                            const int* gtab, const int* stab, uint32_t tmem, uint64_t* acc_full,
-                                            uint64_t* acc_empty, const uint8_t* sS, uint64_t* s_full,
-                                            uint64_t* s_empty, uint64_t* x_full, float* sX, Ctl ctl) {
-  using C = Cfg<BITS, 1, BN, true>;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = warp & 3, r = quad * 32 + lane;
-  const int et = threadIdx.x - C::EPI_WARP0 * 32;  // 0..127 over the epilogue warps
-  const int NKB = args.K / BK, G = args.K / 64;
-  const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-  // group sums of a tile's B rows, staged in shared memory [FQ_GMAX][BN] plus
-  // the rows' scales [BN]: thread et loads column tc of groups g0 + GS j, the
-  // next tile's values one tile ahead
-  constexpr int GS = 128 / BN;
-  constexpr int XPT = C::FQ_GMAX / GS;
-  const int tc = et % BN, g0 = et / BN;
-  float xr[XPT], xsc = 0.f;
-  auto fetch = [&](int tt) {
-    const Tile tl = tile_of<BN>(tt, plan, U, NT, args, gtab, stab);
-    int rw = -1;
-    if (tc < tl.nvalid) {
-      const int pos = tl.goff + tl.n0 + tc;
-      rw = args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
-      if (rw < 0 || rw >= args.in_rows) rw = -1;
-    }
-#pragma unroll
-    for (int j = 0; j < XPT; ++j) {
-      const int g = g0 + GS * j;
-      xr[j] = (rw >= 0 && g < G) ? __ldg(args.xsum + (size_t)rw * G + g) : 0.f;
-    }
-    xsc = rw >= 0 ? __ldg(args.xscale + rw) : 0.f;
-  };
-  int t = blockIdx.x;
-  if (t < total) fetch(t);
-  int git = 0, ss = 0, it = 0;
-  uint32_t sph = 0;
-  bool ok = true;
-  for (; t < total && ok; t += gridDim.x, ++it) {
-    const Tile tl = tile_of<BN>(t, plan, U, NT, args, gtab, stab);
-    const int tb = it & 1;
-    float* X = sX + tb * C::X_FLOATS;
-    // every warp has passed the previous tile's staging, so none still reads
-    // this buffer (last used two tiles ago)
-#pragma unroll
-    for (int j = 0; j < XPT; ++j) X[(g0 + GS * j) * BN + tc] = xr[j];
-    if (g0 == 0) X[C::FQ_GMAX * BN + tc] = xsc;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&x_full[tb]);
-    ok = wait_bar(&x_full[tb], static_cast<uint32_t>((it >> 1) & 1), ctl);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok) break;
-    if (t + gridDim.x < total) fetch(t + gridDim.x);
-    float yg[BN], yu[BN];
-#pragma unroll
-    for (int i = 0; i < BN; ++i) yg[i] = yu[i] = 0.f;
-    for (int kb = 0; kb < NKB; ++kb) {
-      if ((kb & 7) == 0) {
-        ok = wait_bar(&s_full[ss], sph, ctl);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
-      const int gb = git % C::NACC;
-      ok = wait_bar(&acc_full[gb], static_cast<uint32_t>((git / C::NACC) & 1), ctl);
-      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t a[32];
-      tmem_ld32(tmem + lane_off + gb * C::ACC_COLS, a);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[gb]);
-      ++git;
-      const uint8_t* sc = sS + ss * C::S_BYTES + r * 16 + (kb & 7) * 2;
-      const float s0 = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc));
-      const float b0 = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc + BM * 16));
-      const float s1 = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc + 2 * BM * 16));
-      const float b1 = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc + 3 * BM * 16));
-      const float c0 = __fmaf_rn(-1024.f, s0, b0), c1 = __fmaf_rn(-1024.f, s1, b1);
-      const float4* xg = reinterpret_cast<const float4*>(X + kb * BN);
-#pragma unroll
-      for (int q = 0; q < BN / 4; ++q) {
-        const float4 xv = xg[q];
-        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int tt = 4 * q + i;
-          yg[tt] = __fmaf_rn(s0, __uint_as_float(a[tt]), __fmaf_rn(c0, xs[i], yg[tt]));
-          yu[tt] = __fmaf_rn(s1, __uint_as_float(a[BN + tt]), __fmaf_rn(c1, xs[i], yu[tt]));
-        }
-      }
-      if ((kb & 7) == 7) {  // scale chunk done (group counts are multiples of 8)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[ss]);
-        if (++ss == C::SS) { ss = 0; sph ^= 1; }
-      }
-    }
-    if (!ok) break;
-    const bool slot_ok = tl.slot >= 0 && tl.slot < args.num_slots;
-    const int ocol = tl.m * BM + r;
-    int my_row = 0;
-    if (lane < tl.nvalid) {
-      const int pos = tl.goff + tl.n0 + lane;
-      my_row = args.out_by_pos ? pos : args.perm[pos];
-    }
-    const float* xs_sc = X + C::FQ_GMAX * BN;
-#pragma unroll
-    for (int jj = 0; jj < BN; ++jj) {
-      const int orow = __shfl_sync(0xffffffffu, my_row, jj);
-      if (jj < tl.nvalid) {
-        const float e = xs_sc[jj];
-        args.out[(size_t)orow * args.OUT + ocol] = slot_ok ? swiglu_bf16(yg[jj] * e, yu[jj] * e) : 0;
-      }
-    }
-  }
-}
-
-template <int BITS, int MODE, int BN, bool STMA, bool FQ = false>
-__global__ void __launch_bounds__(Cfg<BITS, MODE, BN, FQ>::THREADS, 1)
+template <int BITS, int MODE, int BN, bool STMA>
+__global__ void __launch_bounds__(Cfg<BITS, MODE, BN>::THREADS, 1)
 glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS0,
               const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__ CUtensorMap tmS1,
               const __grid_constant__ CUtensorMap tmQ1, const Args args) {
-  using C = Cfg<BITS, MODE, BN, FQ>;
+  using C = Cfg<BITS, MODE, BN>;
   constexpr bool DUAL = C::DUAL;
   constexpr int RO1 = MODE == 2 ? BM : 0;  // row offset of the second matrix
   extern __shared__ uint8_t smem_raw[];
@@ -948,8 +751,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   uint64_t* acc_full = p_empty + C::SP;      // [NACC] accumulator ready (MMA commit)
   uint64_t* acc_empty = acc_full + C::NACC;  // [NACC] accumulator drained (4 epilogue warps)
   uint64_t* s_full = acc_empty + C::NACC;    // [SS] scale chunk landed (TMA tx)
-  uint64_t* s_empty = s_full + C::SS;        // [SS] scale chunk consumed (dequantiser warps; FQ: epilogue)
-  uint64_t* x_full = s_empty + C::SS;        // FQ [2] a tile's group sums staged (4 epilogue warps)
+  uint64_t* s_empty = s_full + C::SS;        // [SS] scale chunk consumed (dequantiser warps)
   const uint8_t* sS = smem + C::OFF_S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -979,11 +781,7 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     }
     for (int i = 0; i < C::SS; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], FQ ? 4 : C::DQW);  // FQ: the epilogue warps read the scales
-    }
-    if (FQ) {
-      mbar_init(&x_full[0], 4);
-      mbar_init(&x_full[1], 4);
+      mbar_init(&s_empty[i], C::DQW);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1203,20 +1001,18 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = FQ ? idesc_f16<BN>() : idesc_bf16<BN>();
+      const uint32_t idesc = idesc_bf16<BN>();
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
-      int it = 0, git = 0;  // tiles, FQ groups
+      int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const int ab = it % C::NACC;
         const uint32_t accp = static_cast<uint32_t>((it / C::NACC) & 1);
-        if (!FQ) {
-          ok = wait_bar(&acc_empty[ab], accp ^ 1, ctl);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        uint32_t d0 = tmem + ab * C::ACC_COLS;
+        ok = wait_bar(&acc_empty[ab], accp ^ 1, ctl);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + ab * C::ACC_COLS;
         for (int kb = 0; kb < NKB; ++kb) {
           const int jb = kb % C::KBB;  // operand stage within the B stage
           if (jb == 0) ok = wait_bar(&b_full[sb], pb, ctl);
@@ -1229,23 +1025,14 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             if (sl >= C::SA) { sl -= C::SA; ph ^= 1; }
             ok = wait_bar(&a_full[sl], ph, ctl);
           }
-          int gb = 0;
-          if (FQ && ok) {
-            // this 64-weight group's accumulator: drained by the epilogue
-            // NACC groups ago
-            gb = git % C::NACC;
-            ok = wait_bar(&acc_empty[gb], static_cast<uint32_t>((git / C::NACC) & 1) ^ 1, ctl);
-            d0 = tmem + gb * C::ACC_COLS;
-          }
           if (!ok) break;
           tc_fence_after();
           const uint32_t b_base = smem_u32(sB + sb * C::B_BYTES + jb * C::B_SUB);
-          const uint32_t acc0 = FQ ? 0u : static_cast<uint32_t>(kb != 0);
           if (C::ATM) {
             const uint32_t a_t = tmem + C::ACC_TOTAL + sa * C::NMAT * (BK / 2);
             const uint64_t bd0 = desc_sw128(b_base);  // +2 per 32-byte K step (address field is addr >> 4)
-            umma_bf16_ts(d0, a_t, bd0, idesc, acc0);
-            if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2, bd0, idesc, acc0);
+            umma_bf16_ts(d0, a_t, bd0, idesc, kb != 0);
+            if (DUAL) umma_bf16_ts(d0 + BN, a_t + BK / 2, bd0, idesc, kb != 0);
 #pragma unroll
             for (int kk = 1; kk < BK / 16; ++kk) {
               umma_bf16_ts(d0, a_t + kk * 8, bd0 + 2 * kk, idesc, 1u);
@@ -1262,25 +1049,21 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             }
           }
           umma_commit(&a_empty[sa]);
-          if (FQ) {
-            umma_commit(&acc_full[gb]);
-            ++git;
-          }
           if (++sa == C::SA) { sa = 0; pa ^= 1; }
           if (jb == C::KBB - 1 || kb == NKB - 1) {
             umma_commit(&b_empty[sb]);
             if (++sb == C::SB) { sb = 0; pb ^= 1; }
           }
         }
-        if (ok && !FQ) umma_commit(&acc_full[ab]);
+        if (ok) umma_commit(&acc_full[ab]);
       }
     }
   } else if (warp >= DQ_WARP0 && warp < C::EPI_WARP0) {
     // ---------------------------------------------------------------- dequantisers
     if (BITS != 16) {
       if constexpr (STMA)
-        dequant_role<BITS, MODE, BN, 1, true, FQ>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full,
-                                                  p_empty, ctl, tmem, gtab, stab, sS, s_full, s_empty);
+        dequant_role<BITS, MODE, BN, 1, true>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
+                                              ctl, tmem, gtab, stab, sS, s_full, s_empty);
       else if ((K / 64) % 4 == 0)
         dequant_role<BITS, MODE, BN, 4, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
                                                ctl, tmem, gtab, stab, sS, s_full, s_empty);
@@ -1288,10 +1071,6 @@ glu_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         dequant_role<BITS, MODE, BN, 1, false>(args, plan, U, NT, total, sA, sP, a_full, a_empty, p_full, p_empty,
                                                ctl, tmem, gtab, stab, sS, s_full, s_empty);
     }
-  } else if constexpr (FQ) {
-    // ---------------------------------------------------------------- epilogue, factored scales
-    epilogue_fq<BITS, BN>(args, plan, U, NT, total, gtab, stab, tmem, acc_full, acc_empty, sS, s_full, s_empty,
-                          x_full, reinterpret_cast<float*>(smem + C::OFF_X), ctl);
   } else {
     // ---------------------------------------------------------------- epilogue (last 4 warps)
     const int quad = warp & 3;
@@ -1453,24 +1232,6 @@ static int launch_cfg(const sg_arena* A, const Args& args_in, cudaStream_t s) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done[dev] = true;
   }
-  if (args.xsum) {  // factored-scale gate/up over prepared rows
-    if constexpr (MODE == 1 && BN == 16 && BITS != 16) {
-      using CF = Cfg<BITS, 1, 16, true>;
-      if (!scale_tma || groups > CF::FQ_GMAX || !args.xscale) return SG_ERR_SHAPE;
-      static bool fq_attr_done[64] = {};
-      if (!fq_attr_done[dev]) {
-        SG_CUDA_TRY(cudaFuncSetAttribute(glu_tc_kernel<BITS, 1, 16, true, true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM));
-        fq_attr_done[dev] = true;
-      }
-      glu_tc_kernel<BITS, 1, 16, true, true><<<num_sms(), CF::THREADS, CF::SMEM, s>>>(m0, m1, mb, ms0, mq0, ms1, mq1,
-                                                                                     args);
-      SG_LAUNCH_CHECK();
-      return SG_OK;
-    } else {
-      return SG_ERR_SHAPE;
-    }
-  }
   int grid = num_sms();
   if (args.dense_rows > 0) {  // the tile count is known on the host: no idle CTAs
     const int tiles = (args.OUT / C::ROWS) * ((args.dense_rows + BN - 1) / BN);
@@ -1522,14 +1283,6 @@ static int pick_bn(int P, int grid_groups) {
   return 128;
 }
 
-// Factored-scale gate/up (FQ): quantised arenas, 16-wide pair tiles, scale
-// chunks by TMA (groups a multiple of 8) and at most FQ_GMAX groups per row.
-bool tc_fq_supported(const sg_arena* A, int P, int grid_groups) {
-  const int groups = A->hidden / 64;
-  return A->bits != 16 && pick_bn(P, grid_groups) == 16 && groups % 8 == 0 &&
-         groups <= tc::Cfg<8, 1, 16, true>::FQ_GMAX;
-}
-
 bool tc_supported(const sg_arena* A, bool dual, int grid_groups) {
   const int K = dual ? A->hidden : A->inter;
   const int OUT = dual ? A->inter : A->hidden;
@@ -1540,11 +1293,8 @@ bool tc_supported(const sg_arena* A, bool dual, int grid_groups) {
 
 int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_by_pos,
                   int out_by_pos, int P, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                  const int32_t* perm, int grid_groups, uint16_t* out, const float* xsum, const float* xscale,
-                  cudaStream_t s) {
+                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s) {
   tc::Args a;
-  a.xsum = xsum;
-  a.xscale = xscale;
   a.num_slots = A->num_slots;
   a.K = dual ? A->hidden : A->inter;
   a.OUT = dual ? A->inter : A->hidden;
@@ -1565,7 +1315,7 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   a.out = out;
   a.dense_rows = 0;
   a.dense_slot = 0;
-  const int bn = xsum ? 16 : pick_bn(P, grid_groups);
+  const int bn = pick_bn(P, grid_groups);
   switch (A->bits) {
     case 16: return tc::launch_mode<16>(A, tc::mode_of(dual, a.OUT), bn, a, s);
     case 8: return tc::launch_mode<8>(A, tc::mode_of(dual, a.OUT), bn, a, s);

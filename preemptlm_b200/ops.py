@@ -136,20 +136,6 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int =
     return h
 
 
-def _glu_gate_up_raw(arena, src: torch.Tensor, device, d: Dispatch, pair_div: int, flags: int) -> torch.Tensor:
-    """``sg_glu_gate_up`` on bf16 rows or on a prepared scratch (any dtype)."""
-    P = d.perm.numel()
-    h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=device)
-    if P == 0:
-        return h
-    LAUNCHES[0] += 1
-    _abi.check(_abi.load().sg_glu_gate_up(ctypes.byref(arena.desc()), src.data_ptr(), P, int(pair_div),
-                                          d.counts.data_ptr(), d.slot_ids.data_ptr(), d.group_off.data_ptr(),
-                                          d.perm.data_ptr(), d.grid_groups, h.data_ptr(), int(flags), _stream()),
-               "sg_glu_gate_up")
-    return h
-
-
 def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0) -> torch.Tensor:
     """y = h @ down^T over the arena (``sg_glu_down``)."""
     h = _bf16_2d(h, "h")
@@ -185,45 +171,30 @@ def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: d
     x = _bf16_2d(x, "x")
     P = d.perm.numel()
     lib = _abi.load()
-    desc = ctypes.byref(arena.desc())
-    nbytes = lib.sg_glu_scratch_bytes(desc, P, int(pair_div), d.grid_groups) if P else 0
-    _abi.check(min(0, nbytes), "sg_glu_scratch_bytes")
-    xs = torch.empty(nbytes, dtype=torch.uint8, device=x.device) if nbytes else None
     if timing is None:
         y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device)
         if P == 0:
             return y
         h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
-        LAUNCHES[0] += 3 if nbytes else 2
-        _abi.check(lib.sg_glu_forward(desc, x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
+        permute = lib.sg_glu_use_permute(ctypes.byref(arena.desc()), P, d.grid_groups) == 1
+        xs = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device) if permute else None
+        LAUNCHES[0] += 3 if permute else 2
+        _abi.check(lib.sg_glu_forward(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                       d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                       None if xs is None else xs.data_ptr(), h.data_ptr(), y.data_ptr(), _stream()),
                    "sg_glu_forward")
         return y
+    permute = P > 0 and lib.sg_glu_use_permute(ctypes.byref(arena.desc()), P, d.grid_groups) == 1
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    ev[0].record()  # the gate/up interval includes the input preparation
-    fl = 0
-    if P:
-        fl = lib.sg_glu_prep(desc, x.data_ptr(), P, int(pair_div), d.perm.data_ptr(), d.grid_groups,
-                             None if xs is None else xs.data_ptr(), _stream())
-        _abi.check(min(0, fl), "sg_glu_prep")
-        LAUNCHES[0] += 1 if fl else 0
-    src = x if fl == 0 else xs
-    h = _glu_gate_up_raw(arena, src, x.device, d, pair_div, fl | _abi.SG_OUT_DISPATCH_ORDER)
+    src, fl = (permute_rows(x, d, pair_div), _abi.SG_IN_DISPATCH_ORDER) if permute else (x, 0)
+    ev[0].record()
+    h = glu_gate_up(arena, src, d, pair_div, fl | _abi.SG_OUT_DISPATCH_ORDER)
     ev[1].record()
     y = glu_down(arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
     ev[2].record()
     timing.setdefault("events", []).append(ev)
     timing.setdefault("dispatch", []).append(d)
     return y
-
-
-def glu_scratch_bytes(arena, num_pairs: int, pair_div: int, grid_groups: int) -> int:
-    """Bytes of the prepared-row scratch ``sg_glu_forward`` takes for this
-    problem (``sg_glu_scratch_bytes``; 0: none)."""
-    n = _abi.load().sg_glu_scratch_bytes(ctypes.byref(arena.desc()), int(num_pairs), int(pair_div), int(grid_groups))
-    _abi.check(min(0, n), "sg_glu_scratch_bytes")
-    return int(n)
 
 
 def gather_forward_noalloc(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
@@ -264,7 +235,7 @@ def dense_glu(arena, x: torch.Tensor, sid: int = 0) -> torch.Tensor | None:
     return y
 
 
-GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2, "tc-perm": 3, "tc-exact": 4}
+GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2, "tc-perm": 3}
 
 
 _GLU_PATH = ["auto"]

@@ -13,7 +13,7 @@ from preemptlm_b200 import ops
 from preemptlm_b200.synthetic import CONFIGS, LayerConfig, make_layer, make_tokens
 from preemptlm_b200.layer import Qwen3_xMoEWrapper
 
-from ._util import LazyExperts, assert_close, bits16, bits32, f32
+from ._util import LazyExperts, assert_close, bits16, f32
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -149,72 +149,8 @@ def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
     assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what="y|h")
     # the fused call (h kept in dispatch order, token rows permuted first under
-    # "tc-perm"): bf16 arenas run the same kernels' arithmetic, so the same
-    # bits; quantised decode-sized groups take the factored-scale gate/up
-    # (exact s*q + b, no bf16 rounding of the weights), within the tolerance
-    yf = ops.gather_forward(block.switch_mlp, x, d, k)
-    if bits == 16 or glu_path == "gemv":
-        assert torch.equal(yf, y)
-    else:
-        assert_close(f32(yf), yref, max_abs=2e-2 * max(1.0, float(np.abs(yref).max())), what="y fused")
-
-
-def _fq_reference(tens, bits, inds, xf, k):
-    """Per pair, the exact sum of (s q + b) x in float64 (no bf16 rounding of
-    the weights) through the oracle's SwiGLU, then the oracle's bf16-weight
-    down projection of that bf16 h."""
-    ex = LazyExperts(tens["experts"], bits)
-    raw = tens["experts"]
-    cache = {}
-    P = inds.size
-    hq = np.zeros((P, raw["gate_proj.scales"].shape[1]), np.float32)
-    for p in range(P):
-        e = int(inds.reshape(-1)[p])
-        if e not in cache:
-            mats = []
-            for name in ("gate_proj", "up_proj"):
-                q = orc.unpack_affine(bits32(raw[f"{name}.weight"][e]), bits).astype(np.float64)
-                sc = np.repeat(orc.bf16_bits_to_f32(bits16(raw[f"{name}.scales"][e])), 64, axis=1)
-                bi = np.repeat(orc.bf16_bits_to_f32(bits16(raw[f"{name}.biases"][e])), 64, axis=1)
-                mats.append(sc * q + bi)
-            cache[e] = mats
-        g = (cache[e][0] @ xf[p // k].astype(np.float64)).astype(np.float32)
-        u = (cache[e][1] @ xf[p // k].astype(np.float64)).astype(np.float32)
-        hq[p] = orc.swiglu(u[None], g[None])[0]
-    yq = np.stack([orc._mm_bf16(hq[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(P)])
-    return hq, yq
-
-
-@pytest.mark.parametrize("glu_path", ["auto", "tc-perm"], indirect=True)
-@pytest.mark.parametrize("bits", [8, 4])
-def test_factored_gate_up_edge_rows(glu_path, bits):
-    """Decode-sized groups through sg_glu_forward take the factored-scale
-    gate/up over prepared f16 rows.  Rows whose magnitudes overflow f16
-    (1e6), are tiny (1e-15), all zero, or span 2^40 between elements keep the
-    result of the exact sum thanks to each row's power-of-two prescale."""
-    H, I, E, T, k = 2048, 512, 32, 24, 4
-    cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
-    block, tens = make_layer(cfg, device=DEV)
-    x = _bf16((T, H), 5)
-    x[1] *= 1e6
-    x[2] *= 1e-15
-    x[3] = 0
-    x[4, ::2] *= 2.0 ** 40
-    g = np.random.default_rng(3)
-    inds = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
-    d = ops.dispatch(torch.from_numpy(inds).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
-    P = T * k
-    nbytes = ops.glu_scratch_bytes(block.switch_mlp, P, k, d.grid_groups)
-    R = P if glu_path == "tc-perm" else T
-    assert nbytes == R * H * 2 + R * (H // 64) * 4 + (R * 4 + 255) // 256 * 256  # the prepared-row layout
-    y = ops.gather_forward(block.switch_mlp, x, d, k)
-    xf = f32(x)
-    _, yq = _fq_reference(tens, bits, inds, xf, k)
-    for t in range(T):
-        rows = slice(t * k, (t + 1) * k)
-        scale = max(1.0, float(np.abs(yq[rows]).max()))
-        assert_close(f32(y)[rows], yq[rows], max_abs=2e-2 * scale, what=f"token row {t}")
-    assert torch.all(y[3 * k: 4 * k] == 0)
+    # "tc-perm"): the same kernels' arithmetic, so the same bits
+    assert torch.equal(ops.gather_forward(block.switch_mlp, x, d, k), y)
 
 
 @pytest.mark.parametrize("bits", [16, 8, 4])
