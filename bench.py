@@ -63,7 +63,9 @@ def parse_args():
     ap.add_argument("--no-shared", action="store_true", help="drop the shared expert (profiling cases)")
     ap.add_argument("--glu-path", choices=("auto", "gemv", "tc", "tc-perm"), default="auto")
     ap.add_argument("--microbatches", type=int, default=None,
-                    help="expert-parallel micro-batches per step (default 2 when N > 1)")
+                    help="expert-parallel micro-batches per step (default: 1 with the p2p exchange, 2 with NCCL)")
+    ap.add_argument("--ep-transport", choices=("p2p", "collective"), default="p2p",
+                    help="expert-parallel exchange: the library's NVLink peer-memory kernels or NCCL all-to-alls")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed device-resident steps (for ncu captures); prints ms/step")
     return ap.parse_args()
@@ -265,6 +267,8 @@ def _kernel_roofline(cfg, timing, rows_per_step, T_local):
     for i, (ev, d) in enumerate(zip(timing["events"], timing["dispatch"])):
         U = int(d.counts[0].item())
         P = rows_per_step[i] if rows_per_step else T_local * k
+        if not isinstance(P, int):  # a dispatch over padded inboxes: its filled entries
+            P = int(P.group_off[int(P.counts[0])].item())
         n_in = T_local if not rows_per_step else P  # distinct input rows read
         us.append(U)
         gu_ms.append(ev[0].elapsed_time(ev[1]))
@@ -304,8 +308,9 @@ def run_ours(args, rank, world, local_rank):
         from preemptlm_b200.ep import ExpertParallelMoE, shard_layer
 
         backend, _ = shard_layer(cfg, rank, world, dev)
-        ep = ExpertParallelMoE(backend, cfg.num_experts, H, cfg.top_k)
-        mb = args.microbatches or 2
+        mb = args.microbatches or (1 if args.ep_transport == "p2p" else 2)
+        ep = ExpertParallelMoE(backend, cfg.num_experts, H, cfg.top_k, transport=args.ep_transport,
+                               max_tokens=-(-T // mb))
 
         def step(x):
             # the step's tokens in mb micro-batches, every count exchange queued
@@ -380,6 +385,7 @@ def run_ours(args, rank, world, local_rank):
             print(json.dumps({"profile": cfg.name, "experts": cfg.num_experts, "tokens": T, "ms_per_step": ms_step,
                           "steps_detail": step_stats}))
         if world > 1:
+            ep.close()
             dist.destroy_process_group()
         return
     rl = _kernel_roofline(cfg, timing, timing.get("rows"), T)
@@ -455,7 +461,8 @@ def run_ours(args, rank, world, local_rank):
             "l2": "no flush: each step streams >126 MB (L2) of expert weights per GPU",
             "queue": "device-resident steps are queued behind a bounded device spin (not timed); e2e is not",
             "parallelism": f"ep{world}",
-            "microbatches": (args.microbatches or 2) if world > 1 else 1,
+            "microbatches": mb if world > 1 else 1,
+            "exchange": args.ep_transport if world > 1 else None,
         },
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
@@ -489,6 +496,7 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier()
+        ep.close()
         dist.destroy_process_group()
 
 

@@ -212,6 +212,51 @@ int sg_refill_h2d(const void* blob, size_t blob_len, const sg_arena* arena,
 /* Byte size of one expert blob in the arena's format. */
 size_t sg_expert_bytes(const sg_arena* arena);
 
+/* ------------------------------------------ expert-parallel exchange (e)
+ * The dispatch / combine all-to-alls of one expert-parallel layer over
+ * NVLink peer memory, one process per GPU, R <= 8 ranks in lockstep.  No
+ * counterpart in the reference (it runs on one device); these replace the
+ * NCCL counts / rows / outputs all-to-alls of the expert-parallel layer.
+ *
+ * Each rank allocates one region (sg_ep_alloc, sg_ep_region_bytes(R, cap, H)
+ * bytes, zeroed), exports it with sg_ep_ipc_handle, and opens every peer's
+ * with sg_ep_ipc_open; `regions` lists all R regions in this process's
+ * address space (its own included), in rank order.  cap = the most tokens
+ * per rank per step times k.  Per step (seq = 1, 2, ...; the same on all
+ * ranks):
+ *   sg_ep_send(regions, R, me, cap, H, x [T, H], inds [T, k] global expert
+ *     ids, T, k, per = experts per rank, pos [T*k] and dcnt [R] int32
+ *     scratch, seq): every pair's token row, local expert id and pair id
+ *     into its owner's inbox, then that rank's step flag (T * k <= cap);
+ *   sg_ep_wait_inbox(own region, ..., seq): waits for every source's flag
+ *     and marks unused inbox entries empty (expert id -1);
+ *   sg_dispatch + sg_glu_gate_up / sg_glu_down then run over the R * cap
+ *     inbox rows and ids (sg_ep_layout gives their offsets) in place;
+ *   sg_ep_send_back(regions, ..., y [R * cap, H], seq): each filled entry's
+ *     output row to its source, at its pair id, then the step flag;
+ *   sg_ep_wait_back(own region, ..., seq): waits for every owner's flag; the
+ *     region's pair-order output rows ([T * k, H], offset 4 of sg_ep_layout)
+ *     are then complete for sg_combine.
+ * Every wait is bounded (about 2 s); on expiry sg_device_status reports
+ * SG_ERR_TIMEOUT.  Calls of one exchange must be issued on one stream.
+ * Allocation, IPC and freeing are set-up calls (they synchronise); free a
+ * region only after every rank has stopped using it. */
+long long sg_ep_region_bytes(int R, int cap, int H);
+/* offsets5: byte offsets of rows [R*cap][H] bf16, eids [R*cap] int32,
+ * pair ids [R*cap] int32, counts [R] int32, outputs [cap][H] bf16. */
+int sg_ep_layout(int R, int cap, int H, long long* offsets5);
+int sg_ep_alloc(long long bytes, void** region);
+int sg_ep_free(void* region);
+int sg_ep_ipc_handle(void* region, uint8_t* handle64);
+int sg_ep_ipc_open(const uint8_t* handle64, void** region);
+int sg_ep_ipc_close(void* region);
+int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x, const int32_t* inds,
+               int T, int k, int per, int32_t* pos, int32_t* dcnt, unsigned int seq, void* stream);
+int sg_ep_wait_inbox(void* region, int R, int cap, int H, unsigned int seq, void* stream);
+int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y, unsigned int seq,
+                    void* stream);
+int sg_ep_wait_back(void* region, int R, int cap, int H, unsigned int seq, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,8 @@ EXPORTED_SYMBOLS = (
     "sg_dispatch", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_use_permute", "sg_permute_rows", "sg_glu_gate_up", "sg_glu_down",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
+    "sg_ep_region_bytes", "sg_ep_layout", "sg_ep_alloc", "sg_ep_free", "sg_ep_ipc_handle", "sg_ep_ipc_open",
+    "sg_ep_ipc_close", "sg_ep_send", "sg_ep_wait_inbox", "sg_ep_send_back", "sg_ep_wait_back",
 )
 
 
@@ -69,7 +71,7 @@ def load() -> ctypes.CDLL:
             "(python -m preemptlm_b200.build); there is no CPU fallback"
         )
     lib = ctypes.CDLL(str(path))
-    P, I32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    P, I32, U32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_size_t
     A = ctypes.POINTER(sg_arena)
     sigs = {
         "sg_status_string": (ctypes.c_char_p, [I32]),
@@ -90,6 +92,17 @@ def load() -> ctypes.CDLL:
         "sg_combine": (I32, [P, P, I32, I32, I32, P, P, P, P]),
         "sg_refill_h2d": (I32, [P, SZ, A, I32, P]),
         "sg_expert_bytes": (SZ, [A]),
+        "sg_ep_region_bytes": (ctypes.c_longlong, [I32, I32, I32]),
+        "sg_ep_layout": (I32, [I32, I32, I32, P]),
+        "sg_ep_alloc": (I32, [ctypes.c_longlong, P]),
+        "sg_ep_free": (I32, [P]),
+        "sg_ep_ipc_handle": (I32, [P, P]),
+        "sg_ep_ipc_open": (I32, [P, P]),
+        "sg_ep_ipc_close": (I32, [P]),
+        "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P, U32, P]),
+        "sg_ep_wait_inbox": (I32, [P, I32, I32, I32, U32, P]),
+        "sg_ep_send_back": (I32, [P, I32, I32, I32, I32, P, U32, P]),
+        "sg_ep_wait_back": (I32, [P, I32, I32, I32, U32, P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

@@ -1,0 +1,420 @@
+// Expert-parallel token exchange over NVLink peer memory (row e): the
+// dispatch and combine all-to-alls of one slotted MoE layer split over R
+// GPUs, one process per GPU, without any host round trip.
+//
+// Every rank owns one region of device memory (cudaMalloc'd here, mapped into
+// the other ranks' address spaces by CUDA IPC), laid out identically on all
+// ranks (EpLayout):
+//   rows  [R][CAP][H] bf16  token rows sent to this rank, one inbox per source
+//   eid   [R][CAP]    int32 their local expert ids (-1: empty entry)
+//   pid   [R][CAP]    int32 their pair ids at the source (t * k + j)
+//   cnt   [R]         int32 rows in each inbox
+//   ybuf  [CAP][H]    bf16  expert outputs of this rank's own pairs, in pair
+//                           order, written back by the owning ranks
+//   flag_in [R], flag_back [R] uint32: the step number whose inbox rows /
+//                           outputs from rank s are complete
+// CAP = max tokens per step x k, the most pairs one source can route to one
+// destination, so no inbox can overflow whatever the routing.
+//
+// A step (seq = 1, 2, ... in lockstep on all ranks):
+//   sg_ep_send:      plan (stable position of every pair within its
+//                    destination) and copy each pair's token row, expert id
+//                    and pair id into the destination's inbox; the last CTA
+//                    publishes the counts and raises flag_in[me] = seq at
+//                    every destination (system-scope release)
+//   sg_ep_wait_inbox: acquire flag_in[s] >= seq for every source s, then mark
+//                    the unused inbox entries empty (eid -1, ignored by
+//                    sg_dispatch)
+//   (sg_dispatch + sg_glu_forward run on the inboxes in place)
+//   sg_ep_send_back: copy each output row to its source's ybuf at its pair
+//                    id; the last CTA raises flag_back[me] = seq there
+//   sg_ep_wait_back: acquire flag_back[d] >= seq for every destination d
+//   (sg_combine reads ybuf)
+// Buffer reuse across steps is safe by program order: a rank writes the next
+// step's rows into a peer's inbox only after it saw that peer's outputs of
+// this step (so the peer's GLU is done with its inbox), and writes outputs
+// into a source's ybuf only after the source's next-step rows arrived (so
+// the source's combine of the previous step is done).
+//
+// Every wait is bounded (about two seconds of clock64); on expiry the kernel
+// records SG_ERR_TIMEOUT (read with sg_device_status), empties the inboxes
+// it was waiting for and returns.  No TMA, no multicast: plain 16-byte peer
+// loads and stores.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "sg_common.cuh"
+
+namespace sg {
+
+__device__ int g_ep_status = 0;
+__device__ unsigned int g_ep_send_done = 0;  // CTAs of sg_ep_send finished (last one publishes)
+__device__ unsigned int g_ep_back_done = 0;  // CTAs of sg_ep_send_back finished
+
+constexpr int EP_MAX_RANKS = 8;
+constexpr long long EP_WAIT_CYCLES = 4000000000LL;  // ~2 s
+
+struct EpLayout {
+  size_t rows, eid, pid, cnt, ybuf, flag_in, flag_back, bytes;
+};
+
+static size_t ep_align(size_t v) { return (v + 255) & ~size_t(255); }
+
+static EpLayout ep_layout(int R, int cap, int H) {
+  EpLayout l;
+  size_t o = 0;
+  l.rows = o;
+  o += ep_align((size_t)R * cap * H * 2);
+  l.eid = o;
+  o += ep_align((size_t)R * cap * 4);
+  l.pid = o;
+  o += ep_align((size_t)R * cap * 4);
+  l.cnt = o;
+  o += ep_align((size_t)R * 4);
+  l.ybuf = o;
+  o += ep_align((size_t)cap * H * 2);
+  l.flag_in = o;
+  o += ep_align((size_t)R * 4);
+  l.flag_back = o;
+  o += ep_align((size_t)R * 4);
+  l.bytes = o;
+  return l;
+}
+
+struct EpPeers {
+  uint8_t* base[EP_MAX_RANKS];  // every rank's region in this process's address space (own one included)
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for *flag >= seq (flags only grow); false on expiry.
+__device__ bool ep_wait_flag(const uint32_t* flag, uint32_t seq) {
+  if (ld_acquire_sys(flag) >= seq) return true;
+  const long long t0 = clock64();
+  while (true) {
+    __nanosleep(256);
+    if (ld_acquire_sys(flag) >= seq) return true;
+    if (clock64() - t0 > EP_WAIT_CYCLES) {
+      atomicCAS(&g_ep_status, 0, SG_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// One row by one warp, 16-byte chunks, four loads in flight per lane before
+// their stores (the destination is usually another GPU's memory).
+__device__ __forceinline__ void copy_row(uint4* dst, const uint4* src, int chunks, int lane) {
+  for (int c0 = lane; c0 < chunks; c0 += 128) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c0 + 32 * u < chunks) v[u] = ldg_nc_v4(src + c0 + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c0 + 32 * u < chunks) dst[c0 + 32 * u] = v[u];
+  }
+}
+
+// Stable position of every pair within its destination rank, and the pair
+// count per destination.  One CTA of 1024 threads; pairs in chunks of 1024,
+// per-destination ranks by warp ballots, warp totals scanned per destination.
+constexpr int EP_PLAN_THREADS = 1024;
+__global__ void __launch_bounds__(EP_PLAN_THREADS)
+ep_plan_kernel(const int32_t* __restrict__ inds, int P, int per, int R, int32_t* __restrict__ pos,
+               int32_t* __restrict__ dcnt) {
+  __shared__ int wtot[32][EP_MAX_RANKS];
+  __shared__ int base[EP_MAX_RANKS];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x < EP_MAX_RANKS) base[threadIdx.x] = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < P; c0 += EP_PLAN_THREADS) {
+    const int p = c0 + threadIdx.x;
+    int d = -1;
+    if (p < P) {
+      const int e = inds[p];
+      d = (e >= 0 && e < per * R) ? e / per : -1;
+    }
+    int my_rank = 0;
+#pragma unroll
+    for (int q = 0; q < EP_MAX_RANKS; ++q) {
+      const unsigned m = __ballot_sync(0xffffffffu, d == q);
+      if (d == q) my_rank = __popc(m & ((1u << lane) - 1u));
+      if (lane == 0) wtot[warp][q] = __popc(m);
+    }
+    __syncthreads();
+    if (threadIdx.x < EP_MAX_RANKS) {  // exclusive scan over the warps, per destination
+      int run = base[threadIdx.x];
+      for (int w = 0; w < 32; ++w) {
+        const int v = wtot[w][threadIdx.x];
+        wtot[w][threadIdx.x] = run;
+        run += v;
+      }
+      base[threadIdx.x] = run;
+    }
+    __syncthreads();
+    if (p < P) pos[p] = d >= 0 ? wtot[warp][d] + my_rank : -1;
+    __syncthreads();
+  }
+  if (threadIdx.x < R) dcnt[threadIdx.x] = base[threadIdx.x];
+}
+
+// One warp per pair: its token row (H bf16) to the destination's inbox, plus
+// its local expert id and pair id.  The last CTA to finish publishes the
+// counts and the step flag at every destination.
+__global__ void __launch_bounds__(256)
+ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, const uint16_t* __restrict__ x,
+               const int32_t* __restrict__ inds, const int32_t* __restrict__ pos, const int32_t* __restrict__ dcnt,
+               int P, size_t off_rows, size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in,
+               uint32_t seq) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int chunks = H >> 3;  // 16-byte chunks per row
+  for (int p = gw; p < P; p += nw) {
+    const int e = inds[p], i = pos[p];
+    if (e < 0 || e >= per * R || i < 0 || i >= cap) continue;
+    const int d = e / per;
+    uint8_t* dst_base = peers.base[d];
+    const size_t slot = (size_t)me * cap + i;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(p / k) * H);
+    uint4* dst = reinterpret_cast<uint4*>(dst_base + off_rows + slot * H * 2);
+    copy_row(dst, src, chunks, lane);
+    if (lane == 0) {
+      reinterpret_cast<int32_t*>(dst_base + off_eid)[slot] = e - d * per;
+      reinterpret_cast<int32_t*>(dst_base + off_pid)[slot] = p;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&g_ep_send_done, 1u);
+    if (prev == gridDim.x - 1) {  // every CTA's rows are out: publish
+      __threadfence_system();
+      for (int d = 0; d < R; ++d) reinterpret_cast<int32_t*>(peers.base[d] + off_cnt)[me] = dcnt[d];
+      __threadfence_system();
+      for (int d = 0; d < R; ++d) st_release_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
+      g_ep_send_done = 0;
+    }
+  }
+}
+
+// Block s: wait until source s's rows of step seq are in, then mark the rest
+// of its inbox empty.  On expiry the whole inbox of s is marked empty.
+__global__ void __launch_bounds__(256)
+ep_wait_inbox_kernel(uint8_t* __restrict__ region, int cap, size_t off_eid, size_t off_cnt, size_t off_flag_in,
+                     uint32_t seq) {
+  __shared__ int n;
+  const int s = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const bool ok = ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_in) + s, seq);
+    int c = ok ? reinterpret_cast<volatile int32_t*>(region + off_cnt)[s] : 0;
+    n = (c < 0 || c > cap) ? 0 : c;
+  }
+  __syncthreads();
+  int32_t* eid = reinterpret_cast<int32_t*>(region + off_eid) + (size_t)s * cap;
+  for (int i = n + threadIdx.x; i < cap; i += blockDim.x) eid[i] = -1;
+}
+
+// One warp per inbox entry with a result: its output row back to the source's
+// ybuf at the pair id.  The last CTA raises the step flag at every source.
+__global__ void __launch_bounds__(256)
+ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t* __restrict__ region,
+                    const uint16_t* __restrict__ y, size_t off_pid, size_t off_cnt, size_t off_ybuf,
+                    size_t off_flag_back, uint32_t seq) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int chunks = H >> 3;
+  const int32_t* cnt = reinterpret_cast<const int32_t*>(region + off_cnt);
+  const int32_t* pid = reinterpret_cast<const int32_t*>(region + off_pid);
+  for (int j = gw; j < R * cap; j += nw) {
+    const int s = j / cap, i = j - s * cap;
+    if (i >= cnt[s]) continue;
+    const int p = pid[j];
+    if (p < 0 || p >= cap) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(y + (size_t)j * H);
+    uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + off_ybuf + (size_t)p * H * 2);
+    copy_row(dst, src, chunks, lane);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&g_ep_back_done, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int s = 0; s < R; ++s)
+        st_release_sys(reinterpret_cast<uint32_t*>(peers.base[s] + off_flag_back) + me, seq);
+      g_ep_back_done = 0;
+    }
+  }
+}
+
+// Thread d: wait until rank d's outputs of step seq are in ybuf.
+__global__ void ep_wait_back_kernel(const uint8_t* __restrict__ region, int R, size_t off_flag_back, uint32_t seq) {
+  if (threadIdx.x < R) ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_back) + threadIdx.x, seq);
+}
+
+int ep_device_status(int reset) {
+  int v = 0;
+  SG_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_ep_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    SG_CUDA_TRY(cudaMemcpyToSymbol(g_ep_status, &zero, sizeof(int)));
+  }
+  return v;
+}
+
+static int ep_check(int R, int me, int cap, int H) {
+  if (R < 1 || R > EP_MAX_RANKS || me < 0 || me >= R || cap < 1 || H < 8) return SG_ERR_INVALID_ARG;
+  if (H % 8) return SG_ERR_SHAPE;
+  return SG_OK;
+}
+
+static int grid_for(int rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int want = (rows + 7) / 8;  // 8 warps per CTA, one row each
+  return want < 1 ? 1 : (want < 2 * sms ? want : 2 * sms);
+}
+
+static EpPeers peers_of(void* const* bases, int R) {
+  EpPeers p;
+  for (int i = 0; i < EP_MAX_RANKS; ++i) p.base[i] = i < R ? static_cast<uint8_t*>(bases[i]) : nullptr;
+  return p;
+}
+
+}  // namespace sg
+
+// ============================================================== C-ABI
+extern "C" long long sg_ep_region_bytes(int R, int cap, int H) {
+  int st = sg::ep_check(R, 0, cap, H);
+  if (st) return st;
+  return (long long)sg::ep_layout(R, cap, H).bytes;
+}
+
+extern "C" int sg_ep_alloc(long long bytes, void** region) {
+  if (bytes <= 0 || !region) return SG_ERR_INVALID_ARG;
+  void* p = nullptr;
+  SG_CUDA_TRY(cudaMalloc(&p, (size_t)bytes));
+  const cudaError_t e = cudaMemset(p, 0, (size_t)bytes);  // flags start at step 0
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return SG_ERR_CUDA;
+  }
+  SG_CUDA_TRY(cudaDeviceSynchronize());
+  *region = p;
+  return SG_OK;
+}
+
+extern "C" int sg_ep_free(void* region) {
+  if (!region) return SG_OK;
+  SG_CUDA_TRY(cudaFree(region));
+  return SG_OK;
+}
+
+extern "C" int sg_ep_ipc_handle(void* region, uint8_t* handle64) {
+  if (!region || !handle64) return SG_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  SG_CUDA_TRY(cudaIpcGetMemHandle(&h, region));
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle64, &h, 64);
+  return SG_OK;
+}
+
+extern "C" int sg_ep_ipc_open(const uint8_t* handle64, void** region) {
+  if (!handle64 || !region) return SG_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, 64);
+  void* p = nullptr;
+  SG_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *region = p;
+  return SG_OK;
+}
+
+extern "C" int sg_ep_ipc_close(void* region) {
+  if (!region) return SG_OK;
+  SG_CUDA_TRY(cudaIpcCloseMemHandle(region));
+  return SG_OK;
+}
+
+extern "C" int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x,
+                          const int32_t* inds, int T, int k, int per, int32_t* pos, int32_t* dcnt,
+                          unsigned int seq, void* stream) {
+  int st = sg::ep_check(R, me, cap, H);
+  if (st) return st;
+  if (T < 0 || k < 1 || per < 1 || seq == 0) return SG_ERR_INVALID_ARG;
+  const int P = T * k;
+  if (P > cap) return SG_ERR_CAPACITY;
+  if (!regions || (P > 0 && (!x || !inds || !pos)) || !dcnt) return SG_ERR_INVALID_ARG;
+  for (int i = 0; i < R; ++i)
+    if (!regions[i]) return SG_ERR_INVALID_ARG;
+  const sg::EpLayout l = sg::ep_layout(R, cap, H);
+  cudaStream_t s = (cudaStream_t)stream;
+  sg::ep_plan_kernel<<<1, sg::EP_PLAN_THREADS, 0, s>>>(inds, P, per, R, pos, dcnt);
+  SG_LAUNCH_CHECK();
+  sg::ep_send_kernel<<<sg::grid_for(P), 256, 0, s>>>(sg::peers_of(regions, R), me, R, cap, H, k, per, x, inds, pos,
+                                                       dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, seq);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_ep_wait_inbox(void* region, int R, int cap, int H, unsigned int seq, void* stream) {
+  int st = sg::ep_check(R, 0, cap, H);
+  if (st) return st;
+  if (!region || seq == 0) return SG_ERR_INVALID_ARG;
+  const sg::EpLayout l = sg::ep_layout(R, cap, H);
+  sg::ep_wait_inbox_kernel<<<R, 256, 0, (cudaStream_t)stream>>>(static_cast<uint8_t*>(region), cap, l.eid, l.cnt,
+                                                                 l.flag_in, seq);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y,
+                               unsigned int seq, void* stream) {
+  int st = sg::ep_check(R, me, cap, H);
+  if (st) return st;
+  if (!regions || !y || seq == 0) return SG_ERR_INVALID_ARG;
+  for (int i = 0; i < R; ++i)
+    if (!regions[i]) return SG_ERR_INVALID_ARG;
+  const sg::EpLayout l = sg::ep_layout(R, cap, H);
+  sg::ep_send_back_kernel<<<sg::grid_for(R * cap / 4), 256, 0, (cudaStream_t)stream>>>(
+      sg::peers_of(regions, R), me, R, cap, H, static_cast<const uint8_t*>(regions[me]), y, l.pid, l.cnt, l.ybuf,
+      l.flag_back, seq);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_ep_wait_back(void* region, int R, int cap, int H, unsigned int seq, void* stream) {
+  int st = sg::ep_check(R, 0, cap, H);
+  if (st) return st;
+  if (!region || seq == 0) return SG_ERR_INVALID_ARG;
+  const sg::EpLayout l = sg::ep_layout(R, cap, H);
+  sg::ep_wait_back_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(static_cast<const uint8_t*>(region), R, l.flag_back,
+                                                               seq);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+// Byte offsets of the region's parts (rows, eid, pid, cnt, ybuf): the host
+// wraps them as tensors for sg_dispatch / sg_glu_forward / sg_combine.
+extern "C" int sg_ep_layout(int R, int cap, int H, long long* offsets5) {
+  int st = sg::ep_check(R, 0, cap, H);
+  if (st) return st;
+  if (!offsets5) return SG_ERR_INVALID_ARG;
+  const sg::EpLayout l = sg::ep_layout(R, cap, H);
+  offsets5[0] = (long long)l.rows;
+  offsets5[1] = (long long)l.eid;
+  offsets5[2] = (long long)l.pid;
+  offsets5[3] = (long long)l.cnt;
+  offsets5[4] = (long long)l.ybuf;
+  return SG_OK;
+}

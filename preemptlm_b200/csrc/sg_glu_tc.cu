@@ -1358,6 +1358,10 @@ int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, 
 
 }  // namespace sg
 
+namespace sg {
+int ep_device_status(int reset);  // the expert-parallel exchange kernels' word (sg_ep.cu)
+}
+
 extern "C" int sg_device_status(int reset) {
   int v = 0;
   SG_CUDA_TRY(cudaMemcpyFromSymbol(&v, sg::g_device_status, sizeof(int)));
@@ -1365,5 +1369,6 @@ extern "C" int sg_device_status(int reset) {
     const int zero = 0;
     SG_CUDA_TRY(cudaMemcpyToSymbol(sg::g_device_status, &zero, sizeof(int)));
   }
-  return v;
+  const int ep = sg::ep_device_status(reset);
+  return v ? v : ep;
 }

@@ -17,18 +17,28 @@ own tokens.  Per layer:
 
 The math of steps 1, 4, 5 goes through a ``backend`` object so that the same
 exchange logic runs with the CUDA kernels (``CudaBackend``) on GPUs and with a
-CPU implementation in the multi-process CPU tests.  The exchange itself uses
-``torch.distributed.all_to_all_single`` (NCCL on GPUs, gloo on CPU).
+CPU implementation in the multi-process CPU tests.
+
+Two transports for steps 2, 3 and 5:
+  * ``"p2p"`` (GPUs, the default there): the library's own exchange kernels
+    over NVLink peer memory (``sg_ep_*``, ``PeerExchange``).  Every rank owns
+    an inbox per source rank sized for the worst case, sources write rows,
+    expert ids and pair ids straight into it and raise a per-step flag, and
+    outputs go back the same way into the source's pair-order buffer.  There
+    is no host read in the step, so the host queues steps ahead of the GPU.
+  * ``"collective"``: ``torch.distributed.all_to_all_single`` (NCCL or gloo)
+    with the per-rank pair counts read on the host; the CPU tests use it.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+import ctypes
+from dataclasses import dataclass, replace
 
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _abi, ops
 from .arena import SlottedGLU
 
 
@@ -75,6 +85,31 @@ class CudaBackend:
             self.timing.setdefault("rows", []).append(rows.shape[0])
         return y
 
+    def experts_inbox(self, rows: torch.Tensor, local_eids: torch.Tensor, expected_pairs: int) -> torch.Tensor:
+        """The experts over peer-exchange inboxes in place: ``rows`` [N, H]
+        with ``local_eids`` [N] (-1: empty entry, skipped by the dispatch).
+        Returns y [N, H] with each filled entry's output in its row."""
+        N = rows.shape[0]
+        d = ops.dispatch(local_eids, self.arena.num_slots, self.ident)
+        # the pair-tile width follows the mean pairs per group: count only the
+        # entries expected to be filled (a host hint; any bound >= the groups works)
+        hint = -(-N * self.arena.num_slots // max(1, expected_pairs))
+        d = replace(d, grid_groups=max(d.grid_groups, min(2048, hint)))
+        t = self.timing
+        if t is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+        h = ops.glu_gate_up(self.arena, rows, d, 1, _abi.SG_OUT_DISPATCH_ORDER)
+        if t is not None:
+            ev[1].record()
+        y = ops.glu_down(self.arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
+        if t is not None:
+            ev[2].record()
+            t.setdefault("events", []).append(ev)
+            t.setdefault("dispatch", []).append(d)
+            t.setdefault("rows", []).append(d)  # filled entries: read from the dispatch after timing
+        return y
+
     def shared_terms(self, x: torch.Tensor):
         if self.shared is None:
             return None, None
@@ -86,10 +121,81 @@ class CudaBackend:
         return ops.combine(y, scores, shared_y, shared_gate)
 
 
+class _DeviceArray:
+    """A raw device pointer as a tensor source (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "strides": None, "version": 3}
+
+
+def _view(ptr: int, shape, dtype, device) -> torch.Tensor:
+    code = {torch.bfloat16: "<i2", torch.int32: "<i4"}[dtype]
+    t = torch.as_tensor(_DeviceArray(ptr, shape, code), device=device)
+    return t.view(dtype) if dtype == torch.bfloat16 else t
+
+
+class PeerExchange:
+    """This rank's buffers of the NVLink peer-memory exchange (``sg_ep_*``).
+
+    One region per rank (allocated by the library, every peer's region mapped
+    here by CUDA IPC), laid out identically on all ranks for ``max_tokens``
+    tokens per rank per step.  Creation and ``close`` are collective."""
+
+    def __init__(self, group, world: int, rank: int, max_tokens: int, top_k: int, hidden: int, device):
+        lib = _abi.load()
+        self.lib, self.world, self.rank, self.hidden = lib, world, rank, hidden
+        self.cap = max_tokens * top_k
+        self.device = torch.device(device)
+        nbytes = lib.sg_ep_region_bytes(world, self.cap, hidden)
+        _abi.check(min(0, nbytes), "sg_ep_region_bytes")
+        region = ctypes.c_void_p()
+        _abi.check(lib.sg_ep_alloc(nbytes, ctypes.byref(region)), "sg_ep_alloc")
+        self.region = region.value
+        handle = (ctypes.c_uint8 * 64)()
+        _abi.check(lib.sg_ep_ipc_handle(ctypes.c_void_p(self.region), handle), "sg_ep_ipc_handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened, bases = [], []
+        for r in range(world):
+            if r == rank:
+                bases.append(self.region)
+                continue
+            p = ctypes.c_void_p()
+            _abi.check(lib.sg_ep_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(handles[r]), ctypes.byref(p)),
+                       "sg_ep_ipc_open")
+            self.opened.append(p.value)
+            bases.append(p.value)
+        self.regions = (ctypes.c_void_p * world)(*bases)
+        off = (ctypes.c_longlong * 5)()
+        _abi.check(lib.sg_ep_layout(world, self.cap, hidden, off), "sg_ep_layout")
+        n = world * self.cap
+        self.rows = _view(self.region + off[0], (n, hidden), torch.bfloat16, self.device)
+        self.eids = _view(self.region + off[1], (n,), torch.int32, self.device)
+        self.ybuf = _view(self.region + off[4], (self.cap, hidden), torch.bfloat16, self.device)
+        self.pos = torch.empty(self.cap, dtype=torch.int32, device=self.device)
+        self.dcnt = torch.empty(world, dtype=torch.int32, device=self.device)
+        self.seq = 0
+        self.group = group
+
+    def close(self) -> None:
+        """Collective: every rank stops touching every region before any is freed."""
+        if self.region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            _abi.check(self.lib.sg_ep_ipc_close(ctypes.c_void_p(p)), "sg_ep_ipc_close")
+        dist.barrier(group=self.group)
+        _abi.check(self.lib.sg_ep_free(ctypes.c_void_p(self.region)), "sg_ep_free")
+        self.region, self.opened = None, []
+
+
 class ExpertParallelMoE:
     """One slotted MoE layer split expert-parallel over the process group."""
 
-    def __init__(self, backend, num_experts: int, hidden: int, top_k: int, group=None):
+    def __init__(self, backend, num_experts: int, hidden: int, top_k: int, group=None, transport: str | None = None,
+                 max_tokens: int = 256):
         self.backend = backend
         self.group = group
         self.world = dist.get_world_size(group)
@@ -97,7 +203,46 @@ class ExpertParallelMoE:
         check_divisible(num_experts, self.world)
         self.shard = ExpertShard(self.rank, self.world, num_experts)
         self.num_experts, self.hidden, self.top_k = num_experts, hidden, top_k
-        self.last_counts = None  # (send, recv) per-rank pair counts of the last step
+        self.last_counts = None  # (send, recv) per-rank pair counts of the last collective step
+        if transport is None:
+            transport = "p2p" if isinstance(backend, CudaBackend) else "collective"
+        if transport not in ("p2p", "collective"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.max_tokens = max_tokens
+        self.exchange = None
+        if transport == "p2p":
+            self.exchange = PeerExchange(group, self.world, self.rank, max_tokens, top_k, hidden,
+                                         backend.router.device)
+
+    def close(self) -> None:
+        """Collective: release the peer-exchange buffers (p2p transport)."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
+
+    def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        ex, lib = self.exchange, self.exchange.lib
+        T, H = x.shape
+        k, R, per = self.top_k, self.world, self.shard.count
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens} per rank")
+        x = x.contiguous()
+        inds, scores = self.backend.route(x)
+        shared_y, shared_gate = self.backend.shared_terms(x)
+        ex.seq += 1
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _abi.check(lib.sg_ep_send(ex.regions, R, self.rank, ex.cap, H, x.data_ptr(), inds.data_ptr(), T, k, per,
+                                  ex.pos.data_ptr(), ex.dcnt.data_ptr(), ex.seq, stream), "sg_ep_send")
+        _abi.check(lib.sg_ep_wait_inbox(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
+                   "sg_ep_wait_inbox")
+        y_local = self.backend.experts_inbox(ex.rows, ex.eids, T * k)
+        _abi.check(lib.sg_ep_send_back(ex.regions, R, self.rank, ex.cap, H, y_local.data_ptr(), ex.seq, stream),
+                   "sg_ep_send_back")
+        _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
+                   "sg_ep_wait_back")
+        ops.LAUNCHES[0] += 6
+        return self.backend.combine(ex.ybuf[: T * k], scores, shared_y, shared_gate)
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
         if out.dtype == torch.bfloat16:  # moved as raw bytes (an all-to-all is a copy; gloo has no bf16)
@@ -158,12 +303,17 @@ class ExpertParallelMoE:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x [T, H] bf16 (this rank's tokens) -> [T, H] bf16."""
+        if self.transport == "p2p":
+            return self._forward_p2p(x)
         return self.end(self.begin(x))
 
     def forward_many(self, xs) -> list:
-        """Several independent token batches (micro-batches of one step):
-        every batch's count exchange is queued before the host waits on the
-        first, so the GPU stays busy while the host issues the rest."""
+        """Several independent token batches (micro-batches of one step).
+        Collective transport: every batch's count exchange is queued before
+        the host waits on the first, so the GPU stays busy while the host
+        issues the rest."""
+        if self.transport == "p2p":
+            return [self._forward_p2p(x) for x in xs]
         states = [self.begin(x) for x in xs]
         return [self.end(s) for s in states]
 

@@ -1,6 +1,8 @@
-"""GPU, 2 ranks over NCCL (skipped with fewer than 2 GPUs): the expert-parallel
-layer on the CUDA kernels gives the single-GPU layer's output for every rank's
-tokens (same seeded weights; each rank holds half of the experts)."""
+"""GPU, 2 ranks (skipped with fewer than 2 GPUs): the expert-parallel layer on
+the CUDA kernels gives the single-GPU layer's output for every rank's tokens
+(same seeded weights; each rank holds half of the experts), over the
+library's NVLink peer-memory exchange (three steps in a row, so inbox and
+output buffers are reused) and over NCCL all-to-alls."""
 
 import os
 import socket
@@ -21,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, errfile):
+def _worker(rank, world, port, errfile, transport):
     try:
         sys.path.insert(0, ROOT)
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -34,18 +36,26 @@ def _worker(rank, world, port, errfile):
         from preemptlm_b200.layer import Qwen3_xMoEWrapper
         from preemptlm_b200.synthetic import LayerConfig, make_layer, make_tokens
 
+        from preemptlm_b200 import ops
+
         cfg = LayerConfig("ep", 8, 1024, 64, 6, 256, 256, 8, 64)
         backend, _ = shard_layer(cfg, rank, world, dev)
-        ep = ExpertParallelMoE(backend, cfg.num_experts, cfg.hidden, cfg.top_k)
-        T = 40 + 24 * rank  # ragged token counts across ranks
-        x = make_tokens(cfg, T, device=dev, step=rank)
-        out = ep(x)
+        ep = ExpertParallelMoE(backend, cfg.num_experts, cfg.hidden, cfg.top_k, transport=transport, max_tokens=64)
         block, _ = make_layer(cfg, device=dev)
-        ref = Qwen3_xMoEWrapper(block, "fp", "l", 0).forward_resident(x)
-        err = (out.float() - ref.float()).abs().max().item()
-        assert err <= 1e-2, f"rank {rank}: max-abs {err} vs the single-GPU layer"
-        send, recv = ep.last_counts
-        assert sum(send) == T * cfg.top_k
+        single = Qwen3_xMoEWrapper(block, "fp", "l", 0)
+        for step in range(3 if transport == "p2p" else 1):
+            T = 40 + 24 * rank - 7 * step  # ragged token counts across ranks and steps
+            x = make_tokens(cfg, T, device=dev, step=10 * step + rank)
+            out = ep(x)
+            ref = single.forward_resident(x)
+            err = (out.float() - ref.float()).abs().max().item()
+            assert err <= 1e-2, f"rank {rank} step {step}: max-abs {err} vs the single-GPU layer"
+        if transport == "collective":
+            send, recv = ep.last_counts
+            assert sum(send) == T * cfg.top_k
+        torch.cuda.synchronize()
+        assert ops.device_status(reset=True) == 0  # no exchange wait gave up
+        ep.close()
         dist.barrier()
         dist.destroy_process_group()
     except BaseException:
@@ -55,13 +65,14 @@ def _worker(rank, world, port, errfile):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_gpus_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
+def test_ep_two_gpus_matches_single_gpu(tmp_path, transport):
     import torch.multiprocessing as mp
 
     world, port = 2, _free_port()
     err = tmp_path / "err.txt"
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, world, port, str(err))) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(err), transport)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
