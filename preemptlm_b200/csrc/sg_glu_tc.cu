@@ -246,6 +246,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -663,11 +673,11 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
           tc_fence_after();
           const uint32_t ta = tmem_a + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
                               C::ACC_TOTAL + (sa * C::NMAT + mat) * (BK / 2) + (DUAL ? 0 : 16 * part);
-          const uint32_t (&lo)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[0]);
-          tmem_st16(ta, lo);
-          if (DUAL) {
-            const uint32_t (&hi)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[16]);
-            tmem_st16(ta + 16, hi);
+          if (DUAL) {  // the row's 32 columns of this stage in one store
+            tmem_st32(ta, out);
+          } else {
+            const uint32_t (&lo)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&out[0]);
+            tmem_st16(ta, lo);
           }
           // one store wait per group of MG stages (the MMA reads a group only
           // once all of it is full): the first stage's stores complete while

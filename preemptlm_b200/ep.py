@@ -106,8 +106,9 @@ class CudaBackend:
         if t is not None:
             ev[2].record()
             t.setdefault("events", []).append(ev)
-            t.setdefault("dispatch", []).append(d)
-            t.setdefault("rows", []).append(d)  # filled entries: read from the dispatch after timing
+            t.setdefault("dispatch", []).append(d.counts)
+            # filled entries (group_off[U]): read after timing
+            t.setdefault("rows", []).append((d.counts, d.group_off))
         return y
 
     def shared_terms(self, x: torch.Tensor):

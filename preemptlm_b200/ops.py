@@ -193,7 +193,7 @@ def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: d
     y = glu_down(arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
     ev[2].record()
     timing.setdefault("events", []).append(ev)
-    timing.setdefault("dispatch", []).append(d)
+    timing.setdefault("dispatch", []).append(d.counts)  # U of the step (the rest is freed and reused)
     return y
 
 
