@@ -46,7 +46,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # experts, 64 tokens: 291.59 MB for 128 unique experts); the launch streams
 # each unique expert's weights once, so traffic scales with the unique count
 TRAFFIC_PER_EXPERT = {"cfg3-q8-decode-shared": 291.59e6 / 128}
-QUEUE_AHEAD_CYCLES = 200_000_000  # ~0.1 s of device spin before the device-resident timed region
+QUEUE_AHEAD_CYCLES = 1_000_000_000  # ~0.5 s of device spin before the device-resident timed region
 METRIC = "SlottedGLU tokens/s at 1/2/4/8 B200; expert-GEMM HBM GB/s vs 8 TB/s peak"
 
 
@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--glu-path", choices=("auto", "gemv", "tc", "tc-perm"), default="auto")
     ap.add_argument("--microbatches", type=int, default=None,
                     help="expert-parallel micro-batches per step (default: 1 with the p2p exchange, 2 with NCCL)")
+    ap.add_argument("--ep", action="store_true",
+                    help="run the expert-parallel layer even on one GPU (one rank exchanging with itself)")
     ap.add_argument("--ep-transport", choices=("p2p", "collective"), default="p2p",
                     help="expert-parallel exchange: the library's NVLink peer-memory kernels or NCCL all-to-alls")
     ap.add_argument("--profile", action="store_true",
@@ -303,8 +305,14 @@ def run_ours(args, rank, world, local_rank):
     ops.set_glu_path(args.glu_path)
     T = args.tokens
     H = cfg.hidden
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    use_ep = world > 1 or args.ep
+    if use_ep:
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+            dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=180), device_id=dev)
+        else:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         from preemptlm_b200.ep import ExpertParallelMoE, shard_layer
 
         backend, _ = shard_layer(cfg, rank, world, dev)
@@ -330,7 +338,7 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier(device_ids=[local_rank])
 
     def run_step(x, timing=None):
-        if world > 1:
+        if use_ep:
             backend.timing = timing
             return step(x)
         return moe.forward_resident(x, timing=timing)
@@ -376,8 +384,14 @@ def run_ours(args, rank, world, local_rank):
     step_stats = {"min_ms": round(min(per_step), 4), "median_ms": round(statistics.median(per_step), 4),
                   "max_ms": round(max(per_step), 4), "host_median_ms": round(1e3 * statistics.median(host_t), 4),
                   "host_max_ms": round(1e3 * max(host_t), 4)}
-    if world > 1:
+    if use_ep:
         backend.timing = None
+        if timing.get("phases"):  # per-phase device time of the exchange step, mean over the timed steps
+            names = ("route_shared", "send", "wait_inbox", "experts", "send_back", "wait_back", "combine")
+            ph = timing["phases"]
+            step_stats["phases_ms"] = {n: round(statistics.mean(m[j].elapsed_time(m[j + 1]) for m in ph), 4)
+                                       for j, n in enumerate(names)}
+    if world > 1:
         t = torch.tensor([ms_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = float(t.item())
@@ -386,7 +400,7 @@ def run_ours(args, rank, world, local_rank):
         if rank == 0:
             print(json.dumps({"profile": cfg.name, "experts": cfg.num_experts, "tokens": T, "ms_per_step": ms_step,
                           "steps_detail": step_stats}))
-        if world > 1:
+        if use_ep:
             ep.close()
             dist.destroy_process_group()
         return
@@ -405,7 +419,7 @@ def run_ours(args, rank, world, local_rank):
 
     def e2e_step(i):
         xd = x_host[i % 2].to(dev, non_blocking=True)
-        out = step(xd) if world > 1 else moe(xd.view(1, T, H)).view(T, H)
+        out = step(xd) if use_ep else moe(xd.view(1, T, H)).view(T, H)
         out_host.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -463,8 +477,8 @@ def run_ours(args, rank, world, local_rank):
             "l2": "no flush: each step streams >126 MB (L2) of expert weights per GPU",
             "queue": "device-resident steps are queued behind a bounded device spin (not timed); e2e is not",
             "parallelism": f"ep{world}",
-            "microbatches": mb if world > 1 else 1,
-            "exchange": args.ep_transport if world > 1 else None,
+            "microbatches": mb if use_ep else 1,
+            "exchange": args.ep_transport if use_ep else None,
         },
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
@@ -496,7 +510,7 @@ def run_ours(args, rank, world, local_rank):
                  frac=r["tensor"]["frac"], peak_kind=tpeak_kind, hbm=hbm)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if use_ep:
         barrier()
         ep.close()
         dist.destroy_process_group()

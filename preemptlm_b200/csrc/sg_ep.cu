@@ -86,8 +86,8 @@ struct EpPeers {
   uint8_t* base[EP_MAX_RANKS];  // every rank's region in this process's address space (own one included)
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -109,19 +109,24 @@ __device__ bool ep_wait_flag(const uint32_t* flag, uint32_t seq) {
   }
 }
 
-// One row by one warp, 16-byte chunks, four loads in flight per lane before
-// their stores (the destination is usually another GPU's memory).
+// One row by one warp, 16-byte chunks, eight loads in flight per lane before
+// their stores (a 4 KB row in one round trip; the destination is usually
+// another GPU's memory).
 __device__ __forceinline__ void copy_row(uint4* dst, const uint4* src, int chunks, int lane) {
-  for (int c0 = lane; c0 < chunks; c0 += 128) {
-    uint4 v[4];
+  for (int c0 = lane; c0 < chunks; c0 += 256) {
+    uint4 v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 8; ++u)
       if (c0 + 32 * u < chunks) v[u] = ldg_nc_v4(src + c0 + 32 * u);
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 8; ++u)
       if (c0 + 32 * u < chunks) dst[c0 + 32 * u] = v[u];
   }
 }
+
+// Release / acquire fences at system scope (lighter than the sequentially
+// consistent __threadfence_system).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // Stable position of every pair within its destination rank, and the pair
 // count per destination.  One CTA of 1024 threads; pairs in chunks of 1024,
@@ -150,14 +155,18 @@ ep_plan_kernel(const int32_t* __restrict__ inds, int P, int per, int R, int32_t*
       if (lane == 0) wtot[warp][q] = __popc(m);
     }
     __syncthreads();
-    if (threadIdx.x < EP_MAX_RANKS) {  // exclusive scan over the warps, per destination
-      int run = base[threadIdx.x];
-      for (int w = 0; w < 32; ++w) {
-        const int v = wtot[w][threadIdx.x];
-        wtot[w][threadIdx.x] = run;
-        run += v;
+    if (warp < EP_MAX_RANKS) {  // warp q: exclusive scan of destination q's warp totals
+      const int v = wtot[lane][warp];
+      int incl = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
       }
-      base[threadIdx.x] = run;
+      const int b = base[warp];
+      wtot[lane][warp] = b + incl - v;
+      __syncwarp();
+      if (lane == 31) base[warp] = b + incl;
     }
     __syncthreads();
     if (p < P) pos[p] = d >= 0 ? wtot[warp][d] + my_rank : -1;
@@ -192,15 +201,20 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
       reinterpret_cast<int32_t*>(dst_base + off_pid)[slot] = p;
     }
   }
-  __threadfence_system();
+  // The CTA barrier orders every thread's stores before thread 0's GPU-scope
+  // fence and counter update; the last CTA's GPU-scope fence then has every
+  // CTA's rows in its causal past, and its one system-scope fence (cumulative)
+  // orders all of them before the flags.  A system fence costs microseconds,
+  // so the kernel pays for exactly one.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const unsigned prev = atomicAdd(&g_ep_send_done, 1u);
     if (prev == gridDim.x - 1) {  // every CTA's rows are out: publish
-      __threadfence_system();
+      __threadfence();
       for (int d = 0; d < R; ++d) reinterpret_cast<int32_t*>(peers.base[d] + off_cnt)[me] = dcnt[d];
-      __threadfence_system();
-      for (int d = 0; d < R; ++d) st_release_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
+      fence_acq_rel_sys();
+      for (int d = 0; d < R; ++d) st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
       g_ep_send_done = 0;
     }
   }
@@ -244,14 +258,15 @@ ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t*
     uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + off_ybuf + (size_t)p * H * 2);
     copy_row(dst, src, chunks, lane);
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0) {  // as in ep_send_kernel: one system fence, by the last CTA
+    __threadfence();
     const unsigned prev = atomicAdd(&g_ep_back_done, 1u);
     if (prev == gridDim.x - 1) {
-      __threadfence_system();
+      __threadfence();
+      fence_acq_rel_sys();
       for (int s = 0; s < R; ++s)
-        st_release_sys(reinterpret_cast<uint32_t*>(peers.base[s] + off_flag_back) + me, seq);
+        st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[s] + off_flag_back) + me, seq);
       g_ep_back_done = 0;
     }
   }
@@ -278,12 +293,13 @@ static int ep_check(int R, int me, int cap, int H) {
   return SG_OK;
 }
 
+// One warp per row while that fits 8 resident 256-thread CTAs per SM.
 static int grid_for(int rows) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int want = (rows + 7) / 8;  // 8 warps per CTA, one row each
-  return want < 1 ? 1 : (want < 2 * sms ? want : 2 * sms);
+  return want < 1 ? 1 : (want < 8 * sms ? want : 8 * sms);
 }
 
 static EpPeers peers_of(void* const* bases, int R) {
@@ -386,7 +402,7 @@ extern "C" int sg_ep_send_back(void* const* regions, int R, int me, int cap, int
   for (int i = 0; i < R; ++i)
     if (!regions[i]) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
-  sg::ep_send_back_kernel<<<sg::grid_for(R * cap / 4), 256, 0, (cudaStream_t)stream>>>(
+  sg::ep_send_back_kernel<<<sg::grid_for(R * cap), 256, 0, (cudaStream_t)stream>>>(
       sg::peers_of(regions, R), me, R, cap, H, static_cast<const uint8_t*>(regions[me]), y, l.pid, l.cnt, l.ybuf,
       l.flag_back, seq);
   SG_LAUNCH_CHECK();

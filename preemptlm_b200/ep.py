@@ -73,6 +73,7 @@ class CudaBackend:
         self.arena, self.shared, self.shared_gate = arena, shared, shared_gate
         self.ident = torch.arange(arena.num_slots, dtype=torch.int32, device=router.device)
         self.timing: dict | None = None  # receives events around the expert kernels when set
+        self._side: torch.cuda.Stream | None = None  # the shared expert's stream
 
     def route(self, x: torch.Tensor):
         logits = ops.router_linear(x, self.router)
@@ -112,13 +113,28 @@ class CudaBackend:
         return y
 
     def shared_terms(self, x: torch.Tensor):
+        """The shared expert and its gate, queued on a side stream beside the
+        exchange and the routed experts; joined by ``combine``."""
         if self.shared is None:
             return None, None
         from .layer import shared_expert_forward
 
-        return shared_expert_forward(self.shared, x), ops.router_linear(x, self.shared_gate).reshape(-1)
+        main = torch.cuda.current_stream(x.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(x.device)
+        self._side.wait_stream(main)
+        x.record_stream(self._side)
+        with torch.cuda.stream(self._side):
+            sy = shared_expert_forward(self.shared, x)
+            sg = ops.router_linear(x, self.shared_gate).reshape(-1)
+        return sy, sg
 
     def combine(self, y: torch.Tensor, scores: torch.Tensor, shared_y, shared_gate) -> torch.Tensor:
+        if shared_y is not None:
+            main = torch.cuda.current_stream(y.device)
+            main.wait_stream(self._side)
+            shared_y.record_stream(main)
+            shared_gate.record_stream(main)
         return ops.combine(y, scores, shared_y, shared_gate)
 
 
@@ -229,21 +245,41 @@ class ExpertParallelMoE:
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens} per rank")
         x = x.contiguous()
+        timing = getattr(self.backend, "timing", None)
+        marks = [] if timing is not None else None
+
+        def mark():  # phase boundaries of the step, when timing
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        mark()
         inds, scores = self.backend.route(x)
         shared_y, shared_gate = self.backend.shared_terms(x)
+        mark()
         ex.seq += 1
         stream = torch.cuda.current_stream(x.device).cuda_stream
         _abi.check(lib.sg_ep_send(ex.regions, R, self.rank, ex.cap, H, x.data_ptr(), inds.data_ptr(), T, k, per,
                                   ex.pos.data_ptr(), ex.dcnt.data_ptr(), ex.seq, stream), "sg_ep_send")
+        mark()
         _abi.check(lib.sg_ep_wait_inbox(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
                    "sg_ep_wait_inbox")
+        mark()
         y_local = self.backend.experts_inbox(ex.rows, ex.eids, T * k)
+        mark()
         _abi.check(lib.sg_ep_send_back(ex.regions, R, self.rank, ex.cap, H, y_local.data_ptr(), ex.seq, stream),
                    "sg_ep_send_back")
+        mark()
         _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
                    "sg_ep_wait_back")
+        mark()
         ops.LAUNCHES[0] += 6
-        return self.backend.combine(ex.ybuf[: T * k], scores, shared_y, shared_gate)
+        out = self.backend.combine(ex.ybuf[: T * k], scores, shared_y, shared_gate)
+        mark()
+        if marks is not None:
+            timing.setdefault("phases", []).append(marks)
+        return out
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
         if out.dtype == torch.bfloat16:  # moved as raw bytes (an all-to-all is a copy; gloo has no bf16)
