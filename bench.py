@@ -366,6 +366,11 @@ def run_ours(args, rank, world, local_rank):
     # steps before the GPU reaches them, so a host-side hiccup (driver lock,
     # allocator) cannot idle the GPU inside the timed region
     torch.cuda._sleep(QUEUE_AHEAD_CYCLES)
+    if world > 1:
+        # one untimed exchange step after the spin: the ranks' spins end a
+        # little apart, and this step (which waits on every peer) lines up
+        # their timed regions
+        run_step(xs[0], timing={})
     start.record()
     for i in range(args.steps):
         step_ev[i].record()
