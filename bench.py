@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--glu-path", choices=("auto", "gemv", "tc", "tc-perm"), default="auto")
     ap.add_argument("--microbatches", type=int, default=None,
                     help="expert-parallel micro-batches per step (default: 1 with the p2p exchange, 2 with NCCL)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="expert-parallel e2e steps issued eagerly instead of as a captured CUDA graph")
     ap.add_argument("--ep", action="store_true",
                     help="run the expert-parallel layer even on one GPU (one rank exchanging with itself)")
     ap.add_argument("--ep-transport", choices=("p2p", "collective"), default="p2p",
@@ -422,9 +424,20 @@ def run_ours(args, rank, world, local_rank):
         xh.copy_(xs[i].cpu())
     out_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
 
+    graphed = use_ep and args.ep_transport == "p2p" and mb == 1 and not args.no_graph
+    if graphed:
+        # the expert-parallel step as one CUDA graph (captured once, collective):
+        # the host's per-step cost is the input copy, one graph launch and the
+        # output copy
+        ep.capture(T)
+
     def e2e_step(i):
-        xd = x_host[i % 2].to(dev, non_blocking=True)
-        out = step(xd) if use_ep else moe(xd.view(1, T, H)).view(T, H)
+        if graphed:
+            ep.graph_input.copy_(x_host[i % 2], non_blocking=True)
+            out = ep.replay()
+        else:
+            xd = x_host[i % 2].to(dev, non_blocking=True)
+            out = step(xd) if use_ep else moe(xd.view(1, T, H)).view(T, H)
         out_host.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -484,6 +497,7 @@ def run_ours(args, rank, world, local_rank):
             "parallelism": f"ep{world}",
             "microbatches": mb if use_ep else 1,
             "exchange": args.ep_transport if use_ep else None,
+            "e2e_graph": bool(use_ep and graphed),
         },
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),

@@ -222,19 +222,20 @@ size_t sg_expert_bytes(const sg_arena* arena);
  * bytes, zeroed), exports it with sg_ep_ipc_handle, and opens every peer's
  * with sg_ep_ipc_open; `regions` lists all R regions in this process's
  * address space (its own included), in rank order.  cap = the most tokens
- * per rank per step times k.  Per step (seq = 1, 2, ...; the same on all
- * ranks):
+ * per rank per step times k.  Every rank runs the same number of steps; the
+ * step number lives in the region (sg_ep_send bumps it), so a step captured
+ * in a CUDA graph replays correctly.  Per step:
  *   sg_ep_send(regions, R, me, cap, H, x [T, H], inds [T, k] global expert
  *     ids, T, k, per = experts per rank, pos [T*k] and dcnt [R] int32
- *     scratch, seq): every pair's token row, local expert id and pair id
+ *     scratch): every pair's token row, local expert id and pair id
  *     into its owner's inbox, then that rank's step flag (T * k <= cap);
- *   sg_ep_wait_inbox(own region, ..., seq): waits for every source's flag
+ *   sg_ep_wait_inbox(own region, ...): waits for every source's flag
  *     and marks unused inbox entries empty (expert id -1);
  *   sg_dispatch + sg_glu_gate_up / sg_glu_down then run over the R * cap
  *     inbox rows and ids (sg_ep_layout gives their offsets) in place;
- *   sg_ep_send_back(regions, ..., y [R * cap, H], seq): each filled entry's
+ *   sg_ep_send_back(regions, ..., y [R * cap, H]): each filled entry's
  *     output row to its source, at its pair id, then the step flag;
- *   sg_ep_wait_back(own region, ..., seq): waits for every owner's flag; the
+ *   sg_ep_wait_back(own region, ...): waits for every owner's flag; the
  *     region's pair-order output rows ([T * k, H], offset 4 of sg_ep_layout)
  *     are then complete for sg_combine.
  * Every wait is bounded (about 2 s); on expiry sg_device_status reports
@@ -251,11 +252,10 @@ int sg_ep_ipc_handle(void* region, uint8_t* handle64);
 int sg_ep_ipc_open(const uint8_t* handle64, void** region);
 int sg_ep_ipc_close(void* region);
 int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x, const int32_t* inds,
-               int T, int k, int per, int32_t* pos, int32_t* dcnt, unsigned int seq, void* stream);
-int sg_ep_wait_inbox(void* region, int R, int cap, int H, unsigned int seq, void* stream);
-int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y, unsigned int seq,
-                    void* stream);
-int sg_ep_wait_back(void* region, int R, int cap, int H, unsigned int seq, void* stream);
+               int T, int k, int per, int32_t* pos, int32_t* dcnt, void* stream);
+int sg_ep_wait_inbox(void* region, int R, int cap, int H, void* stream);
+int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y, void* stream);
+int sg_ep_wait_back(void* region, int R, int cap, int H, void* stream);
 
 #ifdef __cplusplus
 }

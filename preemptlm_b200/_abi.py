@@ -71,7 +71,7 @@ def load() -> ctypes.CDLL:
             "(python -m preemptlm_b200.build); there is no CPU fallback"
         )
     lib = ctypes.CDLL(str(path))
-    P, I32, U32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_size_t
+    P, I32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
     A = ctypes.POINTER(sg_arena)
     sigs = {
         "sg_status_string": (ctypes.c_char_p, [I32]),
@@ -99,10 +99,10 @@ def load() -> ctypes.CDLL:
         "sg_ep_ipc_handle": (I32, [P, P]),
         "sg_ep_ipc_open": (I32, [P, P]),
         "sg_ep_ipc_close": (I32, [P]),
-        "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P, U32, P]),
-        "sg_ep_wait_inbox": (I32, [P, I32, I32, I32, U32, P]),
-        "sg_ep_send_back": (I32, [P, I32, I32, I32, I32, P, U32, P]),
-        "sg_ep_wait_back": (I32, [P, I32, I32, I32, U32, P]),
+        "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P, P]),
+        "sg_ep_wait_inbox": (I32, [P, I32, I32, I32, P]),
+        "sg_ep_send_back": (I32, [P, I32, I32, I32, I32, P, P]),
+        "sg_ep_wait_back": (I32, [P, I32, I32, I32, P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

@@ -13,10 +13,13 @@
 //                           order, written back by the owning ranks
 //   flag_in [R], flag_back [R] uint32: the step number whose inbox rows /
 //                           outputs from rank s are complete
+//   step              uint32 this rank's step counter (bumped by sg_ep_send;
+//                           every later call of the step reads it, so a
+//                           captured CUDA graph of the step replays correctly)
 // CAP = max tokens per step x k, the most pairs one source can route to one
 // destination, so no inbox can overflow whatever the routing.
 //
-// A step (seq = 1, 2, ... in lockstep on all ranks):
+// A step (seq = 1, 2, ... in lockstep on all ranks, kept on the device):
 //   sg_ep_send:      plan (stable position of every pair within its
 //                    destination) and copy each pair's token row, expert id
 //                    and pair id into the destination's inbox; the last CTA
@@ -56,7 +59,7 @@ constexpr int EP_MAX_RANKS = 8;
 constexpr long long EP_WAIT_CYCLES = 4000000000LL;  // ~2 s
 
 struct EpLayout {
-  size_t rows, eid, pid, cnt, ybuf, flag_in, flag_back, bytes;
+  size_t rows, eid, pid, cnt, ybuf, flag_in, flag_back, step, bytes;
 };
 
 static size_t ep_align(size_t v) { return (v + 255) & ~size_t(255); }
@@ -78,6 +81,8 @@ static EpLayout ep_layout(int R, int cap, int H) {
   o += ep_align((size_t)R * 4);
   l.flag_back = o;
   o += ep_align((size_t)R * 4);
+  l.step = o;
+  o += 256;
   l.bytes = o;
   return l;
 }
@@ -134,7 +139,7 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 constexpr int EP_PLAN_THREADS = 1024;
 __global__ void __launch_bounds__(EP_PLAN_THREADS)
 ep_plan_kernel(const int32_t* __restrict__ inds, int P, int per, int R, int32_t* __restrict__ pos,
-               int32_t* __restrict__ dcnt) {
+               int32_t* __restrict__ dcnt, uint32_t* __restrict__ step) {
   __shared__ int wtot[32][EP_MAX_RANKS];
   __shared__ int base[EP_MAX_RANKS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -173,6 +178,7 @@ ep_plan_kernel(const int32_t* __restrict__ inds, int P, int per, int R, int32_t*
     __syncthreads();
   }
   if (threadIdx.x < R) dcnt[threadIdx.x] = base[threadIdx.x];
+  if (threadIdx.x == 0) *step += 1;  // this step's number, read by the step's later kernels
 }
 
 // One warp per pair: its token row (H bf16) to the destination's inbox, plus
@@ -182,7 +188,7 @@ __global__ void __launch_bounds__(256)
 ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, const uint16_t* __restrict__ x,
                const int32_t* __restrict__ inds, const int32_t* __restrict__ pos, const int32_t* __restrict__ dcnt,
                int P, size_t off_rows, size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in,
-               uint32_t seq) {
+               size_t off_step) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -214,6 +220,7 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
       __threadfence();
       for (int d = 0; d < R; ++d) reinterpret_cast<int32_t*>(peers.base[d] + off_cnt)[me] = dcnt[d];
       fence_acq_rel_sys();
+      const uint32_t seq = *reinterpret_cast<const uint32_t*>(peers.base[me] + off_step);
       for (int d = 0; d < R; ++d) st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
       g_ep_send_done = 0;
     }
@@ -224,10 +231,11 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
 // of its inbox empty.  On expiry the whole inbox of s is marked empty.
 __global__ void __launch_bounds__(256)
 ep_wait_inbox_kernel(uint8_t* __restrict__ region, int cap, size_t off_eid, size_t off_cnt, size_t off_flag_in,
-                     uint32_t seq) {
+                     size_t off_step) {
   __shared__ int n;
   const int s = blockIdx.x;
   if (threadIdx.x == 0) {
+    const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
     const bool ok = ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_in) + s, seq);
     int c = ok ? reinterpret_cast<volatile int32_t*>(region + off_cnt)[s] : 0;
     n = (c < 0 || c > cap) ? 0 : c;
@@ -242,7 +250,7 @@ ep_wait_inbox_kernel(uint8_t* __restrict__ region, int cap, size_t off_eid, size
 __global__ void __launch_bounds__(256)
 ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t* __restrict__ region,
                     const uint16_t* __restrict__ y, size_t off_pid, size_t off_cnt, size_t off_ybuf,
-                    size_t off_flag_back, uint32_t seq) {
+                    size_t off_flag_back, size_t off_step) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -265,6 +273,7 @@ ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t*
     if (prev == gridDim.x - 1) {
       __threadfence();
       fence_acq_rel_sys();
+      const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
       for (int s = 0; s < R; ++s)
         st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[s] + off_flag_back) + me, seq);
       g_ep_back_done = 0;
@@ -273,7 +282,9 @@ ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t*
 }
 
 // Thread d: wait until rank d's outputs of step seq are in ybuf.
-__global__ void ep_wait_back_kernel(const uint8_t* __restrict__ region, int R, size_t off_flag_back, uint32_t seq) {
+__global__ void ep_wait_back_kernel(const uint8_t* __restrict__ region, int R, size_t off_flag_back,
+                                    size_t off_step) {
+  const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
   if (threadIdx.x < R) ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_back) + threadIdx.x, seq);
 }
 
@@ -363,11 +374,10 @@ extern "C" int sg_ep_ipc_close(void* region) {
 }
 
 extern "C" int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x,
-                          const int32_t* inds, int T, int k, int per, int32_t* pos, int32_t* dcnt,
-                          unsigned int seq, void* stream) {
+                          const int32_t* inds, int T, int k, int per, int32_t* pos, int32_t* dcnt, void* stream) {
   int st = sg::ep_check(R, me, cap, H);
   if (st) return st;
-  if (T < 0 || k < 1 || per < 1 || seq == 0) return SG_ERR_INVALID_ARG;
+  if (T < 0 || k < 1 || per < 1) return SG_ERR_INVALID_ARG;
   const int P = T * k;
   if (P > cap) return SG_ERR_CAPACITY;
   if (!regions || (P > 0 && (!x || !inds || !pos)) || !dcnt) return SG_ERR_INVALID_ARG;
@@ -375,47 +385,48 @@ extern "C" int sg_ep_send(void* const* regions, int R, int me, int cap, int H, c
     if (!regions[i]) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   cudaStream_t s = (cudaStream_t)stream;
-  sg::ep_plan_kernel<<<1, sg::EP_PLAN_THREADS, 0, s>>>(inds, P, per, R, pos, dcnt);
+  sg::ep_plan_kernel<<<1, sg::EP_PLAN_THREADS, 0, s>>>(
+      inds, P, per, R, pos, dcnt, reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(regions[me]) + l.step));
   SG_LAUNCH_CHECK();
   sg::ep_send_kernel<<<sg::grid_for(P), 256, 0, s>>>(sg::peers_of(regions, R), me, R, cap, H, k, per, x, inds, pos,
-                                                       dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, seq);
+                                                       dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, l.step);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
-extern "C" int sg_ep_wait_inbox(void* region, int R, int cap, int H, unsigned int seq, void* stream) {
+extern "C" int sg_ep_wait_inbox(void* region, int R, int cap, int H, void* stream) {
   int st = sg::ep_check(R, 0, cap, H);
   if (st) return st;
-  if (!region || seq == 0) return SG_ERR_INVALID_ARG;
+  if (!region) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   sg::ep_wait_inbox_kernel<<<R, 256, 0, (cudaStream_t)stream>>>(static_cast<uint8_t*>(region), cap, l.eid, l.cnt,
-                                                                 l.flag_in, seq);
+                                                                 l.flag_in, l.step);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
 extern "C" int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y,
-                               unsigned int seq, void* stream) {
+                               void* stream) {
   int st = sg::ep_check(R, me, cap, H);
   if (st) return st;
-  if (!regions || !y || seq == 0) return SG_ERR_INVALID_ARG;
+  if (!regions || !y) return SG_ERR_INVALID_ARG;
   for (int i = 0; i < R; ++i)
     if (!regions[i]) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   sg::ep_send_back_kernel<<<sg::grid_for(R * cap), 256, 0, (cudaStream_t)stream>>>(
       sg::peers_of(regions, R), me, R, cap, H, static_cast<const uint8_t*>(regions[me]), y, l.pid, l.cnt, l.ybuf,
-      l.flag_back, seq);
+      l.flag_back, l.step);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
-extern "C" int sg_ep_wait_back(void* region, int R, int cap, int H, unsigned int seq, void* stream) {
+extern "C" int sg_ep_wait_back(void* region, int R, int cap, int H, void* stream) {
   int st = sg::ep_check(R, 0, cap, H);
   if (st) return st;
-  if (!region || seq == 0) return SG_ERR_INVALID_ARG;
+  if (!region) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   sg::ep_wait_back_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(static_cast<const uint8_t*>(region), R, l.flag_back,
-                                                               seq);
+                                                               l.step);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }

@@ -123,7 +123,8 @@ class CudaBackend:
         if self._side is None:
             self._side = torch.cuda.Stream(x.device)
         self._side.wait_stream(main)
-        x.record_stream(self._side)
+        if not torch.cuda.is_current_stream_capturing():  # a graph's pool keeps its tensors alive
+            x.record_stream(self._side)
         with torch.cuda.stream(self._side):
             sy = shared_expert_forward(self.shared, x)
             sg = ops.router_linear(x, self.shared_gate).reshape(-1)
@@ -133,8 +134,9 @@ class CudaBackend:
         if shared_y is not None:
             main = torch.cuda.current_stream(y.device)
             main.wait_stream(self._side)
-            shared_y.record_stream(main)
-            shared_gate.record_stream(main)
+            if not torch.cuda.is_current_stream_capturing():
+                shared_y.record_stream(main)
+                shared_gate.record_stream(main)
         return ops.combine(y, scores, shared_y, shared_gate)
 
 
@@ -192,7 +194,6 @@ class PeerExchange:
         self.ybuf = _view(self.region + off[4], (self.cap, hidden), torch.bfloat16, self.device)
         self.pos = torch.empty(self.cap, dtype=torch.int32, device=self.device)
         self.dcnt = torch.empty(world, dtype=torch.int32, device=self.device)
-        self.seq = 0
         self.group = group
 
     def close(self) -> None:
@@ -231,9 +232,52 @@ class ExpertParallelMoE:
         if transport == "p2p":
             self.exchange = PeerExchange(group, self.world, self.rank, max_tokens, top_k, hidden,
                                          backend.router.device)
+        self._graph = None
+        self.graph_input = self.graph_output = None
+        self._graph_launches = 0
+
+    def capture(self, T: int, warmup: int = 2, seed: int = 0) -> None:
+        """Record one peer-exchange step for T tokens in a CUDA graph, so that
+        a step costs the host one graph launch (``replay``).  Collective:
+        every rank captures with the same arguments (the warm-up steps
+        exchange with the peers).  The step number lives on the device, so
+        replays synchronise correctly."""
+        if self.transport != "p2p":
+            raise ValueError("only the p2p transport can be captured")
+        dev = self.backend.router.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.graph_input = torch.randn((T, self.hidden), generator=g, device=dev).to(torch.bfloat16)
+        timing, self.backend.timing = self.backend.timing, None
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):  # warm-up off the default stream, as capture requires
+            for _ in range(warmup):
+                self._forward_p2p(self.graph_input)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        n0 = ops.LAUNCHES[0]
+        with torch.cuda.graph(graph):
+            self.graph_output = self._forward_p2p(self.graph_input)
+        self._graph_launches = ops.LAUNCHES[0] - n0
+        self._graph = graph
+        self.backend.timing = timing
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        """One captured step; ``x`` (if given) is first copied into the
+        graph's input.  Returns the graph's output buffer, overwritten by
+        the next replay."""
+        if x is not None:
+            self.graph_input.copy_(x, non_blocking=True)
+        self._graph.replay()
+        ops.LAUNCHES[0] += self._graph_launches
+        return self.graph_output
 
     def close(self) -> None:
-        """Collective: release the peer-exchange buffers (p2p transport)."""
+        """Collective: release the captured graph and the peer-exchange
+        buffers (p2p transport)."""
+        self._graph = None
+        self.graph_input = self.graph_output = None
         if self.exchange is not None:
             self.exchange.close()
             self.exchange = None
@@ -258,21 +302,18 @@ class ExpertParallelMoE:
         inds, scores = self.backend.route(x)
         shared_y, shared_gate = self.backend.shared_terms(x)
         mark()
-        ex.seq += 1
         stream = torch.cuda.current_stream(x.device).cuda_stream
         _abi.check(lib.sg_ep_send(ex.regions, R, self.rank, ex.cap, H, x.data_ptr(), inds.data_ptr(), T, k, per,
-                                  ex.pos.data_ptr(), ex.dcnt.data_ptr(), ex.seq, stream), "sg_ep_send")
+                                  ex.pos.data_ptr(), ex.dcnt.data_ptr(), stream), "sg_ep_send")
         mark()
-        _abi.check(lib.sg_ep_wait_inbox(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
-                   "sg_ep_wait_inbox")
+        _abi.check(lib.sg_ep_wait_inbox(ctypes.c_void_p(ex.region), R, ex.cap, H, stream), "sg_ep_wait_inbox")
         mark()
         y_local = self.backend.experts_inbox(ex.rows, ex.eids, T * k)
         mark()
-        _abi.check(lib.sg_ep_send_back(ex.regions, R, self.rank, ex.cap, H, y_local.data_ptr(), ex.seq, stream),
+        _abi.check(lib.sg_ep_send_back(ex.regions, R, self.rank, ex.cap, H, y_local.data_ptr(), stream),
                    "sg_ep_send_back")
         mark()
-        _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, ex.seq, stream),
-                   "sg_ep_wait_back")
+        _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, stream), "sg_ep_wait_back")
         mark()
         ops.LAUNCHES[0] += 6
         out = self.backend.combine(ex.ybuf[: T * k], scores, shared_y, shared_gate)

@@ -53,6 +53,14 @@ def _worker(rank, world, port, errfile, transport):
         if transport == "collective":
             send, recv = ep.last_counts
             assert sum(send) == T * cfg.top_k
+        else:  # the step captured in a CUDA graph, replayed on new tokens
+            ep.capture(T)
+            for step in range(2):
+                x = make_tokens(cfg, T, device=dev, step=100 + 10 * step + rank)
+                out = ep.replay(x).clone()
+                ref = single.forward_resident(x)
+                err = (out.float() - ref.float()).abs().max().item()
+                assert err <= 1e-2, f"rank {rank} replay {step}: max-abs {err} vs the single-GPU layer"
         torch.cuda.synchronize()
         assert ops.device_status(reset=True) == 0  # no exchange wait gave up
         ep.close()
@@ -62,6 +70,22 @@ def _worker(rank, world, port, errfile, transport):
         with open(errfile, "a") as f:
             f.write(f"rank {rank}:\n{traceback.format_exc()}\n")
         raise
+
+
+def test_ep_one_rank_exchange_and_graph(tmp_path):
+    """One rank exchanging with itself over the same peer-memory kernels
+    (inboxes, flags, outputs written back), eager and as a replayed CUDA
+    graph, against the single-GPU layer: the exchange path runs on one GPU."""
+    import torch.multiprocessing as mp
+
+    err = tmp_path / "err.txt"
+    p = mp.get_context("spawn").Process(target=_worker, args=(0, 1, _free_port(), str(err), "p2p"))
+    p.start()
+    p.join(timeout=300)
+    if p.is_alive():
+        p.kill()
+        pytest.fail("EP rank hung")
+    assert p.exitcode == 0, err.read_text() if err.exists() else ""
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
