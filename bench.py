@@ -65,7 +65,7 @@ def parse_args():
     ap.add_argument("--microbatches", type=int, default=None,
                     help="expert-parallel micro-batches per step (default: 1 with the p2p exchange, 2 with NCCL)")
     ap.add_argument("--no-graph", action="store_true",
-                    help="expert-parallel e2e steps issued eagerly instead of as a captured CUDA graph")
+                    help="e2e steps issued eagerly instead of as a captured CUDA graph of the layer call")
     ap.add_argument("--ep", action="store_true",
                     help="run the expert-parallel layer even on one GPU (one rank exchanging with itself)")
     ap.add_argument("--ep-transport", choices=("p2p", "collective"), default="p2p",
@@ -431,10 +431,16 @@ def run_ours(args, rank, world, local_rank):
         # output copy
         ep.capture(T)
 
+    if not use_ep and not args.no_graph:
+        moe.capture(1, T)  # the public layer call as one CUDA graph
+
     def e2e_step(i):
         if graphed:
             ep.graph_input.copy_(x_host[i % 2], non_blocking=True)
             out = ep.replay()
+        elif not use_ep and not args.no_graph:
+            moe.graph_input.view(T, H).copy_(x_host[i % 2], non_blocking=True)
+            out = moe.replay().view(T, H)
         else:
             xd = x_host[i % 2].to(dev, non_blocking=True)
             out = step(xd) if use_ep else moe(xd.view(1, T, H)).view(T, H)
@@ -497,7 +503,7 @@ def run_ours(args, rank, world, local_rank):
             "parallelism": f"ep{world}",
             "microbatches": mb if use_ep else 1,
             "exchange": args.ep_transport if use_ep else None,
-            "e2e_graph": bool(use_ep and graphed),
+            "e2e_graph": not args.no_graph and (graphed or not use_ep),
         },
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),

@@ -8,35 +8,53 @@ namespace sg {
 // CTA = 8 warps; a CTA covers RT_TOK tokens x (8 * RT_EXP) experts.  Each warp
 // owns RT_EXP experts and all RT_TOK tokens of the tile; lane j accumulates
 // h = 256*i + 8*j + e in (i, e) order, then every (expert, token) partial is
-// folded 16, 8, 4, 2, 1 across the warp.  x for the token tile is staged in
-// shared memory; router rows stream from global (read once per token tile).
+// folded 16, 8, 4, 2, 1 across the warp.  Tokens go in pairs through packed
+// fma.rn.f32x2 (two accumulators, one instruction; each lane's FMA rounds as
+// a scalar FMA would, so the order and the bits are those of one accumulator
+// per (expert, token)).  x for the token tile is staged in shared memory as
+// bf16x2 words holding a token pair's element h, laid out so that a lane's
+// four pairs for one h are one 16-byte load; router rows stream from global
+// (read once per token tile).
 constexpr int RT_TOK = 8;
 constexpr int RT_EXP = 4;
 constexpr int RT_WARPS = 8;
+constexpr int RT_PAIRS = RT_TOK / 2;
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
 
 __global__ void __launch_bounds__(RT_WARPS * 32)
 router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                      uint16_t* __restrict__ logits, int T, int H, int E) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint4* xs = reinterpret_cast<uint4*>(smem_raw);  // [RT_TOK][H/8] 16-byte chunks
+  // word ((i * 8 + e) * 32 + j) * 4 + p = (x[t0 + 2p][h], x[t0 + 2p + 1][h]), h = 256 i + 8 j + e
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * RT_TOK;
   const int e0 = (blockIdx.y * RT_WARPS + warp) * RT_EXP;
   const int chunks = H >> 3;  // 16-byte chunks per row
 
-  for (int c = threadIdx.x; c < RT_TOK * chunks; c += blockDim.x) {
-    int tt = c / chunks, cc = c - tt * chunks;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t0 + tt < T) v = reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H)[cc];
-    xs[c] = v;
+  for (int it = threadIdx.x; it < RT_PAIRS * chunks; it += blockDim.x) {
+    const int p = it / chunks, c = it - p * chunks;
+    const int ta = t0 + 2 * p, tb = ta + 1;
+    const uint4 va = ta < T ? reinterpret_cast<const uint4*>(x + (size_t)ta * H)[c] : make_uint4(0, 0, 0, 0);
+    const uint4 vb = tb < T ? reinterpret_cast<const uint4*>(x + (size_t)tb * H)[c] : make_uint4(0, 0, 0, 0);
+    const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+    const int i = c >> 5, j = c & 31;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      xs[((i * 8 + 2 * q) * 32 + j) * 4 + p] = __byte_perm(wa[q], wb[q], 0x5410);      // element 2q
+      xs[((i * 8 + 2 * q + 1) * 32 + j) * 4 + p] = __byte_perm(wa[q], wb[q], 0x7632);  // element 2q + 1
+    }
   }
   __syncthreads();
 
-  float acc[RT_EXP][RT_TOK];
+  unsigned long long acc[RT_EXP][RT_PAIRS];
 #pragma unroll
   for (int a = 0; a < RT_EXP; ++a)
 #pragma unroll
-    for (int b = 0; b < RT_TOK; ++b) acc[a][b] = 0.0f;
+    for (int b = 0; b < RT_PAIRS; ++b) acc[a][b] = 0ull;
 
   const int iters = H >> 8;
   // router rows: this lane's 16-byte chunk of iteration i + 1 is in flight
@@ -48,27 +66,28 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
     wn[a] = (e < E) ? ldg_nc_v4(w + (size_t)e * H + (size_t)lane * 8) : make_uint4(0, 0, 0, 0);
   }
   for (int i = 0; i < iters; ++i) {
-    const int cc = i * 32 + lane;  // this lane's 16-byte chunk of the row
     uint4 wv[RT_EXP];
 #pragma unroll
     for (int a = 0; a < RT_EXP; ++a) {
       wv[a] = wn[a];
       const int e = e0 + a;
-      if (i + 1 < iters && e < E) wn[a] = ldg_nc_v4(w + (size_t)e * H + (size_t)(cc + 32) * 8);
+      if (i + 1 < iters && e < E) wn[a] = ldg_nc_v4(w + (size_t)e * H + (size_t)((i + 1) * 32 + lane) * 8);
     }
 #pragma unroll
-    for (int b = 0; b < RT_TOK; ++b) {
-      uint4 xv = xs[b * chunks + cc];
+    for (int el = 0; el < 8; ++el) {  // element order within the lane's chunk
+      const uint4 xv = *reinterpret_cast<const uint4*>(xs + ((i * 8 + el) * 32 + lane) * 4);
       const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+      unsigned long long xp[RT_PAIRS];
+#pragma unroll
+      for (int p = 0; p < RT_PAIRS; ++p) xp[p] = pack2(lo_bf16(xw[p]), hi_bf16(xw[p]));
 #pragma unroll
       for (int a = 0; a < RT_EXP; ++a) {
         const uint32_t ww[4] = {wv[a].x, wv[a].y, wv[a].z, wv[a].w};
+        const float wf = (el & 1) ? hi_bf16(ww[el >> 1]) : lo_bf16(ww[el >> 1]);
+        const unsigned long long w2 = pack2(wf, wf);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          // element order e = 2q, 2q+1 within the chunk; products are exact
-          acc[a][b] = __fmaf_rn(lo_bf16(xw[q]), lo_bf16(ww[q]), acc[a][b]);
-          acc[a][b] = __fmaf_rn(hi_bf16(xw[q]), hi_bf16(ww[q]), acc[a][b]);
-        }
+        for (int p = 0; p < RT_PAIRS; ++p)
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc[a][p]) : "l"(xp[p]), "l"(w2));
       }
     }
   }
@@ -76,9 +95,11 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   for (int a = 0; a < RT_EXP; ++a) {
 #pragma unroll
     for (int b = 0; b < RT_TOK; ++b) {
-      float s = warp_fold_sum(acc[a][b]);
-      int e = e0 + a, t = t0 + b;
-      if (lane == ((a * RT_TOK + b) & 31) && e < E && t < T) logits[(size_t)t * E + e] = f32_to_bf16(s);
+      const unsigned long long pr = acc[a][b >> 1];
+      const float v = __uint_as_float(static_cast<uint32_t>((b & 1) ? (pr >> 32) : pr));
+      const float sum = warp_fold_sum(v);
+      const int e = e0 + a, t = t0 + b;
+      if (lane == ((a * RT_TOK + b) & 31) && e < E && t < T) logits[(size_t)t * E + e] = f32_to_bf16(sum);
     }
   }
 }

@@ -223,7 +223,8 @@ class Qwen3_xMoEWrapper(SlotTable):
             self._side_stream = torch.cuda.Stream(x2.device)
         side = self._side_stream
         side.wait_stream(main)
-        x2.record_stream(side)  # read on the side stream after the caller may drop it
+        if not torch.cuda.is_current_stream_capturing():  # a graph's pool keeps its tensors alive
+            x2.record_stream(side)  # read on the side stream after the caller may drop it
         with torch.cuda.stream(side):
             sy = shared_expert_forward(self.inner.shared_expert, x2)
             sg = ops.router_linear(x2, self.inner.shared_expert_gate)
@@ -237,8 +238,9 @@ class Qwen3_xMoEWrapper(SlotTable):
         sy, sg = pending
         main = torch.cuda.current_stream(sy.device)
         main.wait_stream(self._side_stream)
-        sy.record_stream(main)
-        sg.record_stream(main)
+        if not torch.cuda.is_current_stream_capturing():
+            sy.record_stream(main)
+            sg.record_stream(main)
         return sy, sg
 
     def _gather_forward_dispatched(self, x2: torch.Tensor, d: ops.Dispatch, arena: SlottedGLU) -> torch.Tensor:
@@ -289,6 +291,46 @@ class Qwen3_xMoEWrapper(SlotTable):
         shared_y, shared_gate = self._shared_end(pending)
         out = _combine_shared(y.reshape(B * S, self.inner.top_k, H), scores, shared_y, shared_gate)
         return out.reshape(B, S, H)
+
+    def capture(self, B: int, S: int, warmup: int = 2, seed: int = 0) -> None:
+        """Record the layer call for [B, S, H] inputs in a CUDA graph, so that
+        ``replay`` runs it on new tokens for the host cost of one graph
+        launch.  Only the non-streaming wrapper (every expert resident, no
+        trace recorder): the streaming branch reads slot misses on the host.
+        No counterpart in the reference (MLX builds its own graphs)."""
+        if self.expert_cache is not None or self._identity is None:
+            raise ValueError("only the non-streaming wrapper (all experts resident) can be captured")
+        if self.should_capture_traces:
+            raise ValueError("a wrapper with a trace recorder cannot be captured")
+        dev = self._device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        H = self.inner.hidden_size
+        self.graph_input = torch.randn((B, S, H), generator=g, device=dev).to(torch.bfloat16)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):  # warm-up off the default stream, as capture requires
+            for _ in range(warmup):
+                self(self.graph_input)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        n0 = ops.LAUNCHES[0]
+        with torch.cuda.graph(graph):
+            self.graph_output = self(self.graph_input)
+        self._graph_launches = ops.LAUNCHES[0] - n0
+        self._graph = graph
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        """One captured layer call; ``x`` (if given) is first copied into the
+        graph's input.  Returns the graph's output buffer [B, S, H],
+        overwritten by the next replay."""
+        if getattr(self, "_graph", None) is None:
+            raise RuntimeError("capture() first")
+        if x is not None:
+            self.graph_input.copy_(x, non_blocking=True)
+        self._graph.replay()
+        ops.LAUNCHES[0] += self._graph_launches
+        return self.graph_output
 
     def forward_resident(self, x2: torch.Tensor, timing: dict | None = None) -> torch.Tensor:
         """The non-streaming step on [T, H] with no host synchronisation at all
