@@ -44,7 +44,7 @@ def _worker(rank, world, port, errfile, transport):
         block, _ = make_layer(cfg, device=dev)
         single = Qwen3_xMoEWrapper(block, "fp", "l", 0)
         for step in range(3 if transport == "p2p" else 1):
-            T = 40 + 24 * rank - 7 * step  # ragged token counts across ranks and steps
+            T = 40 + 8 * (rank % 4) - 7 * step  # ragged token counts across ranks and steps (<= 64)
             x = make_tokens(cfg, T, device=dev, step=10 * step + rank)
             out = ep(x)
             ref = single.forward_resident(x)
@@ -97,6 +97,31 @@ def test_ep_two_gpus_matches_single_gpu(tmp_path, transport):
     err = tmp_path / "err.txt"
     ctx = mp.get_context("spawn")
     procs = [ctx.Process(target=_worker, args=(r, world, port, str(err), transport)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("EP rank hung")
+    msg = err.read_text() if err.exists() else ""
+    assert all(p.exitcode == 0 for p in procs), msg
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs more than 2 GPUs")
+def test_ep_all_gpus_matches_single_gpu(tmp_path):
+    """The peer transport over every GPU of the box (the largest power of two
+    that divides the 64 experts): ragged tokens, eager steps and graph
+    replays, against the single-GPU layer."""
+    import torch.multiprocessing as mp
+
+    world = 1
+    while world * 2 <= min(8, torch.cuda.device_count()):
+        world *= 2
+    port = _free_port()
+    err = tmp_path / "err.txt"
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(err), "p2p")) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
