@@ -226,9 +226,10 @@ size_t sg_expert_bytes(const sg_arena* arena);
  * step number lives in the region (sg_ep_send bumps it), so a step captured
  * in a CUDA graph replays correctly.  Per step:
  *   sg_ep_send(regions, R, me, cap, H, x [T, H], inds [T, k] global expert
- *     ids, T, k, per = experts per rank, pos [T*k] and dcnt [R] int32
- *     scratch): every pair's token row, local expert id and pair id
- *     into its owner's inbox, then that rank's step flag (T * k <= cap);
+ *     ids, T, k, per = experts per rank, dcnt [R] int32 counters, zero
+ *     before the first call and left zero by every call): every pair's token
+ *     row, local expert id and pair id into its owner's inbox, then that
+ *     rank's step flag (T * k <= cap);
  *   sg_ep_wait_inbox(own region, ...): waits for every source's flag
  *     and marks unused inbox entries empty (expert id -1);
  *   sg_dispatch + sg_glu_gate_up / sg_glu_down then run over the R * cap
@@ -252,7 +253,7 @@ int sg_ep_ipc_handle(void* region, uint8_t* handle64);
 int sg_ep_ipc_open(const uint8_t* handle64, void** region);
 int sg_ep_ipc_close(void* region);
 int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x, const int32_t* inds,
-               int T, int k, int per, int32_t* pos, int32_t* dcnt, void* stream);
+               int T, int k, int per, int32_t* dcnt, void* stream);
 int sg_ep_wait_inbox(void* region, int R, int cap, int H, void* stream);
 int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y, void* stream);
 int sg_ep_wait_back(void* region, int R, int cap, int H, void* stream);

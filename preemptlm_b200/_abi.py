@@ -99,7 +99,7 @@ def load() -> ctypes.CDLL:
         "sg_ep_ipc_handle": (I32, [P, P]),
         "sg_ep_ipc_open": (I32, [P, P]),
         "sg_ep_ipc_close": (I32, [P]),
-        "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P, P]),
+        "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P]),
         "sg_ep_wait_inbox": (I32, [P, I32, I32, I32, P]),
         "sg_ep_send_back": (I32, [P, I32, I32, I32, I32, P, P]),
         "sg_ep_wait_back": (I32, [P, I32, I32, I32, P]),

@@ -20,11 +20,13 @@
 // destination, so no inbox can overflow whatever the routing.
 //
 // A step (seq = 1, 2, ... in lockstep on all ranks, kept on the device):
-//   sg_ep_send:      plan (stable position of every pair within its
-//                    destination) and copy each pair's token row, expert id
-//                    and pair id into the destination's inbox; the last CTA
-//                    publishes the counts and raises flag_in[me] = seq at
-//                    every destination (system-scope release)
+//   sg_ep_send:      copy each pair's token row, expert id and pair id into
+//                    the destination's inbox, at a position taken from a
+//                    per-destination counter (the order within an inbox does
+//                    not matter: outputs go back by pair id); the last CTA
+//                    bumps the step number, publishes the counts, resets the
+//                    counters and raises flag_in[me] = seq at every
+//                    destination (system-scope release)
 //   sg_ep_wait_inbox: acquire flag_in[s] >= seq for every source s, then mark
 //                    the unused inbox entries empty (eid -1, ignored by
 //                    sg_dispatch)
@@ -133,70 +135,26 @@ __device__ __forceinline__ void copy_row(uint4* dst, const uint4* src, int chunk
 // consistent __threadfence_system).
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// Stable position of every pair within its destination rank, and the pair
-// count per destination.  One CTA of 1024 threads; pairs in chunks of 1024,
-// per-destination ranks by warp ballots, warp totals scanned per destination.
-constexpr int EP_PLAN_THREADS = 1024;
-__global__ void __launch_bounds__(EP_PLAN_THREADS)
-ep_plan_kernel(const int32_t* __restrict__ inds, int P, int per, int R, int32_t* __restrict__ pos,
-               int32_t* __restrict__ dcnt, uint32_t* __restrict__ step) {
-  __shared__ int wtot[32][EP_MAX_RANKS];
-  __shared__ int base[EP_MAX_RANKS];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x < EP_MAX_RANKS) base[threadIdx.x] = 0;
-  __syncthreads();
-  for (int c0 = 0; c0 < P; c0 += EP_PLAN_THREADS) {
-    const int p = c0 + threadIdx.x;
-    int d = -1;
-    if (p < P) {
-      const int e = inds[p];
-      d = (e >= 0 && e < per * R) ? e / per : -1;
-    }
-    int my_rank = 0;
-#pragma unroll
-    for (int q = 0; q < EP_MAX_RANKS; ++q) {
-      const unsigned m = __ballot_sync(0xffffffffu, d == q);
-      if (d == q) my_rank = __popc(m & ((1u << lane) - 1u));
-      if (lane == 0) wtot[warp][q] = __popc(m);
-    }
-    __syncthreads();
-    if (warp < EP_MAX_RANKS) {  // warp q: exclusive scan of destination q's warp totals
-      const int v = wtot[lane][warp];
-      int incl = v;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
-      }
-      const int b = base[warp];
-      wtot[lane][warp] = b + incl - v;
-      __syncwarp();
-      if (lane == 31) base[warp] = b + incl;
-    }
-    __syncthreads();
-    if (p < P) pos[p] = d >= 0 ? wtot[warp][d] + my_rank : -1;
-    __syncthreads();
-  }
-  if (threadIdx.x < R) dcnt[threadIdx.x] = base[threadIdx.x];
-  if (threadIdx.x == 0) *step += 1;  // this step's number, read by the step's later kernels
-}
-
 // One warp per pair: its token row (H bf16) to the destination's inbox, plus
-// its local expert id and pair id.  The last CTA to finish publishes the
-// counts and the step flag at every destination.
+// its local expert id and pair id, at a slot taken from dcnt[destination]
+// (zero on entry).  The last CTA to finish bumps the step number, publishes
+// the counts and the step flag at every destination and zeroes dcnt.
 __global__ void __launch_bounds__(256)
 ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, const uint16_t* __restrict__ x,
-               const int32_t* __restrict__ inds, const int32_t* __restrict__ pos, const int32_t* __restrict__ dcnt,
-               int P, size_t off_rows, size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in,
-               size_t off_step) {
+               const int32_t* __restrict__ inds, int32_t* __restrict__ dcnt, int P, size_t off_rows,
+               size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in, size_t off_step) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
   const int chunks = H >> 3;  // 16-byte chunks per row
   for (int p = gw; p < P; p += nw) {
-    const int e = inds[p], i = pos[p];
-    if (e < 0 || e >= per * R || i < 0 || i >= cap) continue;
+    const int e = inds[p];  // the same for the whole warp
+    if (e < 0 || e >= per * R) continue;
     const int d = e / per;
+    int i = 0;
+    if (lane == 0) i = atomicAdd(&dcnt[d], 1);
+    i = __shfl_sync(0xffffffffu, i, 0);
+    if (i >= cap) continue;  // cannot happen (at most P <= cap pairs per destination)
     uint8_t* dst_base = peers.base[d];
     const size_t slot = (size_t)me * cap + i;
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(p / k) * H);
@@ -218,9 +176,12 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
     const unsigned prev = atomicAdd(&g_ep_send_done, 1u);
     if (prev == gridDim.x - 1) {  // every CTA's rows are out: publish
       __threadfence();
-      for (int d = 0; d < R; ++d) reinterpret_cast<int32_t*>(peers.base[d] + off_cnt)[me] = dcnt[d];
+      for (int d = 0; d < R; ++d)  // the count, and the counter back to zero for the next step
+        reinterpret_cast<int32_t*>(peers.base[d] + off_cnt)[me] = atomicExch(&dcnt[d], 0);
+      uint32_t* step = reinterpret_cast<uint32_t*>(peers.base[me] + off_step);
+      const uint32_t seq = *step + 1;  // this step's number, read by the step's later kernels
+      *step = seq;
       fence_acq_rel_sys();
-      const uint32_t seq = *reinterpret_cast<const uint32_t*>(peers.base[me] + off_step);
       for (int d = 0; d < R; ++d) st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
       g_ep_send_done = 0;
     }
@@ -374,21 +335,18 @@ extern "C" int sg_ep_ipc_close(void* region) {
 }
 
 extern "C" int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16_t* x,
-                          const int32_t* inds, int T, int k, int per, int32_t* pos, int32_t* dcnt, void* stream) {
+                          const int32_t* inds, int T, int k, int per, int32_t* dcnt, void* stream) {
   int st = sg::ep_check(R, me, cap, H);
   if (st) return st;
   if (T < 0 || k < 1 || per < 1) return SG_ERR_INVALID_ARG;
   const int P = T * k;
   if (P > cap) return SG_ERR_CAPACITY;
-  if (!regions || (P > 0 && (!x || !inds || !pos)) || !dcnt) return SG_ERR_INVALID_ARG;
+  if (!regions || (P > 0 && (!x || !inds)) || !dcnt) return SG_ERR_INVALID_ARG;
   for (int i = 0; i < R; ++i)
     if (!regions[i]) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   cudaStream_t s = (cudaStream_t)stream;
-  sg::ep_plan_kernel<<<1, sg::EP_PLAN_THREADS, 0, s>>>(
-      inds, P, per, R, pos, dcnt, reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(regions[me]) + l.step));
-  SG_LAUNCH_CHECK();
-  sg::ep_send_kernel<<<sg::grid_for(P), 256, 0, s>>>(sg::peers_of(regions, R), me, R, cap, H, k, per, x, inds, pos,
+  sg::ep_send_kernel<<<sg::grid_for(P), 256, 0, s>>>(sg::peers_of(regions, R), me, R, cap, H, k, per, x, inds,
                                                        dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, l.step);
   SG_LAUNCH_CHECK();
   return SG_OK;

@@ -192,8 +192,7 @@ class PeerExchange:
         self.rows = _view(self.region + off[0], (n, hidden), torch.bfloat16, self.device)
         self.eids = _view(self.region + off[1], (n,), torch.int32, self.device)
         self.ybuf = _view(self.region + off[4], (self.cap, hidden), torch.bfloat16, self.device)
-        self.pos = torch.empty(self.cap, dtype=torch.int32, device=self.device)
-        self.dcnt = torch.empty(world, dtype=torch.int32, device=self.device)
+        self.dcnt = torch.zeros(world, dtype=torch.int32, device=self.device)  # inbox slot counters (kept at zero)
         self.group = group
 
     def close(self) -> None:
@@ -304,7 +303,7 @@ class ExpertParallelMoE:
         mark()
         stream = torch.cuda.current_stream(x.device).cuda_stream
         _abi.check(lib.sg_ep_send(ex.regions, R, self.rank, ex.cap, H, x.data_ptr(), inds.data_ptr(), T, k, per,
-                                  ex.pos.data_ptr(), ex.dcnt.data_ptr(), stream), "sg_ep_send")
+                                  ex.dcnt.data_ptr(), stream), "sg_ep_send")
         mark()
         _abi.check(lib.sg_ep_wait_inbox(ctypes.c_void_p(ex.region), R, ex.cap, H, stream), "sg_ep_wait_inbox")
         mark()

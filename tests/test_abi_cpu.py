@@ -83,9 +83,9 @@ def test_host_side_argument_checks(lib):
     assert list(off) == [0, rows, rows + 2 * 2560 * 4, rows + 2 * 2 * 2560 * 4, rows + 2 * 2 * 2560 * 4 + 256]
     assert lib.sg_ep_region_bytes(2, 2560, 2048) == off[4] + 2560 * 2048 * 2 + 2 * 256 + 256  # + step counter
     regs = (ctypes.c_void_p * 2)(1, 1)
-    assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 4, 5, 8, 1, 1, None) == _abi.SG_ERR_CAPACITY  # 20 > 16
-    assert lib.sg_ep_send(regs, 2, 2, 16, 256, 1, 1, 2, 5, 8, 1, 1, None) == _abi.SG_ERR_INVALID_ARG  # me
-    assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 2, 5, 0, 1, 1, None) == _abi.SG_ERR_INVALID_ARG  # per 0
+    assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 4, 5, 8, 1, None) == _abi.SG_ERR_CAPACITY  # 20 > 16
+    assert lib.sg_ep_send(regs, 2, 2, 16, 256, 1, 1, 2, 5, 8, 1, None) == _abi.SG_ERR_INVALID_ARG  # me
+    assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 2, 5, 0, 1, None) == _abi.SG_ERR_INVALID_ARG  # per 0
     assert lib.sg_ep_wait_inbox(None, 2, 16, 256, None) == _abi.SG_ERR_INVALID_ARG
     assert lib.sg_ep_alloc(0, None) == _abi.SG_ERR_INVALID_ARG
     a = _abi.sg_arena(num_slots=2, hidden=1024, inter=512, bits=8, group_size=64, gate_w=1, up_w=1, down_w=1,
