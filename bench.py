@@ -16,10 +16,17 @@ One JSON line on rank 0:
   value     whole-job tokens/s, inputs resident in HBM, CUDA-event timed
   e2e       tokens/s through the public layer call with the tokens copied
             host->device and the output device->host every step
-  roofline  the routed gate/up kernel: algorithmic bytes / its event time
-  cpu_baseline  the CPU oracle port on a bounded token sample (rank 0, N=1)
-``--impl reference`` times that CPU port alone (the reference itself is MLX,
-which is not installed here) on the same workload, all host cores.
+  roofline  the routed gate/up kernel: algorithmic bytes / its event time;
+            ``traffic`` scales the DRAM bytes per unique expert of the
+            committed ncu summary named in ``traffic_source``
+  cpu_baseline  the CPU oracle port on the same 256-token step (rank 0, N=1)
+  sweep     (N=1) every configuration at its benchmark sizes on one GPU:
+            decode tokens/s with the HBM fraction, prefill with the tensor
+            fraction, and the streaming miss path
+  strong    (N>1) a fixed global batch of 256 tokens split over the N GPUs
+``--impl reference`` times that CPU port alone (the reference itself runs on
+MLX, which is not installed here; the line records the import probe) on the
+same 256-token step, all host cores.
 """
 
 from __future__ import annotations
@@ -28,6 +35,7 @@ import argparse
 import gc
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -41,11 +49,12 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# DRAM bytes (read + write) of the routed gate/up launch per unique expert, from
-# an ncu capture of the same kernel on a smaller case of the workload (128
-# experts, 64 tokens: 291.59 MB for 128 unique experts); the launch streams
-# each unique expert's weights once, so traffic scales with the unique count
-TRAFFIC_PER_EXPERT = {"cfg3-q8-decode-shared": 291.59e6 / 128}
+# A committed ncu summary states the DRAM bytes (read + write) of the routed
+# gate/up launch per unique expert on a smaller case of a workload, on a line
+#   roofline-traffic: <workload> <bytes> bytes per unique expert
+# The launch streams each unique expert's weights once, so the traffic of a
+# bench launch is that figure times its unique experts.
+TRAFFIC_RE = re.compile(r"^roofline-traffic:\s+(\S+)\s+(\d+)\s+bytes per unique expert", re.M)
 QUEUE_AHEAD_CYCLES = 1_000_000_000  # ~0.5 s of device spin before the device-resident timed region
 METRIC = "SlottedGLU tokens/s at 1/2/4/8 B200; expert-GEMM HBM GB/s vs 8 TB/s peak"
 
@@ -72,6 +81,10 @@ def parse_args():
                     help="expert-parallel exchange: the library's NVLink peer-memory kernels or NCCL all-to-alls")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed device-resident steps (for ncu captures); prints ms/step")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-configuration sweep (N=1)")
+    ap.add_argument("--sweep-steps", type=int, default=20, help="timed steps per sweep point")
+    ap.add_argument("--sweep-only", default=None,
+                    help="comma-separated sweep configurations to run (default: all)")
     return ap.parse_args()
 
 
@@ -90,6 +103,26 @@ def tensor_peak():
         return float(p["bf16_tflops"]), "measured"
     except Exception:
         return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic(workload: str):
+    """(bytes per unique expert, summary file) from the committed ncu summaries."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for m in TRAFFIC_RE.finditer(f.read_text()):
+            if m.group(1) == workload:
+                return int(m.group(2)), f"profiles/{f.name}"
+    return None, None
+
+
+def mlx_probe() -> str:
+    """Whether the reference's own numerics (mlx, mlx_lm) import on this host."""
+    try:
+        import mlx.core  # noqa: F401
+        import mlx_lm  # noqa: F401
+
+        return "mlx and mlx_lm import"
+    except Exception as e:  # ModuleNotFoundError on the images this runs on
+        return f"{type(e).__name__}: {e}"
 
 
 # --------------------------------------------------------------------------- clocks
@@ -146,29 +179,32 @@ class ClockSampler:
 # --------------------------------------------------------------------------- CPU port (oracle)
 
 
-def cpu_port_step(cfg, x_bits, router_bits, expert_fn, shared, sgate_bits, threads):
-    """The CPU oracle's layer on a token sample, experts spread over threads."""
+def cpu_port_step(cfg, x_bits, host, threads):
+    """The CPU oracle's layer on one batch of tokens, experts spread over
+    threads (one BLAS thread each)."""
     import numpy as np
+    from threadpoolctl import threadpool_limits
 
     from oracle import slotted_glu_oracle as orc
 
     T = x_bits.shape[0]
     x = orc.bf16_bits_to_f32(x_bits)
-    logits = orc.router_logits(x_bits, router_bits)
+    logits = orc.router_logits(x_bits, host["router"])
     inds, sc, _ = orc.get_routings(logits, cfg.top_k, cfg.norm_topk_prob)
     flat = inds.reshape(-1)
     y = np.zeros((T * cfg.top_k, cfg.hidden), np.float32)
+    experts = host["experts"]
 
     def run(eid):
         pairs = np.nonzero(flat == eid)[0]
-        y[pairs] = orc.expert_forward(x[pairs // cfg.top_k], expert_fn(int(eid)))
+        y[pairs] = orc.expert_forward(x[pairs // cfg.top_k], experts[int(eid)])
 
-    with ThreadPoolExecutor(max_workers=threads) as ex:
+    with threadpool_limits(1), ThreadPoolExecutor(max_workers=threads) as ex:
         list(ex.map(run, np.unique(flat)))
     sy = sg = None
-    if shared is not None:
-        sy = orc.expert_forward(x, shared)
-        sg = orc.bf16_bits_to_f32(orc.router_logits(x_bits, sgate_bits))
+    if host["shared"] is not None:
+        sy = orc.expert_forward(x, host["shared"])
+        sg = orc.bf16_bits_to_f32(orc.router_logits(x_bits, host["shared_gate"]))
     return orc.combine_shared(y.reshape(T, cfg.top_k, cfg.hidden), orc.bf16_bits_to_f32(sc), sy, sg)
 
 
@@ -186,8 +222,7 @@ def _b16(t):
 
 
 def _deq(cfg, ts, i):
-    """Dequantised weights of expert ``i`` of a host tensor dict (the CPU
-    port's per-call dequantisation)."""
+    """Dequantised weights of expert ``i`` of a host tensor dict."""
     import numpy as np
 
     from oracle import slotted_glu_oracle as orc
@@ -197,57 +232,68 @@ def _deq(cfg, ts, i):
         if cfg.bits == 16:
             mats.append(orc.bf16_bits_to_f32(_b16(ts[f"{p}.weight"][i])))
         else:
-            mats.append(orc.dequant_affine(ts[f"{p}.weight"][i].cpu().numpy().view(np.uint32),
+            mats.append(orc.dequant_affine(ts[f"{p}.weight"][i].numpy().view(np.uint32),
                                            _b16(ts[f"{p}.scales"][i]), _b16(ts[f"{p}.biases"][i]), cfg.bits))
     return orc.ExpertWeights(*mats)
 
 
-def _host_layer(cfg, n_samples, sample_tokens, tens=None):
-    """Host copies of what the CPU port's samples touch: router, shared expert
-    and, per routed expert id, its packed tensors.  Copied from the GPU layer,
-    or generated on the host (reference arm: no GPU use at all; routed experts
-    then come from per-expert seeds).  Untimed set-up."""
+def host_layer(cfg, T, n_steps, tens=None):
+    """Host copy of the layer for the CPU port, made once before any timing:
+    router and shared-gate bits, and the weights of every routed expert the
+    timed token batches reach, dequantised once (the reference's arena holds
+    bf16 expert weights, expert_cache.py:198-224, so its step does no
+    dequantisation either).  Copied from the GPU layer's tensors, or generated
+    on the host (reference arm: no GPU use; routed experts then come from
+    per-expert seeds, with the layer's shapes and distributions)."""
+    import numpy as np
+    import torch
+
     from oracle import slotted_glu_oracle as orc
     from preemptlm_b200.synthetic import _gen, _randn, make_expert_tensors
 
     c = cfg.cfg_id
+    threads = os.cpu_count() or 1
     if tens is not None:
-        router, shared = tens["router"].cpu(), tens["shared"]
+        router = tens["router"].cpu()
         sgate = None if tens["shared_gate"] is None else tens["shared_gate"].cpu()
+        shared_t = None if tens["shared"] is None else {k: v.cpu() for k, v in tens["shared"].items()}
     else:
         router = _randn((cfg.num_experts, cfg.hidden), _gen(1000 * c + 1, "cpu"), "cpu", 0.02)
-        shared = sgate = None
+        shared_t = sgate = None
         if cfg.shared_inter is not None:
-            shared = make_expert_tensors(cfg, 1, cfg.shared_inter, 1000 * c + 3, "cpu")
+            shared_t = make_expert_tensors(cfg, 1, cfg.shared_inter, 1000 * c + 3, "cpu")
             sgate = _randn((1, cfg.hidden), _gen(1000 * c + 4, "cpu"), "cpu", 0.02)
-    if shared is not None:
-        shared = {k: v.cpu() for k, v in shared.items()}
+    rb = _b16(router)
     needed = set()
-    rb = _b16(router)
-    for i in range(n_samples):
-        lg = orc.router_logits(_b16(_sample_tokens(cfg, sample_tokens, i)), rb)
+    for i in range(n_steps):
+        lg = orc.router_logits(_b16(_sample_tokens(cfg, T, i)), rb)
         needed.update(orc.get_routings(lg, cfg.top_k, cfg.norm_topk_prob)[0].reshape(-1).tolist())
-    experts = {}
-    for e in sorted(needed):
-        if tens is not None:
-            experts[e] = {k: v[e: e + 1].cpu() for k, v in tens["experts"].items()}
-        else:
-            experts[e] = make_expert_tensors(cfg, 1, cfg.inter, 1000 * c + 2 + 7919 * (e + 1), "cpu")
-    return experts, router, shared, sgate
+    needed = sorted(needed)
+    if tens is not None:
+        idx = torch.tensor(needed, device=tens["router"].device)
+        host_t = {k: v.index_select(0, idx).cpu() for k, v in tens["experts"].items()}
+        load = lambda j: _deq(cfg, host_t, j)  # noqa: E731
+    else:
+        def load(j):
+            e = needed[j]
+            return _deq(cfg, make_expert_tensors(cfg, 1, cfg.inter, 1000 * c + 2 + 7919 * (e + 1), "cpu"), 0)
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(1), ThreadPoolExecutor(max_workers=threads) as ex:
+        mats = list(ex.map(load, range(len(needed))))
+    return {"router": rb, "experts": dict(zip(needed, mats)),
+            "shared": None if shared_t is None else _deq(cfg, shared_t, 0),
+            "shared_gate": None if sgate is None else _b16(sgate)}
 
 
-def time_cpu_port(cfg, sample_tokens, steps, host_layer, warmup=0):
+def time_cpu_port(cfg, T, steps, host, warmup=0):
+    """Seconds per step of the CPU port on batches of T tokens, all host threads."""
     threads = os.cpu_count() or 1
-    experts, router, shared_t, sgate = host_layer
-    rb = _b16(router)
-    sgate_bits = None if sgate is None else _b16(sgate)
-    expert_fn = lambda e: _deq(cfg, experts[e], 0)  # noqa: E731
     times = []
     for i in range(warmup + steps):
-        xb = _b16(_sample_tokens(cfg, sample_tokens, i))
+        xb = _b16(_sample_tokens(cfg, T, i))
         t0 = time.perf_counter()
-        shared = None if shared_t is None else _deq(cfg, shared_t, 0)
-        cpu_port_step(cfg, xb, rb, expert_fn, shared, sgate_bits, threads)
+        cpu_port_step(cfg, xb, host, threads)
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     return times, threads
@@ -286,6 +332,125 @@ def _kernel_roofline(cfg, timing, rows_per_step, T_local):
             "gu_tflops": gu_f / (sum(gu_ms) * 1e-3) / 1e12, "dn_tflops": dn_f / (sum(dn_ms) * 1e-3) / 1e12,
             "pairs_per_expert": (gu_f / (4 * H * I)) / max(1, sum(us)),
             "mean_unique": st.mean(us)}
+
+
+def _abi_check_status(where: str) -> None:
+    """Raise if a kernel of the library recorded an error (a bounded wait that
+    gave up) since the last check; synchronises, so never inside a timed region."""
+    from preemptlm_b200 import ops
+
+    st = ops.device_status(reset=True)
+    if st != 0:
+        raise RuntimeError(f"{where}: a kernel recorded status {st} (bounded wait expired)")
+
+
+# (configuration, token counts) of the one-GPU sweep: the sizes BASELINE's configurations name
+SWEEP = (("cfg3", (1, 8, 32, 128)), ("cfg1", (1, 4, 16, 32)), ("cfg2", (512, 2048, 8192)), ("cfg4", (64, 4096)))
+
+
+def _step_roofline(cfg, T, U, ms):
+    """Fraction of the binding roofline of a whole layer step: algorithmic
+    bytes (every byte once: the unique experts' weights, router, shared
+    expert, tokens in and out) over the measured copy bandwidth, or
+    algorithmic FLOPs over the measured bf16 tensor peak, whichever takes
+    longer."""
+    hbm, _ = hbm_peak()
+    tpk, _ = tensor_peak()
+    H, E, k, I = cfg.hidden, cfg.num_experts, cfg.top_k, cfg.inter
+    nbytes = U * cfg.expert_bytes() + cfg.shared_bytes() + E * H * 2 + 2 * T * H * 2
+    flops = 2 * T * k * 3 * H * I + 2 * T * H * E
+    if cfg.shared_inter is not None:
+        nbytes += H * 2
+        flops += 2 * T * 3 * H * cfg.shared_inter + 2 * T * H
+    t_hbm, t_tc = nbytes / (hbm * 1e9), flops / (tpk * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+    return {"bound": bound, "step_frac": round(max(t_hbm, t_tc) / (ms * 1e-3), 4),
+            "step_GBs": round(nbytes / (ms * 1e-3) / 1e9, 1), "step_TFLOPs": round(flops / (ms * 1e-3) / 1e12, 1)}
+
+
+def _sweep_point(moe, cfg, T, steps, warmup, dev, flush):
+    """One (configuration, T) point: the layer step captured as a CUDA graph
+    and replayed on new tokens, an L2 flush (a 256 MB read) before every
+    timed replay, CUDA events around each replay; then the same steps eagerly
+    with events around the routed gate/up and down launches."""
+    import torch
+
+    from preemptlm_b200.synthetic import make_tokens
+
+    H = cfg.hidden
+    xs = [make_tokens(cfg, T, device=dev, step=5000 + i) for i in range(warmup + steps)]
+    for i in range(warmup):
+        moe.forward_resident(xs[i], timing={})
+    moe.capture(1, T)
+    g_in = moe.graph_input.view(T, H)
+    for i in range(warmup):
+        g_in.copy_(xs[i], non_blocking=True)
+        moe.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        g_in.copy_(xs[warmup + i], non_blocking=True)
+        flush()
+        ev[i][0].record()
+        moe.replay()
+        ev[i][1].record()
+    timing: dict = {}
+    for i in range(steps):
+        flush()
+        moe.forward_resident(xs[warmup + i], timing=timing)
+    torch.cuda.synchronize()
+    _abi_check_status(f"sweep {cfg.name} T={T}")
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    rl = _kernel_roofline(cfg, timing, None, T)
+    hbm, _ = hbm_peak()
+    tpk, _ = tensor_peak()
+    gu_ms, dn_ms = statistics.mean(rl["gu_ms"]), statistics.mean(rl["dn_ms"])
+    pt = {"T": T, "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+          "unique_experts": round(rl["mean_unique"], 1), "pairs_per_expert": round(rl["pairs_per_expert"], 1),
+          **_step_roofline(cfg, T, rl["mean_unique"], ms),
+          "gate_up": {"ms": round(gu_ms, 4), "GBs": round(rl["gu_gbs"], 1), "hbm_frac": round(rl["gu_gbs"] / hbm, 4),
+                      "TFLOPs": round(rl["gu_tflops"], 1), "tensor_frac": round(rl["gu_tflops"] / tpk, 4)},
+          "down": {"ms": round(dn_ms, 4), "GBs": round(rl["dn_gbs"], 1), "hbm_frac": round(rl["dn_gbs"] / hbm, 4),
+                   "TFLOPs": round(rl["dn_tflops"], 1), "tensor_frac": round(rl["dn_tflops"] / tpk, 4)}}
+    return pt
+
+
+def run_sweep(args, dev):
+    """Every configuration at its benchmark sizes on one GPU (all experts of
+    the layer resident), plus the streaming miss path."""
+    import torch
+
+    from preemptlm_b200 import ops
+    from preemptlm_b200.layer import Qwen3_xMoEWrapper
+    from preemptlm_b200.synthetic import CONFIGS, make_layer
+
+    only = set(args.sweep_only.split(",")) if args.sweep_only else None
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)  # 256 MB, twice the L2
+    sink = torch.empty(1, dtype=torch.float32, device=dev)
+
+    def flush():
+        torch.amax(flush_buf, dim=0, keepdim=True, out=sink)
+
+    ops.set_glu_path("auto")
+    out = {"l2": "a 256 MB read before every timed step", "timed_steps": "CUDA graph replays",
+           "steps": args.sweep_steps}
+    for name, Ts in SWEEP:
+        if only and name not in only:
+            continue
+        cfg = CONFIGS[name]
+        block, tens = make_layer(cfg, device=dev)
+        del tens  # the arena holds its own copy
+        torch.cuda.empty_cache()
+        moe = Qwen3_xMoEWrapper(block, "synthetic", "model.layers.0.mlp", 0)
+        pts = [_sweep_point(moe, cfg, T, args.sweep_steps, 3, dev, flush) for T in Ts]
+        out[name] = {"workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
+                                 f"shared{cfg.shared_inter} {'bf16' if cfg.bits == 16 else f'affine-q{cfg.bits} g64'}, "
+                                 f"all {cfg.num_experts} experts resident", "points": pts}
+        del moe, block
+        torch.cuda.empty_cache()
+    if not only or "cfg5" in only:
+        out["cfg5"] = stream_points(dev, steps=max(10, args.sweep_steps), warmup=3)
+    return out
 
 
 def run_ours(args, rank, world, local_rank):
@@ -496,18 +661,64 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    # a bounded wait that gave up inside any of the steps above fails the run
+    if use_ep:
+        ep.check()
+    else:
+        _abi_check_status("timed steps")
+
+    # ---------------------------------------------------------------- strong scaling (N > 1)
+    strong = None
+    if use_ep and world > 1 and graph_ok:
+        Ts = max(1, 256 // world)
+        ep.capture(Ts)
+        xs_s = [make_tokens(cfg, Ts, device=dev, step=3000 + i + 1000 * rank) for i in range(args.steps)]
+        for i in range(min(3, args.steps)):
+            ep.replay(xs_s[i])
+        torch.cuda.synchronize()
+        barrier()
+        gc.disable()
+        torch.cuda._sleep(QUEUE_AHEAD_CYCLES)
+        ep.replay(xs_s[0])  # lines up the ranks after the spin (untimed)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for i in range(args.steps):
+            ep.replay(xs_s[i])
+        s1.record()
+        torch.cuda.synchronize()
+        gc.enable()
+        barrier()
+        ep.check()
+        t = torch.tensor([s0.elapsed_time(s1) / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_s = float(t.item())
+        strong = {"tokens_global": Ts * world, "tokens_per_gpu": Ts, "value": round(Ts * world / (ms_s * 1e-3), 1),
+                  "unit": "tokens/s", "ms_per_step": round(ms_s, 4), "scaling": "strong",
+                  "timed_steps": "CUDA graph replays"}
+
     # ---------------------------------------------------------------- CPU baseline (oracle port)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample, n = 8, 4
-        times, threads = time_cpu_port(cfg, sample, n, _host_layer(cfg, n + 1, sample, tens), warmup=1)
-        cpu = {"value": round(sample * len(times) / sum(times), 3), "unit": "tokens/s", "cores": threads,
+        n = 2
+        times, threads = time_cpu_port(cfg, T, n, host_layer(cfg, T, n + 1, tens), warmup=1)
+        cpu = {"value": round(T * len(times) / sum(times), 3), "unit": "tokens/s", "cores": threads,
                "kind": "port",
-               "sample": f"{len(times)} steps of {sample} tokens through the CPU oracle of the same layer "
-                         f"(routing, dequantise, fp32 matmul), experts over {threads} threads"}
+               "sample": f"{len(times)} steps of the same {T}-token step through the CPU oracle of the layer "
+                         f"(router, routing, fp32 matmuls of weights dequantised once at set-up, combine), "
+                         f"experts over {threads} threads"}
+
+    # ---------------------------------------------------------------- per-configuration sweep (one GPU)
+    sweep = None
+    if world == 1 and not use_ep and not args.no_sweep and not args.experts:
+        del moe, block, tens
+        torch.cuda.empty_cache()
+        sweep = run_sweep(args, dev)
 
     shard = cfg.num_experts // world
     value = T * world / (ms_step * 1e-3)
+    # DRAM bytes per unique expert of the same kernel from the committed ncu
+    # summary (a 1-GPU capture of this workload's layer shape)
+    traffic_pe, traffic_src = profile_traffic(cfg.name) if not args.experts else (None, None)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -539,8 +750,8 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {
             "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
             "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4), "peak_kind": peak_kind,
-            "traffic": (round(TRAFFIC_PER_EXPERT[cfg.name] * us_mean) if cfg.name in TRAFFIC_PER_EXPERT
-                        and world == 1 and not args.experts else None),
+            "traffic": round(traffic_pe * us_mean) if traffic_pe else None,
+            "traffic_source": traffic_src,
             "bytes_per_launch": round(rl["gu_bytes"] / len(rl["gu_ms"])),
             "ms_per_launch": round(statistics.mean(rl["gu_ms"]), 5),
             "down": {"achieved": round(rl["dn_gbs"], 1), "frac": round(rl["dn_gbs"] / peak, 4),
@@ -558,6 +769,10 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "cpu_baseline": cpu,
     }
+    if strong is not None:
+        line["strong"] = strong
+    if sweep is not None:
+        line["sweep"] = sweep
     if rl["pairs_per_expert"] >= 64:
         # prefill-sized expert groups: the gate/up launch is tensor-core bound
         r = line["roofline"]
@@ -576,38 +791,65 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_reference(args, rank, world):
+    """The CPU port of the layer (the oracle; the reference's own MLX numerics
+    do not import here) on the same step as our arm: a batch of --tokens
+    tokens (256) of the cfg3 layer, all host cores."""
     if rank != 0:
         return
     from preemptlm_b200.synthetic import CONFIGS
 
     cfg = CONFIGS[args.workload]
-    sample = 4
-    host = _host_layer(cfg, args.warmup + args.steps, sample)
-    times, threads = time_cpu_port(cfg, sample, args.steps, host, warmup=args.warmup)
-    value = sample * len(times) / sum(times)
+    T = args.tokens
+    probe = mlx_probe()
+    warm = min(args.warmup, 1)  # CPU steps need no long warm-up; the run stays within minutes
+    t0 = time.perf_counter()
+    host = host_layer(cfg, T, warm + args.steps)
+    setup_s = time.perf_counter() - t0
+    times, threads = time_cpu_port(cfg, T, args.steps, host, warmup=warm)
+    value = T * len(times) / sum(times)
+    sample = (f"{len(times)} steps of {T} tokens of the {cfg.name} layer through the CPU oracle port (router, "
+              f"routing, fp32 matmuls of expert weights dequantised once at set-up, combine), experts over "
+              f"{threads} threads; mlx probe: {probe}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
-        "steps": len(times), "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 2),
+        "steps": len(times), "warmup": warm, "ms_per_step": round(1e3 * sum(times) / len(times), 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": f"u{cfg.bits}" if cfg.bits != 16 else "bf16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)",
-        "config": {"workload": f"{cfg.name} (CPU port, {sample}-token sample per step)", "tokens_per_gpu": args.tokens,
-                   "parallelism": "cpu"},
+        "config": {"workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
+                               f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, decode {T} tokens per step "
+                               f"(CPU port, one host)",
+                   "tokens_per_gpu": T, "parallelism": "cpu", "setup_s": round(setup_s, 1)},
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} tokens per step through the CPU oracle of the layer; the reference's "
-                                   "MLX path cannot be installed here (mlx/mlx-lm absent, no network)"},
+                         "sample": sample},
+        "mlx_probe": probe,
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_stream(args, rank, world, local_rank):
+def _fs_of(path) -> str:
+    """File-system type of the mount holding ``path`` (from /proc/mounts)."""
+    try:
+        best, fs = "", "unknown"
+        p = str(Path(path).resolve())
+        for line in Path("/proc/mounts").read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 3 and p.startswith(parts[1]) and len(parts[1]) > len(best):
+                best, fs = parts[1], f"{parts[2]} ({parts[0]} on {parts[1]})"
+        return fs
+    except Exception:
+        return "unknown"
+
+
+def stream_points(dev, steps, warmup, batches=(1, 16)):
     """Streaming miss path (config-2 layer shape: H2048 E128 k8 I768, affine
     q4 g64, 64 slots): a seeded expert bank written to local disk, Zipf(1.1)
     expert popularity, demand refills through DiskBackedExpertLoader (pread
-    into pinned host buffers, cudaMemcpyAsync into slots on a side stream while
-    the shared-expert-free step continues), end-to-end decode tokens/s at batch
-    1 and 16 (tokens host->device, output device->host every step)."""
+    into pinned host buffers, cudaMemcpyAsync into slots on a side stream),
+    end-to-end decode tokens/s (tokens host->device, output device->host every
+    step)."""
+    import shutil
     import tempfile
 
     import torch
@@ -618,10 +860,6 @@ def run_stream(args, rank, world, local_rank):
     from preemptlm_b200.loader import DiskBackedExpertLoader, HostExpertCache
     from preemptlm_b200.synthetic import CONFIGS, make_layer, make_zipf_tokens, write_bank
 
-    if world > 1:
-        raise SystemExit("the streaming workload runs on one GPU")
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
     cfg = CONFIGS["cfg2"].scaled(name="cfg5-stream-q4", num_slots=64)
     block, tens = make_layer(cfg, device=dev)
     tmp = Path(tempfile.mkdtemp(prefix="sg_bank_", dir=os.environ.get("SG_BANK_DIR")))
@@ -629,48 +867,64 @@ def run_stream(args, rank, world, local_rank):
     write_bank(tmp, cfg, tens["experts"], block.switch_mlp.tensor_names())
     os.sync()
     write_s = time.perf_counter() - t0
-    results = {}
-    for batch in (1, 16):
-        bank = PreadExpertBank(tmp, bypass_page_cache=True)
-        nbytes = bank.manifest.expert_num_bytes()
-        cache = HostExpertCache(ExpertCacheManager(budget_bytes=32 * nbytes))
-        loader = DiskBackedExpertLoader(expert_bank=bank, cache=cache)
+    results = {"workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} affine-q4 g64, "
+                           f"{cfg.num_slots} slots, host blob cache of 32 experts, lfru slots, Zipf(1.1) routing",
+               "bank_fs": _fs_of(tmp), "bank_write_s": round(write_s, 2)}
+    try:
+        for batch in batches:
+            bank = PreadExpertBank(tmp, bypass_page_cache=True)
+            nbytes = bank.manifest.expert_num_bytes()
+            cache = HostExpertCache(ExpertCacheManager(budget_bytes=32 * nbytes))
+            loader = DiskBackedExpertLoader(expert_bank=bank, cache=cache)
 
-        class Cand:
-            layer_path, block_idx = "model.layers.0.mlp", 0
+            class Cand:
+                layer_path, block_idx = "model.layers.0.mlp", 0
 
-        moe = Qwen3_xMoEWrapper.make_wrapper_factory(model_fingerprint=bank.model_fingerprint, expert_loader=loader,
-                                                     expert_cache=cache, num_slots=cfg.num_slots, slot_size=nbytes,
-                                                     slot_policy="lfru")(block, Cand())
-        n = args.warmup + args.steps
-        xs = make_zipf_tokens(tens["router"], n * batch, cfg.top_k, seed=500 + batch, device=dev)
-        x_host = xs.cpu().pin_memory().view(n, batch, cfg.hidden)
-        out_host = torch.empty((batch, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+            moe = Qwen3_xMoEWrapper.make_wrapper_factory(model_fingerprint=bank.model_fingerprint,
+                                                         expert_loader=loader, expert_cache=cache,
+                                                         num_slots=cfg.num_slots, slot_size=nbytes,
+                                                         slot_policy="lfru")(block, Cand())
+            n = warmup + steps
+            xs = make_zipf_tokens(tens["router"], n * batch, cfg.top_k, seed=500 + batch, device=dev)
+            x_host = xs.cpu().pin_memory().view(n, batch, cfg.hidden)
+            out_host = torch.empty((batch, cfg.hidden), dtype=torch.bfloat16).pin_memory()
 
-        def step(i):
-            xd = x_host[i].to(dev, non_blocking=True)
-            out_host.copy_(moe(xd.view(1, batch, cfg.hidden)).view(batch, cfg.hidden), non_blocking=True)
+            def step(i):
+                xd = x_host[i].to(dev, non_blocking=True)
+                out_host.copy_(moe(xd.view(1, batch, cfg.hidden)).view(batch, cfg.hidden), non_blocking=True)
 
-        for i in range(args.warmup):
-            step(i)
-        torch.cuda.synchronize()
-        moe.admit_stats.update(steps=0, unique=0, missed=0)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(args.warmup, n):
-            step(i)
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        st = moe.admit_stats
-        results[f"batch{batch}"] = {"tokens_per_s": round(batch * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
-                                    "hit_rate": round(1 - st["missed"] / max(1, st["unique"]), 4),
-                                    "refills_per_step": round(st["missed"] / max(1, st["steps"]), 2)}
-        loader.close()
-        bank.close()
-    import shutil
+            for i in range(warmup):
+                step(i)
+            torch.cuda.synchronize()
+            moe.admit_stats.update(steps=0, unique=0, missed=0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(warmup, n):
+                step(i)
+            e1.record()
+            torch.cuda.synchronize()
+            _abi_check_status(f"streaming batch {batch}")
+            ms = e0.elapsed_time(e1) / steps
+            st = moe.admit_stats
+            results[f"batch{batch}"] = {"tokens_per_s": round(batch * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                                        "hit_rate": round(1 - st["missed"] / max(1, st["unique"]), 4),
+                                        "refills_per_step": round(st["missed"] / max(1, st["steps"]), 2)}
+            loader.close()
+            bank.close()
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return results
 
-    shutil.rmtree(tmp, ignore_errors=True)
+
+def run_stream(args, rank, world, local_rank):
+    """``--workload cfg5``: the streaming miss path alone (one GPU)."""
+    import torch
+
+    if world > 1:
+        raise SystemExit("the streaming workload runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    results = stream_points(dev, args.steps, args.warmup)
     if rank == 0:
         b16 = results["batch16"]
         print(json.dumps({
@@ -678,9 +932,7 @@ def run_stream(args, rank, world, local_rank):
             "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": b16["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u4", "data": "synthetic (seeded bank on local disk, Zipf(1.1) routing)",
-            "config": {"workload": f"{cfg.name}: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
-                                   f"affine-q4 g64, {cfg.num_slots} slots, host cache 32 experts, lfru slots",
-                       "bank_write_s": round(write_s, 2), **results},
+            "config": results,
         }))
 
 

@@ -236,11 +236,16 @@ size_t sg_expert_bytes(const sg_arena* arena);
  *     inbox rows and ids (sg_ep_layout gives their offsets) in place;
  *   sg_ep_send_back(regions, ..., y [R * cap, H]): each filled entry's
  *     output row to its source, at its pair id, then the step flag;
- *   sg_ep_wait_back(own region, ...): waits for every owner's flag; the
- *     region's pair-order output rows ([T * k, H], offset 4 of sg_ep_layout)
- *     are then complete for sg_combine.
- * Every wait is bounded (about 2 s); on expiry sg_device_status reports
- * SG_ERR_TIMEOUT.  Calls of one exchange must be issued on one stream.
+ *   sg_ep_wait_back(own region, ..., inds, T, k, per): waits for every
+ *     owner's flag; the region's pair-order output rows ([T * k, H], offset 4
+ *     of sg_ep_layout) are then complete for sg_combine.
+ * Every wait is bounded (2 s by default, sg_ep_set_wait_limit); on expiry
+ * sg_device_status reports SG_ERR_TIMEOUT, sg_ep_wait_inbox marks the late
+ * source's inbox empty and sg_ep_wait_back zeroes the output rows of the
+ * pairs owned by the late rank.  A timed-out exchange is out of step (a late
+ * peer may still write into the region): free it and build a new one.
+ * Calls of one exchange must be issued on one stream, one step at a time
+ * (the finished-CTA counters of a rank's send kernels live in its region).
  * Allocation, IPC and freeing are set-up calls (they synchronise); free a
  * region only after every rank has stopped using it. */
 long long sg_ep_region_bytes(int R, int cap, int H);
@@ -256,7 +261,11 @@ int sg_ep_send(void* const* regions, int R, int me, int cap, int H, const uint16
                int T, int k, int per, int32_t* dcnt, void* stream);
 int sg_ep_wait_inbox(void* region, int R, int cap, int H, void* stream);
 int sg_ep_send_back(void* const* regions, int R, int me, int cap, int H, const uint16_t* y, void* stream);
-int sg_ep_wait_back(void* region, int R, int cap, int H, void* stream);
+int sg_ep_wait_back(void* region, int R, int cap, int H, const int32_t* inds, int T, int k, int per,
+                    void* stream);
+/* Wait limit of the exchange kernels launched after this call on the current
+ * device, in microseconds (1 .. 600e6; default 2e6).  Synchronous. */
+int sg_ep_set_wait_limit(long long microseconds);
 
 #ifdef __cplusplus
 }

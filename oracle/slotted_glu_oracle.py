@@ -44,7 +44,12 @@ bit-exact):
 
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
+
+_ROUTER_CHUNK = 64  # tokens per work item of router_logits (numpy releases the GIL)
 
 # --------------------------------------------------------------------------- bf16
 
@@ -126,13 +131,29 @@ def router_logits(x_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
     T, H = x_bits.shape
     E = w_bits.shape[0]
     assert H % 256 == 0
-    X = bf16_bits_to_f32(x_bits).reshape(T, H // 256, 32, 8)
-    W = bf16_bits_to_f32(w_bits).reshape(E, H // 256, 32, 8)
-    acc = np.zeros((T, E, 32), dtype=np.float32)
-    for i in range(H // 256):
-        for e in range(8):
-            acc += X[:, None, i, :, e] * W[None, :, i, :, e]
-    return f32_to_bf16_bits(_lane_fold(acc))
+    # [i, e, rows, lane]: element h = 256 i + 8 lane + e of every row
+    Xt = np.ascontiguousarray(bf16_bits_to_f32(x_bits).reshape(T, H // 256, 32, 8).transpose(1, 3, 0, 2))
+    Wt = np.ascontiguousarray(bf16_bits_to_f32(w_bits).reshape(E, H // 256, 32, 8).transpose(1, 3, 0, 2))
+    out = np.empty((T, E), np.uint16)
+
+    def tokens(t0: int) -> None:  # one chunk of tokens; the order of adds per lane is (i, e)
+        t1 = min(T, t0 + _ROUTER_CHUNK)
+        acc = np.zeros((t1 - t0, E, 32), np.float32)
+        tmp = np.empty_like(acc)
+        for i in range(H // 256):
+            for e in range(8):
+                np.multiply(Xt[i, e, t0:t1, None, :], Wt[i, e][None], out=tmp)
+                np.add(acc, tmp, out=acc)
+        out[t0:t1] = f32_to_bf16_bits(_lane_fold(acc))
+
+    starts = range(0, T, _ROUTER_CHUNK)
+    if T > _ROUTER_CHUNK:
+        with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+            list(ex.map(tokens, starts))
+    else:
+        for t0 in starts:
+            tokens(t0)
+    return out
 
 
 # --------------------------------------------------------------------------- routing (a2)

@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
     "sg_ep_region_bytes", "sg_ep_layout", "sg_ep_alloc", "sg_ep_free", "sg_ep_ipc_handle", "sg_ep_ipc_open",
     "sg_ep_ipc_close", "sg_ep_send", "sg_ep_wait_inbox", "sg_ep_send_back", "sg_ep_wait_back",
+    "sg_ep_set_wait_limit",
 )
 
 
@@ -102,7 +103,8 @@ def load() -> ctypes.CDLL:
         "sg_ep_send": (I32, [P, I32, I32, I32, I32, P, P, I32, I32, I32, P, P]),
         "sg_ep_wait_inbox": (I32, [P, I32, I32, I32, P]),
         "sg_ep_send_back": (I32, [P, I32, I32, I32, I32, P, P]),
-        "sg_ep_wait_back": (I32, [P, I32, I32, I32, P]),
+        "sg_ep_wait_back": (I32, [P, I32, I32, I32, P, I32, I32, I32, P]),
+        "sg_ep_set_wait_limit": (I32, [ctypes.c_longlong]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

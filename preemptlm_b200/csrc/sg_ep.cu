@@ -16,6 +16,10 @@
 //   step              uint32 this rank's step counter (bumped by sg_ep_send;
 //                           every later call of the step reads it, so a
 //                           captured CUDA graph of the step replays correctly)
+//   done [2]          uint32 finished-CTA counters of this rank's sg_ep_send
+//                           and sg_ep_send_back (the last CTA publishes); one
+//                           pair per region, so exchanges of different layers
+//                           or groups never share a counter
 // CAP = max tokens per step x k, the most pairs one source can route to one
 // destination, so no inbox can overflow whatever the routing.
 //
@@ -34,6 +38,8 @@
 //   sg_ep_send_back: copy each output row to its source's ybuf at its pair
 //                    id; the last CTA raises flag_back[me] = seq there
 //   sg_ep_wait_back: acquire flag_back[d] >= seq for every destination d
+//                    (on expiry the ybuf rows of the pairs sent to d are
+//                    zeroed, so no earlier step's output is read as this one's)
 //   (sg_combine reads ybuf)
 // Buffer reuse across steps is safe by program order: a rank writes the next
 // step's rows into a peer's inbox only after it saw that peer's outputs of
@@ -41,10 +47,25 @@
 // into a source's ybuf only after the source's next-step rows arrived (so
 // the source's combine of the previous step is done).
 //
-// Every wait is bounded (about two seconds of clock64); on expiry the kernel
-// records SG_ERR_TIMEOUT (read with sg_device_status), empties the inboxes
-// it was waiting for and returns.  No TMA, no multicast: plain 16-byte peer
-// loads and stores.
+// Every wait is bounded (two seconds of the global timer by default,
+// sg_ep_set_wait_limit changes it per device); on expiry the kernel records
+// SG_ERR_TIMEOUT (read with sg_device_status), empties the inbox or zeroes the
+// output rows it was waiting for and returns.  After a timeout the exchange
+// is out of step (a late peer may still write into this rank's region): the
+// caller tears it down.  No TMA, no multicast: plain 16-byte peer loads and
+// stores.
+//
+// Memory ordering of a hand-over (PTX memory model): every thread's row
+// stores precede the CTA barrier; thread 0's fence.acq_rel.gpu (the
+// __threadfence) then orders them before its atomicAdd on the done counter,
+// so the CTA whose add returns gridDim.x - 1 observes, through that counter's
+// release sequence, every CTA's rows (causality order is transitive at GPU
+// scope).  Its fence.acq_rel.sys is cumulative: everything in its causal past,
+// the other CTAs' peer stores included, is ordered before its following
+// relaxed system-scope flag stores.  The receiver's ld.acquire.sys that reads
+// the flag value synchronises with that fence, so the rows are visible to
+// every later operation of the receiving thread, and the CTA barrier (or the
+// kernel boundary) after it passes them on to the rest of the receiver.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -54,14 +75,14 @@
 namespace sg {
 
 __device__ int g_ep_status = 0;
-__device__ unsigned int g_ep_send_done = 0;  // CTAs of sg_ep_send finished (last one publishes)
-__device__ unsigned int g_ep_back_done = 0;  // CTAs of sg_ep_send_back finished
+// wait limit of the exchange kernels on this device, in global-timer nanoseconds
+__device__ unsigned long long g_ep_wait_ns = 2000000000ull;
 
 constexpr int EP_MAX_RANKS = 8;
-constexpr long long EP_WAIT_CYCLES = 4000000000LL;  // ~2 s
+constexpr long long EP_MAX_WAIT_US = 600LL * 1000 * 1000;  // upper bound of sg_ep_set_wait_limit
 
 struct EpLayout {
-  size_t rows, eid, pid, cnt, ybuf, flag_in, flag_back, step, bytes;
+  size_t rows, eid, pid, cnt, ybuf, flag_in, flag_back, step, done, bytes;
 };
 
 static size_t ep_align(size_t v) { return (v + 255) & ~size_t(255); }
@@ -85,6 +106,8 @@ static EpLayout ep_layout(int R, int cap, int H) {
   o += ep_align((size_t)R * 4);
   l.step = o;
   o += 256;
+  l.done = o;
+  o += 256;
   l.bytes = o;
   return l;
 }
@@ -102,14 +125,20 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait for *flag >= seq (flags only grow); false on expiry.
 __device__ bool ep_wait_flag(const uint32_t* flag, uint32_t seq) {
   if (ld_acquire_sys(flag) >= seq) return true;
-  const long long t0 = clock64();
+  const unsigned long long t0 = global_ns(), limit = g_ep_wait_ns;
   while (true) {
     __nanosleep(256);
     if (ld_acquire_sys(flag) >= seq) return true;
-    if (clock64() - t0 > EP_WAIT_CYCLES) {
+    if (global_ns() - t0 > limit) {
       atomicCAS(&g_ep_status, 0, SG_ERR_TIMEOUT);
       return false;
     }
@@ -142,7 +171,8 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 __global__ void __launch_bounds__(256)
 ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, const uint16_t* __restrict__ x,
                const int32_t* __restrict__ inds, int32_t* __restrict__ dcnt, int P, size_t off_rows,
-               size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in, size_t off_step) {
+               size_t off_eid, size_t off_pid, size_t off_cnt, size_t off_flag_in, size_t off_step,
+               size_t off_done) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -172,8 +202,9 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
   // so the kernel pays for exactly one.
   __syncthreads();
   if (threadIdx.x == 0) {
+    unsigned int* done = reinterpret_cast<unsigned int*>(peers.base[me] + off_done);
     __threadfence();
-    const unsigned prev = atomicAdd(&g_ep_send_done, 1u);
+    const unsigned prev = atomicAdd(&done[0], 1u);
     if (prev == gridDim.x - 1) {  // every CTA's rows are out: publish
       __threadfence();
       for (int d = 0; d < R; ++d)  // the count, and the counter back to zero for the next step
@@ -183,7 +214,7 @@ ep_send_kernel(EpPeers peers, int me, int R, int cap, int H, int k, int per, con
       *step = seq;
       fence_acq_rel_sys();
       for (int d = 0; d < R; ++d) st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[d] + off_flag_in) + me, seq);
-      g_ep_send_done = 0;
+      done[0] = 0;  // read again only by the next launch (kernel boundary)
     }
   }
 }
@@ -211,7 +242,7 @@ ep_wait_inbox_kernel(uint8_t* __restrict__ region, int cap, size_t off_eid, size
 __global__ void __launch_bounds__(256)
 ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t* __restrict__ region,
                     const uint16_t* __restrict__ y, size_t off_pid, size_t off_cnt, size_t off_ybuf,
-                    size_t off_flag_back, size_t off_step) {
+                    size_t off_flag_back, size_t off_step, size_t off_done) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -229,24 +260,42 @@ ep_send_back_kernel(EpPeers peers, int me, int R, int cap, int H, const uint8_t*
   }
   __syncthreads();
   if (threadIdx.x == 0) {  // as in ep_send_kernel: one system fence, by the last CTA
+    unsigned int* done = reinterpret_cast<unsigned int*>(peers.base[me] + off_done);
     __threadfence();
-    const unsigned prev = atomicAdd(&g_ep_back_done, 1u);
+    const unsigned prev = atomicAdd(&done[1], 1u);
     if (prev == gridDim.x - 1) {
       __threadfence();
       fence_acq_rel_sys();
       const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
       for (int s = 0; s < R; ++s)
         st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.base[s] + off_flag_back) + me, seq);
-      g_ep_back_done = 0;
+      done[1] = 0;
     }
   }
 }
 
-// Thread d: wait until rank d's outputs of step seq are in ybuf.
-__global__ void ep_wait_back_kernel(const uint8_t* __restrict__ region, int R, size_t off_flag_back,
-                                    size_t off_step) {
-  const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
-  if (threadIdx.x < R) ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_back) + threadIdx.x, seq);
+// Block d: wait until rank d's outputs of step seq are in ybuf.  On expiry
+// the rows of this rank's pairs owned by d (inds[p] / per == d) are zeroed,
+// one warp per row, so the combine never reads an earlier step's outputs.
+__global__ void __launch_bounds__(256)
+ep_wait_back_kernel(uint8_t* __restrict__ region, int H, const int32_t* __restrict__ inds, int P, int per,
+                    size_t off_ybuf, size_t off_flag_back, size_t off_step) {
+  __shared__ int ok;
+  const int d = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const uint32_t seq = *reinterpret_cast<const uint32_t*>(region + off_step);
+    ok = ep_wait_flag(reinterpret_cast<const uint32_t*>(region + off_flag_back) + d, seq) ? 1 : 0;
+  }
+  __syncthreads();
+  if (ok) return;
+  const int lane = threadIdx.x & 31;
+  const int chunks = H >> 3;
+  for (int p = threadIdx.x >> 5; p < P; p += blockDim.x >> 5) {
+    const int e = inds[p];
+    if (e < 0 || e / per != d) continue;
+    uint4* row = reinterpret_cast<uint4*>(region + off_ybuf + (size_t)p * H * 2);
+    for (int c = lane; c < chunks; c += 32) row[c] = make_uint4(0, 0, 0, 0);
+  }
 }
 
 int ep_device_status(int reset) {
@@ -347,7 +396,8 @@ extern "C" int sg_ep_send(void* const* regions, int R, int me, int cap, int H, c
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   cudaStream_t s = (cudaStream_t)stream;
   sg::ep_send_kernel<<<sg::grid_for(P), 256, 0, s>>>(sg::peers_of(regions, R), me, R, cap, H, k, per, x, inds,
-                                                       dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, l.step);
+                                                       dcnt, P, l.rows, l.eid, l.pid, l.cnt, l.flag_in, l.step,
+                                                       l.done);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -373,19 +423,30 @@ extern "C" int sg_ep_send_back(void* const* regions, int R, int me, int cap, int
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
   sg::ep_send_back_kernel<<<sg::grid_for(R * cap), 256, 0, (cudaStream_t)stream>>>(
       sg::peers_of(regions, R), me, R, cap, H, static_cast<const uint8_t*>(regions[me]), y, l.pid, l.cnt, l.ybuf,
-      l.flag_back, l.step);
+      l.flag_back, l.step, l.done);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
 
-extern "C" int sg_ep_wait_back(void* region, int R, int cap, int H, void* stream) {
+extern "C" int sg_ep_wait_back(void* region, int R, int cap, int H, const int32_t* inds, int T, int k, int per,
+                               void* stream) {
   int st = sg::ep_check(R, 0, cap, H);
   if (st) return st;
-  if (!region) return SG_ERR_INVALID_ARG;
+  if (T < 0 || k < 1 || per < 1) return SG_ERR_INVALID_ARG;
+  const long long P = (long long)T * k;
+  if (P > cap) return SG_ERR_CAPACITY;
+  if (!region || (P > 0 && !inds)) return SG_ERR_INVALID_ARG;
   const sg::EpLayout l = sg::ep_layout(R, cap, H);
-  sg::ep_wait_back_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(static_cast<const uint8_t*>(region), R, l.flag_back,
-                                                               l.step);
+  sg::ep_wait_back_kernel<<<R, 256, 0, (cudaStream_t)stream>>>(static_cast<uint8_t*>(region), H, inds, (int)P, per,
+                                                                l.ybuf, l.flag_back, l.step);
   SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_ep_set_wait_limit(long long microseconds) {
+  if (microseconds < 1 || microseconds > sg::EP_MAX_WAIT_US) return SG_ERR_INVALID_ARG;
+  const unsigned long long ns = (unsigned long long)microseconds * 1000ull;
+  SG_CUDA_TRY(cudaMemcpyToSymbol(sg::g_ep_wait_ns, &ns, sizeof(ns)));
   return SG_OK;
 }
 

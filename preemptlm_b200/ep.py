@@ -1,6 +1,7 @@
 """Expert parallelism for the slotted MoE layer: one process per GPU, the
 experts of every layer split evenly across ranks, token dispatch and combine
-by NCCL all-to-all over NVLink.
+over NVLink -- by the library's own peer-memory exchange kernels on GPUs (the
+default), or by NCCL / gloo all-to-alls.
 
 Rank r of R owns experts [r*E/R, (r+1)*E/R) in its arena (slot = expert id -
 r*E/R); the router and the shared expert are replicated; every rank routes its
@@ -40,6 +41,17 @@ import torch.distributed as dist
 
 from . import _abi, ops
 from .arena import SlottedGLU
+
+
+class ExchangeTimeoutError(_abi.SlottedGLUError):
+    """A bounded wait of the peer-memory exchange expired (a peer did not
+    take part in the step in time)."""
+
+
+def set_wait_limit(seconds: float) -> None:
+    """Wait limit of the exchange kernels launched from now on, on the current
+    device (default 2 s)."""
+    _abi.call("sg_ep_set_wait_limit", int(round(seconds * 1e6)))
 
 
 @dataclass
@@ -234,6 +246,7 @@ class ExpertParallelMoE:
         self._graph = None
         self.graph_input = self.graph_output = None
         self._graph_launches = 0
+        self.broken = False  # set by check() after a timed-out exchange wait
 
     def capture(self, T: int, warmup: int = 2, seed: int = 0) -> None:
         """Record one peer-exchange step for T tokens in a CUDA graph, so that
@@ -266,11 +279,27 @@ class ExpertParallelMoE:
         """One captured step; ``x`` (if given) is first copied into the
         graph's input.  Returns the graph's output buffer, overwritten by
         the next replay."""
+        if self.broken:
+            raise ExchangeTimeoutError(_abi.SG_ERR_TIMEOUT, "expert-parallel exchange (timed out earlier; rebuild it)")
         if x is not None:
             self.graph_input.copy_(x, non_blocking=True)
         self._graph.replay()
         ops.LAUNCHES[0] += self._graph_launches
         return self.graph_output
+
+    def check(self) -> None:
+        """Read the device status word (synchronises): raise
+        ``ExchangeTimeoutError`` if a bounded wait of an exchange kernel gave
+        up since the last check.  The outputs of such a step had the late
+        rank's rows zeroed, and the exchange is out of step with its peers (a
+        late peer may still write into this rank's region), so it is marked
+        broken: later steps raise until it is closed and rebuilt.  Call it
+        between steps, outside timed regions and graph replays."""
+        st = ops.device_status(reset=True)
+        if st == _abi.SG_ERR_TIMEOUT:
+            self.broken = True
+            raise ExchangeTimeoutError(st, "expert-parallel exchange")
+        _abi.check(st, "expert-parallel step")
 
     def close(self) -> None:
         """Collective: release the captured graph and the peer-exchange
@@ -282,6 +311,8 @@ class ExpertParallelMoE:
             self.exchange = None
 
     def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        if self.broken:
+            raise ExchangeTimeoutError(_abi.SG_ERR_TIMEOUT, "expert-parallel exchange (timed out earlier; rebuild it)")
         ex, lib = self.exchange, self.exchange.lib
         T, H = x.shape
         k, R, per = self.top_k, self.world, self.shard.count
@@ -312,7 +343,8 @@ class ExpertParallelMoE:
         _abi.check(lib.sg_ep_send_back(ex.regions, R, self.rank, ex.cap, H, y_local.data_ptr(), stream),
                    "sg_ep_send_back")
         mark()
-        _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, stream), "sg_ep_wait_back")
+        _abi.check(lib.sg_ep_wait_back(ctypes.c_void_p(ex.region), R, ex.cap, H, inds.data_ptr(), T, k, per, stream),
+                   "sg_ep_wait_back")
         mark()
         ops.LAUNCHES[0] += 6
         out = self.backend.combine(ex.ybuf[: T * k], scores, shared_y, shared_gate)

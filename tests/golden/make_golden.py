@@ -2,7 +2,9 @@
 
 Run here (the reference tree must be importable):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference tree>
+
+(or set PREEMPTLM_REFERENCE to the reference tree and give no argument).
 
 What it pins, and how:
 
@@ -31,6 +33,7 @@ from __future__ import annotations
 
 import json
 import shutil
+import os
 import sys
 import types
 from pathlib import Path
@@ -327,7 +330,10 @@ def make_encoding_tags():
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    where = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PREEMPTLM_REFERENCE")
+    if not where:
+        raise SystemExit("usage: make_golden.py <reference tree>  (or set PREEMPTLM_REFERENCE)")
+    ref = Path(where)
     sys.path.insert(0, str(ref))
     _install_mlx_standin()
     make_admission()

@@ -81,13 +81,17 @@ def test_host_side_argument_checks(lib):
     assert lib.sg_ep_layout(2, 2560, 2048, off) == _abi.SG_OK
     rows = 2 * 2560 * 2048 * 2
     assert list(off) == [0, rows, rows + 2 * 2560 * 4, rows + 2 * 2 * 2560 * 4, rows + 2 * 2 * 2560 * 4 + 256]
-    assert lib.sg_ep_region_bytes(2, 2560, 2048) == off[4] + 2560 * 2048 * 2 + 2 * 256 + 256  # + step counter
+    assert lib.sg_ep_region_bytes(2, 2560, 2048) == off[4] + 2560 * 2048 * 2 + 2 * 256 + 256 + 256  # + step and done counters
     regs = (ctypes.c_void_p * 2)(1, 1)
     assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 4, 5, 8, 1, None) == _abi.SG_ERR_CAPACITY  # 20 > 16
     assert lib.sg_ep_send(regs, 2, 2, 16, 256, 1, 1, 2, 5, 8, 1, None) == _abi.SG_ERR_INVALID_ARG  # me
     assert lib.sg_ep_send(regs, 2, 0, 16, 256, 1, 1, 2, 5, 0, 1, None) == _abi.SG_ERR_INVALID_ARG  # per 0
     assert lib.sg_ep_wait_inbox(None, 2, 16, 256, None) == _abi.SG_ERR_INVALID_ARG
     assert lib.sg_ep_alloc(0, None) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_ep_set_wait_limit(0) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_ep_set_wait_limit(601 * 10**6) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_ep_wait_back(1, 2, 16, 256, 1, 5, 4, 8, None) == _abi.SG_ERR_CAPACITY  # 20 pairs > cap 16
+    assert lib.sg_ep_wait_back(1, 2, 16, 256, None, 2, 4, 8, None) == _abi.SG_ERR_INVALID_ARG
     a = _abi.sg_arena(num_slots=2, hidden=1024, inter=512, bits=8, group_size=64, gate_w=1, up_w=1, down_w=1,
                       gate_s=1, gate_b=1, up_s=1, up_b=1, down_s=1, down_b=1)
     assert lib.sg_dense_glu(ctypes.byref(a), 2, 1, 4, 1, 1, None) == _abi.SG_ERR_INVALID_ARG  # slot out of range

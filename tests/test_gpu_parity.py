@@ -201,8 +201,8 @@ def test_combine_matches_oracle(shared):
 # ----------------------------------------------------------------------------- whole layer
 
 @pytest.mark.parametrize("glu_path", ["auto", "tc"], indirect=True)
-@pytest.mark.parametrize("cfg_name,T", [("cfg1", 1), ("cfg1", 4), ("cfg2", 16), ("cfg2", 512), ("cfg3", 1),
-                                        ("cfg3", 8), ("cfg4", 2)])
+@pytest.mark.parametrize("cfg_name,T", [("cfg1", 1), ("cfg1", 4), ("cfg1", 16), ("cfg1", 32), ("cfg2", 16),
+                                        ("cfg2", 512), ("cfg3", 1), ("cfg3", 8), ("cfg3", 16), ("cfg4", 2)])
 def test_layer_matches_oracle(glu_path, cfg_name, T):
     cfg = CONFIGS[cfg_name]
     block, tens = make_layer(cfg, device=DEV)
@@ -220,30 +220,56 @@ def test_layer_matches_oracle(glu_path, cfg_name, T):
     assert torch.equal(res, out)
 
 
-@pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
-def test_layer_full_size_sampled_tokens_cfg3(glu_path):
-    """cfg3 at its largest decode batch (T=256): routing bit-exact for every
-    token, outputs checked on a sample of tokens."""
-    cfg = CONFIGS["cfg3"]
-    T = 256
+def _sampled_layer_check(cfg, T, n_sample, what):
+    """The whole layer at a benchmark size: router logits, top-k ids and scores
+    bit-exact for every token (and the dispatch of every pair against
+    np.unique), outputs of a seeded sample of tokens against the oracle (the
+    oracle's cost grows with the experts the sample touches, not with T)."""
     block, tens = make_layer(cfg, device=DEV)
     moe = Qwen3_xMoEWrapper(block, "fp", "l", 0)
     x = make_tokens(cfg, T)
     out = f32(moe.forward_resident(x))
     logits = orc.router_logits(bits16(x), bits16(tens["router"]))
-    inds, sc, _ = orc.get_routings(logits, cfg.top_k, True)
+    inds, sc, _ = orc.get_routings(logits, cfg.top_k, cfg.norm_topk_prob)
     dl = ops.router_linear(x, block.gate)
-    di, ds = ops.route_topk(dl, cfg.top_k, True)
-    assert np.array_equal(di.cpu().numpy(), inds) and np.array_equal(bits16(ds), sc)
-    sample = np.random.default_rng(0).choice(T, 6, replace=False)
+    assert np.array_equal(bits16(dl), logits), f"{what}: router logits"
+    di, ds = ops.route_topk(dl, cfg.top_k, cfg.norm_topk_prob)
+    assert np.array_equal(di.cpu().numpy(), inds), f"{what}: top-k ids"
+    assert np.array_equal(bits16(ds), sc), f"{what}: scores"
+    d = ops.dispatch(di, cfg.num_experts, torch.arange(cfg.num_experts, dtype=torch.int32, device=DEV))
+    uq, inv = np.unique(inds.reshape(-1), return_inverse=True)
+    assert int(d.counts[0].item()) == uq.size
+    assert np.array_equal(d.unique[: uq.size].cpu().numpy(), uq) and np.array_equal(d.inverse.cpu().numpy(), inv)
+    sample = np.sort(np.random.default_rng(T).choice(T, n_sample, replace=False))
     ex = LazyExperts(tens["experts"], cfg.bits)
-    sh = LazyExperts(tens["shared"], cfg.bits)[0]
-    sg = orc.bf16_bits_to_f32(orc.router_logits(bits16(x[sample]), bits16(tens["shared_gate"])))
     xs = f32(x)[sample]
     y = np.stack([np.stack([orc.expert_forward(xs[i: i + 1], ex[inds[t, j]])[0] for j in range(cfg.top_k)])
                   for i, t in enumerate(sample)])
-    ref = orc.combine_shared(y, orc.bf16_bits_to_f32(sc[sample]), orc.expert_forward(xs, sh), sg)
-    assert_close(out[sample], ref, what="cfg3 T=256 sampled")
+    sy = sg = None
+    if tens["shared"] is not None:
+        sy = orc.expert_forward(xs, LazyExperts(tens["shared"], cfg.bits)[0])
+        sg = orc.bf16_bits_to_f32(orc.router_logits(bits16(x[sample]), bits16(tens["shared_gate"])))
+    ref = orc.combine_shared(y, orc.bf16_bits_to_f32(sc[sample]), sy, sg)
+    assert_close(out[sample], ref, what=f"{what} sampled")
+    assert ops.device_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("glu_path", ["gemv", "tc"], indirect=True)
+def test_layer_full_size_sampled_tokens_cfg3(glu_path):
+    """cfg3 at its largest decode batch (T=256) on both GLU kernels."""
+    _sampled_layer_check(CONFIGS["cfg3"], 256, 6, f"cfg3 T=256 {glu_path}")
+
+
+@pytest.mark.parametrize("cfg_name,T,n_sample", [
+    ("cfg3", 32, 6), ("cfg3", 64, 6), ("cfg3", 128, 6),   # the decode sweep between 16 and 256
+    ("cfg2", 2048, 6), ("cfg2", 8192, 6),                  # prefill: 128-wide pair tiles, permuted rows
+    ("cfg4", 64, 3), ("cfg4", 4096, 3),                    # the 397B-style layer: decode and prefill
+])
+def test_layer_benchmark_sizes_sampled(cfg_name, T, n_sample):
+    """Every configuration at the sizes it is benchmarked at, on the
+    automatic kernel choice (the path the benchmark times)."""
+    ops.set_glu_path("auto")
+    _sampled_layer_check(CONFIGS[cfg_name], T, n_sample, f"{cfg_name} T={T}")
 
 
 def test_layer_ragged_and_empty():
