@@ -328,9 +328,22 @@ def _host_buffer(nbytes: int, pinned: bool) -> torch.Tensor:
     return torch.empty(nbytes, dtype=torch.uint8, pin_memory=pinned)
 
 
+DIRECT_IO_ALIGN = 4096  # file offset, length and buffer alignment of an O_DIRECT read
+
+
 class PreadExpertBank:
     """banks.py:130-206: positioned reads of ``experts.bin``.  ``read_sync``
-    fills a fresh host buffer; ``read_into`` fills a caller buffer."""
+    fills a fresh host buffer; ``read_into`` fills a caller buffer.
+
+    With ``bypass_page_cache`` (the reference opens the file F_NOCACHE on
+    darwin, banks.py:140-148) blobs are read with O_DIRECT where the file
+    system supports it: the blob offsets are 4096-aligned (writer.py:90-95),
+    the read length is rounded up to 4096 within the blob's zero padding and
+    the destination is a 4096-aligned slice of the host buffer, so the read
+    goes straight from the device into (pinned) memory.  Where O_DIRECT is
+    refused (tmpfs, for one) the read is buffered and its pages are dropped
+    from the page cache right after it, so a later miss on the same blob reads
+    the disk again instead of the page cache."""
 
     def __init__(self, expert_bank_path, bypass_page_cache: bool = False, pinned: bool | None = None):
         self.path = Path(expert_bank_path)
@@ -338,8 +351,22 @@ class PreadExpertBank:
         self._tensor_specs = self._manifest.tensor_specs
         self._pinned = torch.cuda.is_available() if pinned is None else pinned
         self._fd: int | None = os.open(self.path / EXPERTS_FILENAME, os.O_RDONLY)
-        if bypass_page_cache and hasattr(os, "posix_fadvise"):
-            os.posix_fadvise(self._fd, 0, 0, os.POSIX_FADV_DONTNEED)
+        self._dfd: int | None = None
+        self._drop_pages = False
+        if bypass_page_cache:
+            if hasattr(os, "O_DIRECT") and self._manifest.alignment % DIRECT_IO_ALIGN == 0:
+                try:
+                    self._dfd = os.open(self.path / EXPERTS_FILENAME, os.O_RDONLY | os.O_DIRECT)
+                except OSError:
+                    self._dfd = None
+            self._drop_pages = self._dfd is None and hasattr(os, "posix_fadvise")
+            if hasattr(os, "posix_fadvise"):
+                os.posix_fadvise(self._fd, 0, 0, os.POSIX_FADV_DONTNEED)
+
+    @property
+    def direct_io(self) -> bool:
+        """Whether blob reads bypass the page cache by O_DIRECT."""
+        return self._dfd is not None
 
     @property
     def manifest(self) -> ExpertBankManifest:
@@ -358,21 +385,44 @@ class PreadExpertBank:
             raise RuntimeError("Cannot read closed expert bank.")
         return self._fd
 
+    def _direct_span(self, blob) -> int:
+        """Bytes an O_DIRECT read of ``blob`` covers (0: read it buffered)."""
+        if self._dfd is None or blob.offset % DIRECT_IO_ALIGN:
+            return 0
+        return (blob.length + DIRECT_IO_ALIGN - 1) // DIRECT_IO_ALIGN * DIRECT_IO_ALIGN
+
     def read_into(self, expert_idx: int, buf: torch.Tensor) -> SerializedExpert:
         fd = self._validate_fd()
         if not 0 <= expert_idx < len(self.blob_index):
             raise KeyError(expert_idx)
         blob = self.blob_index[expert_idx]
+        span = self._direct_span(blob)
+        if span and buf.numel() >= span and buf.data_ptr() % DIRECT_IO_ALIGN == 0:
+            view = memoryview(buf.numpy()).cast("B")[:span]
+            try:
+                got = os.preadv(self._dfd, [view], blob.offset)  # may stop at end of file inside the padding
+            except OSError:  # the device refused this direct read: read it buffered
+                got = -1
+            if got >= blob.length:
+                return SerializedExpert(expert_idx, buf[: blob.length], self._manifest.encoding, self._tensor_specs)
         view = memoryview(buf.numpy()).cast("B")[: blob.length]
         got = os.preadv(fd, [view], blob.offset)
         if got != blob.length:
             raise IOError(f"short read of expert {expert_idx}: {got} of {blob.length} bytes")
+        if self._drop_pages:
+            os.posix_fadvise(fd, blob.offset, blob.length, os.POSIX_FADV_DONTNEED)
         return SerializedExpert(expert_idx, buf[: blob.length], self._manifest.encoding, self._tensor_specs)
 
     def read_sync(self, expert_idx: int, priority: int = ReadPriority.DEMAND) -> SerializedExpert:
         if not 0 <= expert_idx < len(self.blob_index):
             raise KeyError(expert_idx)
-        return self.read_into(expert_idx, _host_buffer(self.blob_index[expert_idx].length, self._pinned))
+        blob = self.blob_index[expert_idx]
+        span = self._direct_span(blob)
+        if span:  # a 4096-aligned slice of a slightly larger buffer
+            raw = _host_buffer(span + DIRECT_IO_ALIGN, self._pinned)
+            off = (-raw.data_ptr()) % DIRECT_IO_ALIGN
+            return self.read_into(expert_idx, raw[off: off + span])
+        return self.read_into(expert_idx, _host_buffer(blob.length, self._pinned))
 
     def check_model_compatibility(self, model_id: str, num_routed_experts: int, top_k: int,
                                   moe_block_idxs: tuple[int, ...]) -> None:
@@ -386,6 +436,9 @@ class PreadExpertBank:
             raise ValueError(f"expert bank incompatible with model: {bad!r}")
 
     def close(self) -> None:
+        if self._dfd is not None:
+            os.close(self._dfd)
+            self._dfd = None
         if self._fd is not None:
             os.close(self._fd)
             self._fd = None

@@ -28,7 +28,7 @@ from typing import Callable
 import numpy as np
 import torch
 
-from . import ops
+from . import _abi, ops
 from .arena import SlottedGLU
 from .quant import QuantSettings
 from .slot_map import EMPTY, SlotTable
@@ -111,7 +111,7 @@ class Qwen3_xMoEWrapper(SlotTable):
     def __init__(self, inner: SparseMoeBlock, model_fingerprint: str | None, layer_path: str, block_idx: int,
                  recorder=None, capture_gate_logits: bool = False, expert_loader=None, expert_cache=None,
                  num_slots: int = 0, slot_size: int = 0, slot_policy: str = "reference",
-                 device: str | torch.device | None = None):
+                 device: str | torch.device | None = None, prefetch_experts: int = 0):
         # base_moe_wrapper.py:84-87
         if expert_loader is not None and any(v is None for v in (expert_cache, num_slots, slot_size)):
             raise ValueError("expert_loader requires expert_cache, num_slots and slot_size")
@@ -131,6 +131,12 @@ class Qwen3_xMoEWrapper(SlotTable):
         self._copy_stream: torch.cuda.Stream | None = None  # slot refills, overlapped with compute
         self._refill_event: torch.cuda.Event | None = None  # the last step's refills, for the GLU to wait on
         self.admit_stats = {"steps": 0, "unique": 0, "missed": 0}  # streaming: routed experts seen / refilled
+        # streaming: after each step, queue PREFETCH reads of this many of the
+        # most often routed experts that are neither in a slot nor in the host
+        # blob cache (a frequency predictor; the reference has the hook,
+        # loader.py:286-310, but no caller)
+        self.prefetch_experts = int(prefetch_experts)
+        self._routed_freq = np.zeros(inner.num_experts, np.int64)
         self._side_stream: torch.cuda.Stream | None = None  # the shared expert, beside the routed path
         self._weight_slots: SlottedGLU | None = None
         if expert_loader is not None or expert_cache is not None:
@@ -164,9 +170,15 @@ class Qwen3_xMoEWrapper(SlotTable):
     def _release_finished(self) -> None:
         self._pending = [(ev, keep) for ev, keep in self._pending if not ev.query()]
 
-    def _maybe_admit(self, routed_eids: torch.Tensor):
+    def _maybe_admit(self, routed_eids: torch.Tensor, on_miss=None):
         """qwen3_x_moe.py:136-208.  Returns (unique eids on host, inverse_map
-        on device, the step's Dispatch with resolved slot ids)."""
+        on device, the step's Dispatch with resolved slot ids).
+
+        ``on_miss(d)``, when given, is called once the step is known to miss
+        and before any blob is read, with the step's Dispatch (missed experts
+        have slot id -1 there): work queued by it runs on the GPU while the
+        host reads the missed blobs, and the slot refills do not wait for it
+        (they wait only for the compute stream's work queued before it)."""
         assert self.expert_loader is not None and self._weight_slots is not None
         self._release_finished()
         d = ops.dispatch(routed_eids, self.num_experts, self.eid2sid_device)
@@ -186,6 +198,11 @@ class Qwen3_xMoEWrapper(SlotTable):
             return unique, d.inverse, d
         missed = unique[self._eid_lookup_table[unique] < 0]
         glob_eids = self.block_idx * self.num_experts + missed
+        compute = torch.cuda.current_stream(self._device)
+        before = torch.cuda.Event()
+        before.record(compute)  # earlier steps' reads of the slots about to be replaced are queued before this
+        if on_miss is not None:
+            on_miss(d)
         acquired = self._choose_slots(missed.size, protected=unique)
         old = self._sid_lookup_table[acquired]
         evicted = old[old >= 0]
@@ -194,12 +211,12 @@ class Qwen3_xMoEWrapper(SlotTable):
         blobs = self.expert_loader.load_sync(glob_eids.tolist())
         # refills run on a side stream: they start once earlier work on the
         # compute stream (the previous steps' reads of the replaced slots) is
-        # done, and the shared expert runs meanwhile; the GLU waits on them
-        compute = torch.cuda.current_stream(self._device)
+        # done, while the GLU over the resident experts and the shared expert
+        # run; the GLU over the missed experts waits on them
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(self._device)
         copy = self._copy_stream
-        copy.wait_stream(compute)
+        copy.wait_event(before)
         for eid, sid, payload in zip(missed, acquired, blobs):
             self._weight_slots.refill_from_blob(int(sid), payload.as_tensor(), copy)
             self._eid_lookup_table[eid] = sid
@@ -211,6 +228,24 @@ class Qwen3_xMoEWrapper(SlotTable):
         self.sync_device()
         d.slot_ids[:n_unique] = self.eid2sid_device[d.unique[:n_unique].long()]
         return unique, d.inverse, d
+
+    def _prefetch_predicted(self) -> None:
+        """Queue PREFETCH reads (loader.enqueue_prefetch, never blocking) of
+        the most often routed experts that are in no slot and not cached on
+        the host yet, so that a later miss on them costs only the copy."""
+        cand = np.argsort(-self._routed_freq, kind="stable")
+        cand = cand[self._eid_lookup_table[cand] < 0]
+        cache = self.expert_cache
+        picks = []
+        for e in cand:
+            g = self.block_idx * self.num_experts + int(e)
+            if cache is not None and g in cache:
+                continue
+            picks.append(g)
+            if len(picks) == self.prefetch_experts:
+                break
+        if picks:
+            self.expert_loader.enqueue_prefetch(picks, await_free_slot=False)
 
     # ------------------------------------------------------------------ forward
     def _shared_begin(self, x2: torch.Tensor):
@@ -270,8 +305,17 @@ class Qwen3_xMoEWrapper(SlotTable):
         logits = ops.router_linear(x2, self.inner.gate)
         inds, scores = _get_routings(logits, self.inner.top_k, self.inner.norm_topk_prob)
         admitted = None
+        early: dict = {}
         if self.expert_cache is not None:
-            admitted = self._maybe_admit(inds)  # slot refills start on the side stream
+            flat = inds.reshape(-1)
+
+            def start_resident(d):
+                # missed experts have slot -1 in d: the GLU skips their pairs
+                # (zero rows, rewritten below) and runs the rest now
+                early["missed_ids"] = torch.where(self.eid2sid_device[flat.long()] < 0, flat, torch.full_like(flat, -1))
+                early["y"] = self._gather_forward_dispatched(x2, d, self._weight_slots)
+
+            admitted = self._maybe_admit(inds, on_miss=start_resident)  # slot refills start on the side stream
         pending = self._shared_begin(x2)
         if self.should_capture_traces:
             self.recorder.capture(layer_path=self.layer_path, layer_class="Qwen3NextSparseMoeBlock",
@@ -283,11 +327,21 @@ class Qwen3_xMoEWrapper(SlotTable):
         else:
             unique, _inverse, d = admitted
             slot_ids = self._eid_lookup_table[unique]
-            if self._refill_event is not None:
+            if early:
+                # the resident experts' pairs already ran; now the missed
+                # experts' pairs, once their slots are refilled
+                y = early["y"]
                 torch.cuda.current_stream(self._device).wait_event(self._refill_event)
                 self._refill_event = None
-            y = self._gather_forward_dispatched(x2, d, self._weight_slots)
+                dm = ops.dispatch(early["missed_ids"], self.num_experts, self.eid2sid_device)
+                h = ops.glu_gate_up(self._weight_slots, x2, dm, self.inner.top_k, _abi.SG_OUT_DISPATCH_ORDER)
+                ops.glu_down(self._weight_slots, h, dm, _abi.SG_IN_DISPATCH_ORDER, out=y)
+            else:
+                y = self._gather_forward_dispatched(x2, d, self._weight_slots)
             self._touch(slot_ids)
+            self._routed_freq[unique] += 1
+            if self.prefetch_experts > 0:
+                self._prefetch_predicted()
         shared_y, shared_gate = self._shared_end(pending)
         out = _combine_shared(y.reshape(B * S, self.inner.top_k, H), scores, shared_y, shared_gate)
         return out.reshape(B, S, H)
@@ -352,7 +406,7 @@ class Qwen3_xMoEWrapper(SlotTable):
     @staticmethod
     def make_wrapper_factory(*, model_fingerprint: str | None = None, recorder=None, capture_gate_logits: bool = False,
                              expert_loader=None, expert_cache=None, num_slots: int = 0, slot_size: int = 0,
-                             slot_policy: str = "reference") -> Callable:
+                             slot_policy: str = "reference", prefetch_experts: int = 0) -> Callable:
         """qwen3_x_moe.py:299-337.  ``candidate`` needs ``layer_path`` and
         ``block_idx`` attributes (LayerCandidate)."""
 
@@ -364,7 +418,7 @@ class Qwen3_xMoEWrapper(SlotTable):
                 )
             return Qwen3_xMoEWrapper(module, model_fingerprint, candidate.layer_path, candidate.block_idx,
                                      recorder, capture_gate_logits, expert_loader, expert_cache, num_slots,
-                                     slot_size, slot_policy=slot_policy)
+                                     slot_size, slot_policy=slot_policy, prefetch_experts=prefetch_experts)
 
         return factory
 

@@ -136,11 +136,17 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int =
     return h
 
 
-def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0) -> torch.Tensor:
-    """y = h @ down^T over the arena (``sg_glu_down``)."""
+def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = h @ down^T over the arena (``sg_glu_down``); into ``out`` when
+    given (only the rows of the dispatch's pairs are written)."""
     h = _bf16_2d(h, "h")
     P = d.perm.numel()
-    y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=h.device)
+    if out is not None:
+        if out.dtype != torch.bfloat16 or not out.is_contiguous() or tuple(out.shape) != (P, arena.hidden):
+            raise TypeError(f"out must be a contiguous bf16 [{P}, {arena.hidden}] tensor")
+        y = out
+    else:
+        y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=h.device)
     if P == 0:
         return y
     LAUNCHES[0] += 1

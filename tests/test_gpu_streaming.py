@@ -39,8 +39,15 @@ def _write_bank(path, cfg, tens, arena):
     return specs
 
 
-@pytest.mark.parametrize("bits,policy", [(8, "lfru"), (4, "lfru"), (16, "lfru")])
-def test_streaming_layer_matches_oracle(tmp_path, bits, policy):
+@pytest.mark.parametrize("bits,policy,path,prefetch", [(8, "lfru", "auto", 0), (4, "lfru", "auto", 0),
+                                                       (16, "lfru", "auto", 0), (8, "lfru", "tc", 4),
+                                                       (4, "lfru", "gemv", 4)])
+def test_streaming_layer_matches_oracle(tmp_path, bits, policy, path, prefetch):
+    """Steps that miss run the resident experts' pairs first (missed experts
+    skipped), read and refill the missed ones meanwhile, then run the missed
+    pairs into the same output rows; with ``prefetch`` the layer also queues
+    PREFETCH reads of its most often routed non-resident experts."""
+    ops.set_glu_path(path)
     cfg = LayerConfig("stream", 7, 512, 32, 4, 128, 128, bits, 12)
     block, tens = make_layer(cfg, device=DEV)
     _write_bank(tmp_path / "bank", cfg, tens, block.switch_mlp)
@@ -50,7 +57,7 @@ def test_streaming_layer_matches_oracle(tmp_path, bits, policy):
     try:
         factory = Qwen3_xMoEWrapper.make_wrapper_factory(
             model_fingerprint="fp", expert_loader=loader, expert_cache=cache, num_slots=cfg.num_slots,
-            slot_size=bank.manifest.expert_num_bytes(), slot_policy=policy)
+            slot_size=bank.manifest.expert_num_bytes(), slot_policy=policy, prefetch_experts=prefetch)
 
         class Cand:
             layer_path, block_idx = "model.layers.0.mlp", 0
@@ -73,7 +80,9 @@ def test_streaming_layer_matches_oracle(tmp_path, bits, policy):
             assert np.array_equal(moe.eid2sid_device.cpu().numpy(), eid2sid)
             seen.update(int(e) for e in np.unique(ref["inds"]))
         assert len(seen) > cfg.num_slots  # the run had to evict
+        assert moe.admit_stats["missed"] > 0
         assert ops.device_status(reset=True) == 0
     finally:
+        ops.set_glu_path("auto")
         loader.close()
         bank.close()
