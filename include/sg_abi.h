@@ -105,6 +105,26 @@ int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
                 int32_t* slot_ids, int32_t* miss_eids, int32_t* group_off,
                 int32_t* perm, int max_unique, void* stream);
 
+/* ------------------------------------------- fused routing + dispatch (a2/a3/a6)
+ * sg_route_topk followed by sg_dispatch in one launch: softmax, top-k in the
+ * order (gate desc, expert id asc) and renormalisation per token (one warp
+ * per token), then the unique experts, inverse map, slot lookup, miss list,
+ * group offsets and pair permutation, all with the outputs and meaning of
+ * those two calls (inds/scores [T, k]; the sg_dispatch arrays for the
+ * P = T * k pairs; the order of pairs inside a group is not specified).
+ * work: caller-provided int32 [E + 1], all zero before the first call; every
+ * call leaves it zero (calls using one work buffer must not overlap).
+ * Replaces `_get_routings` (qwen3_x_moe.py:26-40), the host np.unique and
+ * miss set of `_maybe_admit` (:145-156) and `slot_ids =
+ * self._eid_lookup_table[unique_eids]` (:277).
+ * Requires E % 32 == 0, E <= 1024, 1 <= k <= 32, k <= E; max_unique >=
+ * min(P, E) + 1. */
+int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, int norm_topk_prob,
+                      const int32_t* eid2sid, int32_t* inds, uint16_t* scores,
+                      int32_t* unique, int32_t* inverse, int32_t* counts, int32_t* slot_ids,
+                      int32_t* miss_eids, int32_t* group_off, int32_t* perm, int max_unique,
+                      int32_t* work, void* stream);
+
 /* ------------------------------------------------- gathered SwiGLU (a9/a10)
  * y[p, H] = bf16(swiglu(x[p / pair_div] @ gate^T, ... @ up^T) @ down^T) for
  * every pair p of every group u < counts[0], against arena slot slot_ids[u];
@@ -174,10 +194,11 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
                  void* stream);
 
 /* Kernel choice for sg_glu_forward / sg_glu_gate_up / sg_glu_down: 0 =
- * automatic (tcgen05 when the mean pairs per group is >= 2 and the shape
- * allows: in-dim % 64, out-dim % 128, <= 2048 groups; token rows permuted
- * once the mean reaches 32), 1 = streaming GEMV always, 2 = tcgen05 whenever
- * the shape allows, 3 = as 2 with the token rows always permuted.
+ * automatic (tcgen05 when the shape allows -- in-dim % 64, out-dim % 128,
+ * <= 2048 groups -- and either the mean pairs per group is >= 2 or the
+ * groups make at least one 128-row tile per SM; token rows permuted once the
+ * mean reaches 32), 1 = streaming GEMV always, 2 = tcgen05 whenever the shape
+ * allows, 3 = as 2 with the token rows always permuted.
  * Process-wide.  No counterpart in the reference (MLX picks
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);

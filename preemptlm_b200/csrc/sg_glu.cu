@@ -270,11 +270,28 @@ int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, 
                     cudaStream_t s);
 static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05, 3 tcgen05 over permuted rows
 
-// auto: the tensor-core path once the mean pairs per group reaches 2
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// auto: the tensor-core path once the mean pairs per group reaches 2, or once
+// the groups give at least one tile per SM (a tile streams 128 weight rows
+// at the HBM rate whatever its pair count, so it beats the CUDA-core GEMV
+// from one pair per group on); the GEMV serves the few-expert steps whose
+// tiles would leave most SMs idle.
 static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || !tc_supported(A, dual, grid_groups)) return false;
   if (g_glu_path >= 2) return true;
-  return P >= 2 * grid_groups;
+  const int out = dual ? A->inter : A->hidden;
+  const long long tiles = (long long)grid_groups * (out / 128);
+  return P >= 2 * grid_groups || tiles >= sm_count();
 }
 
 // Whether sg_glu_forward first copies the pairs' token rows into dispatch

@@ -290,6 +290,138 @@ dispatch_kernel(const int32_t* __restrict__ inds, int P, int E, const int32_t* _
   }
 }
 
+// ============================================================== fused routing + dispatch
+// One launch for softmax / top-k / renormalisation, the expert -> slot lookup
+// and the pair permutation.  Phase 1, every CTA: one warp per token, exactly
+// the arithmetic of route_topk_kernel; lane j < k also takes the pair's
+// position inside its expert's group (an atomicAdd on work[e], the count of
+// pairs routed to e so far) and parks it in inverse[p].  Phase 2, the last
+// CTA to finish (a ticket in work[E]): a block scan over the per-expert
+// counts gives the unique experts in ascending order, their slots, the missed
+// ones and the group offsets; every pair then lands at
+// perm[group_off[u] + position] and inverse[p] becomes u.  The last CTA
+// leaves work[] zero for the next call.
+//
+// Hand-over: each CTA's pair writes and count atomics precede a GPU-scope
+// fence and its ticket atomic; the CTA that draws the last ticket fences again
+// and reads the counts, ids and positions through L2 (ld.global.cg), so it
+// sees every CTA's writes.
+constexpr int RD_WARPS = 32;  // 1024 threads: phase 2 runs on one CTA
+constexpr int RD_MAX_E = 1024;
+
+template <int C>
+__global__ void __launch_bounds__(RD_WARPS * 32)
+route_dispatch_kernel(const uint16_t* __restrict__ logits, int T, int E, int k, int norm,
+                      const int32_t* __restrict__ eid2sid, int32_t* inds, uint16_t* __restrict__ scores,
+                      int32_t* __restrict__ unique, int32_t* inverse, int32_t* __restrict__ counts,
+                      int32_t* __restrict__ slot_ids, int32_t* __restrict__ miss_eids,
+                      int32_t* __restrict__ group_off, int32_t* __restrict__ perm, int32_t* work) {
+  __shared__ int s_rank[RD_MAX_E];  // unique index of expert e (phase 2)
+  __shared__ int s_base[RD_MAX_E];  // first permutation position of expert e's group
+  __shared__ int warp_tot[32];
+  __shared__ int tot_a, tot_b, tot_c, s_last;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * RD_WARPS + (threadIdx.x >> 5);
+  if (t < T) {
+    const uint16_t* row = logits + (size_t)t * E;
+    float v[C];
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      v[c] = bf16_to_f32(row[c * 32 + lane]);
+      m = fmaxf(m, v[c]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      v[c] = routing_exp(__fsub_rn(v[c], m));
+      s = __fadd_rn(s, v[c]);
+    }
+    s = warp_fold_sum(s);
+    uint32_t key[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      uint32_t g = f32_to_bf16(__fdiv_rn(v[c], s));
+      key[c] = (g << 16) | (0xFFFFu - static_cast<uint32_t>(c * 32 + lane));
+    }
+    float ssum = 0.0f;
+    uint32_t my_key = 0;
+    for (int j = 0; j < k; ++j) {
+      uint32_t best = 0;
+#pragma unroll
+      for (int c = 0; c < C; ++c) best = key[c] > best ? key[c] : best;
+      best = __reduce_max_sync(0xffffffffu, best);
+      const int e = static_cast<int>(0xFFFFu - (best & 0xFFFFu));
+      if ((e & 31) == lane) {
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+          if (c == (e >> 5)) key[c] = 0;
+      }
+      if (lane == j) my_key = best;
+      ssum = __fadd_rn(ssum, bf16_to_f32(static_cast<uint16_t>(best >> 16)));
+    }
+    if (lane < k) {
+      const int e = static_cast<int>(0xFFFFu - (my_key & 0xFFFFu));
+      float sc = bf16_to_f32(static_cast<uint16_t>(my_key >> 16));
+      if (norm) sc = __fdiv_rn(sc, round_bf16(ssum));
+      const size_t p = (size_t)t * k + lane;
+      inds[p] = e;
+      scores[p] = f32_to_bf16(sc);
+      inverse[p] = atomicAdd(&work[e], 1);  // position inside the group of e
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&work[E], 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // ---- phase 2, the last CTA: unique / slots / misses / group offsets
+  const int P = T * k;
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int e_lo = min(E, (int)threadIdx.x * per), e_hi = min(E, e_lo + per);
+  int n_present = 0, n_pairs = 0, n_miss = 0;
+  for (int e = e_lo; e < e_hi; ++e) {
+    const int c = __ldcg(work + e);
+    if (c > 0) {
+      ++n_present;
+      n_pairs += c;
+      if (eid2sid[e] < 0) ++n_miss;
+    }
+  }
+  int base_u = block_excl_scan(n_present, warp_tot, &tot_a);
+  int base_p = block_excl_scan(n_pairs, warp_tot, &tot_b);
+  int base_m = block_excl_scan(n_miss, warp_tot, &tot_c);
+  for (int e = e_lo; e < e_hi; ++e) {
+    const int c = __ldcg(work + e);
+    if (c > 0) {
+      const int sid = eid2sid[e];
+      unique[base_u] = e;
+      slot_ids[base_u] = sid;
+      group_off[base_u] = base_p;
+      if (sid < 0) miss_eids[base_m++] = e;
+      s_rank[e] = base_u++;
+      s_base[e] = base_p;
+      base_p += c;
+    }
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = tot_a;
+    counts[1] = tot_c;
+    group_off[tot_a] = tot_b;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = __ldcg(inds + p);
+    perm[s_base[e] + __ldcg(inverse + p)] = p;
+    inverse[p] = s_rank[e];
+  }
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) work[e] = 0;  // ready for the next call
+}
+
 }  // namespace sg
 
 // ============================================================== C-ABI
@@ -343,6 +475,45 @@ extern "C" int sg_route_topk(const uint16_t* logits, int T, int E, int k, int no
     default: return SG_ERR_SHAPE;
   }
 #undef SG_ROUTE_CASE
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, int norm_topk_prob,
+                                 const int32_t* eid2sid, int32_t* inds, uint16_t* scores, int32_t* unique,
+                                 int32_t* inverse, int32_t* counts, int32_t* slot_ids, int32_t* miss_eids,
+                                 int32_t* group_off, int32_t* perm, int max_unique, int32_t* work, void* stream) {
+  if (T < 0) return SG_ERR_INVALID_ARG;
+  if (E % 32 != 0 || E < 32 || E > sg::RD_MAX_E || k < 1 || k > 32 || k > E) return SG_ERR_SHAPE;
+  if (!eid2sid || !unique || !counts || !slot_ids || !miss_eids || !group_off || !work) return SG_ERR_INVALID_ARG;
+  const long long P = (long long)T * k;
+  if (P > 0x7FFFFFFFLL) return SG_ERR_SHAPE;
+  if (max_unique < (P < E ? (int)P : E) + 1) return SG_ERR_CAPACITY;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T == 0) {  // no pairs: an empty dispatch (counts and group_off[0] written)
+    SG_CUDA_TRY(cudaMemsetAsync(counts, 0, 2 * sizeof(int32_t), s));
+    SG_CUDA_TRY(cudaMemsetAsync(group_off, 0, sizeof(int32_t), s));
+    return SG_OK;
+  }
+  if (!logits || !inds || !scores || !inverse || !perm) return SG_ERR_INVALID_ARG;
+  dim3 grid((T + sg::RD_WARPS - 1) / sg::RD_WARPS);
+  const int C = E / 32;
+#define SG_RD_CASE(CC)                                                                                      \
+  case CC:                                                                                                  \
+    sg::route_dispatch_kernel<CC><<<grid, sg::RD_WARPS * 32, 0, s>>>(logits, T, E, k, norm_topk_prob,       \
+                                                                     eid2sid, inds, scores, unique, inverse, \
+                                                                     counts, slot_ids, miss_eids, group_off, \
+                                                                     perm, work);                            \
+    break;
+  switch (C) {
+    SG_RD_CASE(1) SG_RD_CASE(2) SG_RD_CASE(3) SG_RD_CASE(4) SG_RD_CASE(5) SG_RD_CASE(6) SG_RD_CASE(7)
+    SG_RD_CASE(8) SG_RD_CASE(9) SG_RD_CASE(10) SG_RD_CASE(11) SG_RD_CASE(12) SG_RD_CASE(13) SG_RD_CASE(14)
+    SG_RD_CASE(15) SG_RD_CASE(16) SG_RD_CASE(17) SG_RD_CASE(18) SG_RD_CASE(19) SG_RD_CASE(20)
+    SG_RD_CASE(21) SG_RD_CASE(22) SG_RD_CASE(23) SG_RD_CASE(24) SG_RD_CASE(25) SG_RD_CASE(26)
+    SG_RD_CASE(27) SG_RD_CASE(28) SG_RD_CASE(29) SG_RD_CASE(30) SG_RD_CASE(31) SG_RD_CASE(32)
+    default: return SG_ERR_SHAPE;
+  }
+#undef SG_RD_CASE
   SG_LAUNCH_CHECK();
   return SG_OK;
 }

@@ -143,6 +143,8 @@ class Qwen3_xMoEWrapper(SlotTable):
             H, I = inner.hidden_size, inner.moe_intermediate_size
             self._weight_slots = SlottedGLU(self.num_slots, (I, H), (H, I), torch.bfloat16, quant=inner.quant,
                                             device=device)
+        # zero int32 [E + 1] buffer of the fused routing + dispatch kernel (left zero by every call)
+        self._route_work = torch.zeros(inner.num_experts + 1, dtype=torch.int32, device=device)
         self._identity = None
         if expert_cache is None:
             if inner.switch_mlp is None:
@@ -170,7 +172,7 @@ class Qwen3_xMoEWrapper(SlotTable):
     def _release_finished(self) -> None:
         self._pending = [(ev, keep) for ev, keep in self._pending if not ev.query()]
 
-    def _maybe_admit(self, routed_eids: torch.Tensor, on_miss=None):
+    def _maybe_admit(self, routed_eids: torch.Tensor, on_miss=None, dispatch: ops.Dispatch | None = None):
         """qwen3_x_moe.py:136-208.  Returns (unique eids on host, inverse_map
         on device, the step's Dispatch with resolved slot ids).
 
@@ -178,10 +180,12 @@ class Qwen3_xMoEWrapper(SlotTable):
         and before any blob is read, with the step's Dispatch (missed experts
         have slot id -1 there): work queued by it runs on the GPU while the
         host reads the missed blobs, and the slot refills do not wait for it
-        (they wait only for the compute stream's work queued before it)."""
+        (they wait only for the compute stream's work queued before it).
+        ``dispatch``: the step's dispatch when the routing kernel already
+        built it against the current slot table."""
         assert self.expert_loader is not None and self._weight_slots is not None
         self._release_finished()
-        d = ops.dispatch(routed_eids, self.num_experts, self.eid2sid_device)
+        d = dispatch if dispatch is not None else ops.dispatch(routed_eids, self.num_experts, self.eid2sid_device)
         counts = d.counts.cpu()  # the one host read of a hit-only step
         n_unique, n_missed = int(counts[0]), int(counts[1])
         self.admit_stats["steps"] += 1
@@ -303,7 +307,12 @@ class Qwen3_xMoEWrapper(SlotTable):
         B, S, H = x.shape
         x2 = x.reshape(B * S, H).contiguous()
         logits = ops.router_linear(x2, self.inner.gate)
-        inds, scores = _get_routings(logits, self.inner.top_k, self.inner.norm_topk_prob)
+        # softmax / top-k / renorm fused with the slot lookup and the pair
+        # permutation (sg_route_dispatch; _get_routings + the np.unique of
+        # _maybe_admit + the slot lookup of qwen3_x_moe.py:277)
+        table = self._identity if self.expert_cache is None else self.eid2sid_device
+        inds, scores, d_step = ops.route_dispatch(logits, self.inner.top_k, self.inner.norm_topk_prob, table,
+                                                  self._route_work)
         admitted = None
         early: dict = {}
         if self.expert_cache is not None:
@@ -315,15 +324,15 @@ class Qwen3_xMoEWrapper(SlotTable):
                 early["missed_ids"] = torch.where(self.eid2sid_device[flat.long()] < 0, flat, torch.full_like(flat, -1))
                 early["y"] = self._gather_forward_dispatched(x2, d, self._weight_slots)
 
-            admitted = self._maybe_admit(inds, on_miss=start_resident)  # slot refills start on the side stream
+            admitted = self._maybe_admit(inds, on_miss=start_resident, dispatch=d_step)  # refills on the side stream
         pending = self._shared_begin(x2)
         if self.should_capture_traces:
             self.recorder.capture(layer_path=self.layer_path, layer_class="Qwen3NextSparseMoeBlock",
-                                  block_idx=self.block_idx, expert_ids=inds, softmax_weights=scores,
+                                  block_idx=self.block_idx, expert_ids=inds.reshape(B, S, -1),
+                                  softmax_weights=scores.reshape(B, S, -1),
                                   gate_logits=logits if self._capture_gate_logits else None)
         if self.expert_cache is None:
-            d = ops.dispatch(inds, self.num_experts, self._identity)
-            y = self._gather_forward_dispatched(x2, d, self.inner.switch_mlp)
+            y = self._gather_forward_dispatched(x2, d_step, self.inner.switch_mlp)
         else:
             unique, _inverse, d = admitted
             slot_ids = self._eid_lookup_table[unique]
@@ -395,8 +404,8 @@ class Qwen3_xMoEWrapper(SlotTable):
             raise RuntimeError("forward_resident needs the non-streaming (all-resident) wrapper")
         pending = self._shared_begin(x2)
         logits = ops.router_linear(x2, self.inner.gate)
-        inds, scores = ops.route_topk(logits, self.inner.top_k, self.inner.norm_topk_prob)
-        d = ops.dispatch(inds, self.num_experts, self._identity)
+        inds, scores, d = ops.route_dispatch(logits, self.inner.top_k, self.inner.norm_topk_prob, self._identity,
+                                             self._route_work)
         arena = self.inner.switch_mlp
         y = ops.gather_forward(arena, x2, d, self.inner.top_k, timing=timing)
         shared_y, shared_gate = self._shared_end(pending)

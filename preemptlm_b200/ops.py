@@ -92,6 +92,41 @@ def dispatch(ids: torch.Tensor, num_ids: int, eid2sid: torch.Tensor) -> Dispatch
     return d
 
 
+def route_dispatch(logits: torch.Tensor, top_k: int, norm_topk_prob: bool, eid2sid: torch.Tensor,
+                   work: torch.Tensor):
+    """``_get_routings`` plus the dispatch of the routed pairs in one launch
+    (``sg_route_dispatch``): (inds int32 [T, k], scores bf16 [T, k],
+    Dispatch).  ``work`` is an int32 [E + 1] zero buffer owned by the caller
+    (left zero; one call at a time per buffer)."""
+    logits = _bf16_2d(logits, "logits")
+    T, E = logits.shape
+    if eid2sid.dtype != torch.int32 or eid2sid.numel() < E:
+        raise TypeError("eid2sid must be int32 with E entries")
+    if work.dtype != torch.int32 or work.numel() < E + 1 or not work.is_cuda:
+        raise TypeError("work must be an int32 CUDA tensor of E + 1 zeros")
+    dev = logits.device
+    P = T * top_k
+    mu = min(P, E) + 1
+    inds = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+    d = Dispatch(
+        unique=torch.empty(mu, dtype=torch.int32, device=dev),
+        inverse=torch.empty(P, dtype=torch.int32, device=dev),
+        counts=torch.empty(2, dtype=torch.int32, device=dev),
+        slot_ids=torch.empty(mu, dtype=torch.int32, device=dev),
+        miss_eids=torch.empty(mu, dtype=torch.int32, device=dev),
+        group_off=torch.empty(mu, dtype=torch.int32, device=dev),
+        perm=torch.empty(P, dtype=torch.int32, device=dev),
+        grid_groups=mu - 1,
+    )
+    LAUNCHES[0] += 1
+    _abi.call("sg_route_dispatch", logits.data_ptr(), T, E, int(top_k), int(bool(norm_topk_prob)), eid2sid.data_ptr(),
+              inds.data_ptr(), scores.data_ptr(), d.unique.data_ptr(), d.inverse.data_ptr(), d.counts.data_ptr(),
+              d.slot_ids.data_ptr(), d.miss_eids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), mu,
+              work.data_ptr(), _stream())
+    return inds, scores, d
+
+
 _TOKEN_DISPATCH: dict = {}
 
 

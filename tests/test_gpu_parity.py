@@ -101,6 +101,38 @@ def test_dispatch_matches_numpy(P, E, resident):
         assert np.all(inv[grp] == u)
 
 
+@pytest.mark.parametrize("T,E,k,resident", [(1, 512, 10, 1.0), (256, 512, 10, 1.0), (37, 128, 8, 0.5),
+                                             (300, 1024, 32, 0.7), (2048, 128, 8, 0.5), (8192, 128, 8, 1.0),
+                                             (5, 32, 1, 0.0), (64, 96, 5, 0.9)])
+def test_route_dispatch_fused_matches_separate_calls(T, E, k, resident):
+    """sg_route_dispatch (one launch) gives the ids and scores of
+    sg_route_topk bit for bit and the dispatch of sg_dispatch (the order of
+    pairs inside a group aside), and leaves its work buffer zero, on two calls
+    in a row with one buffer."""
+    g = np.random.default_rng(T + E)
+    eid2sid = torch.from_numpy(np.where(g.random(E) < resident, g.permutation(E), -1).astype(np.int32)).to(DEV)
+    work = torch.zeros(E + 1, dtype=torch.int32, device=DEV)
+    for call in range(2):
+        logits = _bf16((T, E), 30 + call, 1.0)
+        inds, scores, d = ops.route_dispatch(logits, k, True, eid2sid, work)
+        ri, rs = ops.route_topk(logits, k, True)
+        assert torch.equal(inds, ri) and torch.equal(scores, rs)
+        ref = ops.dispatch(ri, E, eid2sid)
+        U = int(ref.counts[0].item())
+        assert torch.equal(d.counts, ref.counts)
+        for name in ("unique", "slot_ids", "group_off"):
+            assert torch.equal(getattr(d, name)[: U + (name == "group_off")],
+                               getattr(ref, name)[: U + (name == "group_off")]), name
+        nm = int(ref.counts[1].item())
+        assert torch.equal(d.miss_eids[:nm], ref.miss_eids[:nm])
+        assert torch.equal(d.inverse, ref.inverse)
+        off = d.group_off[: U + 1].cpu().numpy()
+        a, b = d.perm.cpu().numpy(), ref.perm.cpu().numpy()
+        for u in range(U):
+            assert np.array_equal(np.sort(a[off[u]: off[u + 1]]), np.sort(b[off[u]: off[u + 1]]))
+        assert int(work.abs().sum().item()) == 0
+
+
 # ----------------------------------------------------------------------------- gathered GLU
 
 @pytest.fixture
@@ -154,20 +186,73 @@ def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
 
 
 @pytest.mark.parametrize("bits", [16, 8, 4])
-@pytest.mark.parametrize("T", [2, 37, 256, 1100])
-def test_dense_glu_matches_oracle(bits, T):
+@pytest.mark.parametrize("H,I,T", [(1024, 512, 2), (1024, 512, 37), (1024, 512, 256), (1024, 512, 1100),
+                                   (1024, 512, 2400),  # 4 x 38 tiles of 64 > 148 SMs: 128-wide tiles
+                                   (4096, 1024, 4096)])  # the 397B-style shared expert at prefill
+def test_dense_glu_matches_oracle(bits, H, I, T):
     """The shared expert's dense path (sg_dense_glu): 16/32/64-wide pair tiles
-    with TMA row loads, and 128-wide ones once the tiles overflow one wave."""
-    H, I = 1024, 512
+    with TMA row loads, and 128-wide ones once the tiles overflow one wave.
+    Rows are checked on a seeded sample (h and y)."""
     cfg = LayerConfig("t", 9, H, 3, 1, I, None, bits, 3)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((T, H), 13)
-    y = ops.dense_glu(block.switch_mlp, x, sid=2)
-    assert y is not None
+    arena = block.switch_mlp
+    h = torch.empty((T, I), dtype=torch.bfloat16, device=DEV)
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=DEV)
+    from preemptlm_b200 import _abi
+    import ctypes
+    _abi.check(_abi.load().sg_dense_glu(ctypes.byref(arena.desc()), 2, x.data_ptr(), T, h.data_ptr(), y.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream), "sg_dense_glu")
+    rows = np.sort(np.random.default_rng(T).choice(T, min(T, 48), replace=False))
     ew = LazyExperts(tens["experts"], bits)[2]
-    ref = orc.expert_forward(f32(x), ew)
-    assert_close(f32(y), ref, max_abs=2e-2 * max(1.0, float(np.abs(ref).max())), what="dense y")
+    xr = f32(x)[rows]
+    href = orc.swiglu(orc._mm_bf16(xr, ew.up), orc._mm_bf16(xr, ew.gate))
+    assert_close(f32(h)[rows], href, max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="dense h")
+    # down alone, from the device's own h: isolates the down projection
+    ydown = orc._mm_bf16(f32(h)[rows], ew.down)
+    assert_close(f32(y)[rows], ydown, max_abs=1e-2, rel=4e-3, what="dense y|h")
+    ref = orc._mm_bf16(href, ew.down)
+    assert_close(f32(y)[rows], ref, max_abs=2e-2 * max(1.0, float(np.abs(ref).max())), what="dense y")
+    assert torch.equal(ops.dense_glu(arena, x, sid=2), y)
     assert ops.device_status(reset=True) == 0
+
+
+def test_glu_cfg4_shape_prefill_pairs():
+    """Routed gate/up and down at the 397B-style layer shape (H 4096, I 1024,
+    q4) with prefill-sized groups (128-wide pair tiles, token rows permuted):
+    h and y of a sample of pairs against the oracle, down isolated from h."""
+    cfg = CONFIGS["cfg4"]
+    block, tens = make_layer(cfg.scaled(shared_inter=None), device=DEV)
+    T, k, E = 4096, cfg.top_k, cfg.num_experts
+    x = make_tokens(cfg, T)
+    g = np.random.default_rng(41)
+    inds = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    d = ops.dispatch(torch.from_numpy(inds).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    arena = block.switch_mlp
+    xs = ops.permute_rows(x, d, k)
+    h = ops.glu_gate_up(arena, xs, d, k, _abi_flags("in|out"))
+    y = ops.glu_down(arena, h, d, _abi_flags("in"))
+    perm = d.perm.cpu().numpy()
+    pos = np.sort(g.choice(T * k, 40, replace=False))  # dispatch positions
+    ex = LazyExperts(tens["experts"], cfg.bits)
+    xf = f32(x)
+    hd, yd = f32(h), f32(y)
+    for q in pos:
+        p = perm[q]
+        ew = ex[inds.reshape(-1)[p]]
+        xr = xf[p // k: p // k + 1]
+        hr = orc.swiglu(orc._mm_bf16(xr, ew.up), orc._mm_bf16(xr, ew.gate))
+        assert_close(hd[q: q + 1], hr, max_abs=2e-2 * max(1.0, float(np.abs(hr).max())), what=f"h pos {q}")
+        assert_close(yd[p: p + 1], orc._mm_bf16(hd[q: q + 1], ew.down), max_abs=1e-2, rel=4e-3, what=f"y|h pair {p}")
+    assert torch.equal(ops.gather_forward(arena, x, d, k), y)
+    assert ops.device_status(reset=True) == 0
+
+
+def _abi_flags(which: str) -> int:
+    from preemptlm_b200 import _abi
+
+    return {"in|out": _abi.SG_IN_DISPATCH_ORDER | _abi.SG_OUT_DISPATCH_ORDER,
+            "in": _abi.SG_IN_DISPATCH_ORDER}[which]
 
 
 def test_glu_skips_missing_slots():
