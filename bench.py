@@ -388,6 +388,7 @@ def _sweep_point(moe, cfg, T, steps, warmup, dev, flush):
         moe.replay()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
+    torch.cuda._sleep(QUEUE_AHEAD_CYCLES // 4)
     for i in range(steps):
         g_in.copy_(xs[warmup + i], non_blocking=True)
         flush()
@@ -395,6 +396,7 @@ def _sweep_point(moe, cfg, T, steps, warmup, dev, flush):
         moe.replay()
         ev[i][1].record()
     timing: dict = {}
+    torch.cuda._sleep(QUEUE_AHEAD_CYCLES // 4)  # the host queues the eager steps ahead of the GPU
     for i in range(steps):
         flush()
         moe.forward_resident(xs[warmup + i], timing=timing)

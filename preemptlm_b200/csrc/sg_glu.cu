@@ -1,257 +1,295 @@
 // Gathered SwiGLU expert matmuls over the slot arena (a9, a10, a12):
-// streaming GEMV-style kernels for decode batch sizes.
+// streaming GEMV-style kernels for decode steps that touch few experts.
 //
-// Work item = (group u, block of output rows).  A group is one expert slot with
-// the pairs routed to it (sg_dispatch layout).  Eight warps per CTA; each warp
-// owns WROWS weight rows and splits K across lanes in chunks of 16 weights
-// (lane j takes chunks j, j+32, ...).  The pairs' input rows are staged in
-// shared memory NT at a time.  Affine weights are never expanded: per chunk a
-// lane forms dot = sum(q * x) and xs = sum(x) and adds scale*dot + bias*xs,
-// which equals sum((scale*q + bias) * x) without the bf16 rounding of w.
+// Work item of one warp = (group u, a block of output rows): RW weight rows
+// (gate and up rows in pairs for the gate/up projection) x the whole K range.
+// A group is one expert slot with the pairs routed to it (sg_dispatch
+// layout); the pairs' input rows are staged in shared memory NT at a time.
+//
+// Bytes in flight decide the speed of a decode GEMV: each lane first issues
+// all of its 16-byte weight loads of a K block -- RW rows x NI chunks, 16
+// loads, 8 KB per warp -- and the scale/bias words beside them, and only then
+// converts and multiplies.  Lane j takes chunks j, j + 32, ... of a row.
+// Weights are dequantised in fp32, w = scale * q + bias (q an exact float by
+// a magic-number byte permute and one packed subtraction; no bf16 rounding of
+// w), and multiplied with the tokens' fp32 values by packed f32x2 FMAs; a
+// chunk's x values are read from shared memory once per 8 weights and reused
+// across the warp's RW rows.  Partial sums fold across the warp at the end.
 #include <mutex>
 
 #include "sg_common.cuh"
 
 namespace sg {
 
-constexpr int GW_WARPS = 8;
-constexpr int GW_NT = 8;      // pairs staged per pass
-constexpr int GW_CHUNK = 16;  // weights per lane step
+constexpr int GW_WARPS = 4;   // warps (work items) per CTA, all of one group
+constexpr int GW_NTMAX = 4;   // pairs staged per pass
+constexpr int GW_LOADS = 16;  // 16-byte weight loads per lane per K block
 
-// --------------------------------------------------------------- weight chunk
 template <int BITS>
-struct Chunk;
-
-template <>
-struct Chunk<16> {  // 16 bf16 = 32 bytes
-  uint4 a, b;
-  __device__ __forceinline__ void load(const uint8_t* row, int c) {
-    const uint4* p = reinterpret_cast<const uint4*>(row + (size_t)c * 32);
-    a = ldg_nc_v4(p);
-    b = ldg_nc_v4(p + 1);
-  }
-  __device__ __forceinline__ void to_float(float* w) const {
-    const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      w[2 * i] = lo_bf16(v[i]);
-      w[2 * i + 1] = hi_bf16(v[i]);
-    }
-  }
+struct Wpc {  // weights per 16-byte chunk
+  static constexpr int v = BITS == 16 ? 8 : (BITS == 8 ? 16 : 32);
 };
 
-__device__ __forceinline__ float u8f(uint32_t q) {  // exact small unsigned int -> fp32
-  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+  return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
 }
+__device__ __forceinline__ unsigned long long pk2u(uint32_t lo, uint32_t hi) {
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float lo_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
 
-template <>
-struct Chunk<8> {  // 16 x u8 = 16 bytes
-  uint4 a;
-  __device__ __forceinline__ void load(const uint8_t* row, int c) {
-    a = ldg_nc_v4(row + (size_t)c * 16);
-  }
-  __device__ __forceinline__ void to_float(float* w) const {
-    const uint32_t v[4] = {a.x, a.y, a.z, a.w};
+// Weights 8 s .. 8 s + 7 of a 16-byte chunk as four packed fp32 pairs
+// (w = scale * q + bias for affine arenas; sb2 = (scale, scale), bb2 =
+// (bias, bias)).  q becomes the exact float 2^23 + q by placing its bits in
+// the mantissa of 2^23 (0x4B000000), minus 2^23 by one packed add.
+template <int BITS>
+__device__ __forceinline__ void decode8(const uint4& v, int s, unsigned long long sb2, unsigned long long bb2,
+                                        unsigned long long (&w)[4]) {
+  const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+  if (BITS == 16) {  // a bf16 chunk is 8 weights: word q holds weights 2 q, 2 q + 1
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int q = 0; q < 4; ++q) w[q] = pk2u(words[q] << 16, words[q] & 0xFFFF0000u);
+  } else {
+    const unsigned long long m23 = pk2(-8388608.0f, -8388608.0f);
+    uint32_t e[8];
+    if (BITS == 8) {  // two words = 8 bytes
 #pragma unroll
-      for (int m = 0; m < 4; ++m) w[4 * i + m] = u8f((v[i] >> (8 * m)) & 0xFFu);
-  }
-};
-
-template <>
-struct Chunk<4> {  // 16 x u4 = 8 bytes
-  uint2 a;
-  __device__ __forceinline__ void load(const uint8_t* row, int c) {
-    a = __ldg(reinterpret_cast<const uint2*>(row + (size_t)c * 8));
-  }
-  __device__ __forceinline__ void to_float(float* w) const {
-    const uint32_t v[2] = {a.x, a.y};
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int m = 0; m < 8; ++m) w[8 * i + m] = u8f((v[i] >> (4 * m)) & 0xFu);
-  }
-};
-
-struct Mat {  // one projection of the arena
-  const uint8_t* w;
-  const uint16_t* s;
-  const uint16_t* b;
-  int out, k;
-};
-
-__device__ __forceinline__ size_t row_bytes(int bits, int k) { return (size_t)k * bits / 8; }
-
-// Accumulate WROWS rows x NT pairs over the whole K range.
-template <int BITS, int WROWS, int NT>
-__device__ __forceinline__ void gemv_rows(const Mat* mats, const int* mrow, int slot, const uint16_t* xs_smem, int K,
-                                          float (&acc)[WROWS][GW_NT]) {
-  const int lane = threadIdx.x & 31;
-  const int nchunks = K / GW_CHUNK;
-  const int groups = K / 64;
-  for (int c = lane; c < nchunks; c += 32) {
-    Chunk<BITS> ch[WROWS];
-    float sc[WROWS], bi[WROWS];
-#pragma unroll
-    for (int a = 0; a < WROWS; ++a) {
-      const Mat& m = mats[a];
-      const size_t r = (size_t)slot * m.out + mrow[a];
-      ch[a].load(m.w + r * row_bytes(BITS, K), c);
-      if (BITS != 16) {
-        sc[a] = bf16_to_f32(__ldg(m.s + r * groups + (c >> 2)));
-        bi[a] = bf16_to_f32(__ldg(m.b + r * groups + (c >> 2)));
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t wd = words[2 * s + h];
+        // byte m of the word into bits 0-7, zeros above, then the exponent byte of 2^23
+        e[4 * h + 0] = __byte_perm(wd, 0x4B000000u, 0x7640);
+        e[4 * h + 1] = __byte_perm(wd, 0x4B000000u, 0x7641);
+        e[4 * h + 2] = __byte_perm(wd, 0x4B000000u, 0x7642);
+        e[4 * h + 3] = __byte_perm(wd, 0x4B000000u, 0x7643);
       }
+    } else {  // one word = 8 nibbles, nibble m at bits 4 m
+      const uint32_t wd = words[s];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) e[m] = ((wd >> (4 * m)) & 0xFu) | 0x4B000000u;
     }
 #pragma unroll
-    for (int b = 0; b < NT; ++b) {
-      const uint4* xp = reinterpret_cast<const uint4*>(xs_smem + (size_t)b * K + (size_t)c * GW_CHUNK);
-      const uint4 x0 = xp[0], x1 = xp[1];
-      const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      float xf[16];
-      float xsum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        xf[2 * i] = lo_bf16(xv[i]);
-        xf[2 * i + 1] = hi_bf16(xv[i]);
-      }
-      if (BITS != 16) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) xsum += xf[i];
-      }
-#pragma unroll
-      for (int a = 0; a < WROWS; ++a) {
-        float wf[16];
-        ch[a].to_float(wf);
-        float dot = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) dot = fmaf(wf[i], xf[i], dot);
-        if (BITS != 16) {
-          acc[a][b] = fmaf(sc[a], dot, acc[a][b]);
-          acc[a][b] = fmaf(bi[a], xsum, acc[a][b]);
-        } else {
-          acc[a][b] += dot;
-        }
-      }
-    }
+    for (int q = 0; q < 4; ++q) w[q] = fma2(add2(pk2u(e[2 * q], e[2 * q + 1]), m23), sb2, bb2);
   }
 }
 
-// DUAL: gate/up fused with SwiGLU -> h[p, I];  !DUAL: down -> y[p, H].
-template <int BITS, bool DUAL>
+template <int BITS, bool DUAL, int NI, int NT>
 __global__ void __launch_bounds__(GW_WARPS * 32)
 gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, const int32_t* __restrict__ counts,
                 const int32_t* __restrict__ slot_ids, const int32_t* __restrict__ group_off,
                 const int32_t* __restrict__ perm, uint16_t* __restrict__ out, int in_by_pos, int out_by_pos) {
-  constexpr int WROWS = 4;                        // weight rows per warp
-  constexpr int OROWS = DUAL ? WROWS / 2 : WROWS;  // output rows per warp
+  constexpr int RW0 = GW_LOADS / NI > 8 ? 8 : GW_LOADS / NI;
+  constexpr int RW = RW0 * NT > 32 ? 32 / NT : RW0;  // weight rows per warp (accumulators RW x NT pairs)
+  constexpr int ORW = DUAL ? RW / 2 : RW;            // output rows per warp
+  constexpr int W = Wpc<BITS>::v;
+  constexpr int SUB = BITS == 16 ? 1 : W / 8;        // 8-weight steps per chunk (bf16: one chunk = 8 weights)
+  static_assert(!DUAL || RW % 2 == 0, "gate/up rows come in pairs");
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);  // [GW_NT][K]
+  float* xs = reinterpret_cast<float*>(smem_raw);  // [NT][K] fp32
   const int u = blockIdx.y;
   if (u >= counts[0]) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int H = A.hidden, I = A.inter;
   const int K = DUAL ? H : I;
   const int OUT = DUAL ? I : H;
-  const int orow0 = (blockIdx.x * GW_WARPS + warp) * OROWS;
+  const int CPR = K / W;  // 16-byte chunks per row (bf16: K / 8)
+  const int r0 = (blockIdx.x * GW_WARPS + warp) * ORW;
   const int slot = slot_ids[u];
   const int p_begin = group_off[u], p_end = group_off[u + 1];
   const bool slot_ok = slot >= 0 && slot < A.num_slots;
+  const bool rows_ok = r0 < OUT;
+  const size_t rbytes = (size_t)K * BITS / 8;
+  const int groups = K / 64;
 
-  Mat mats[WROWS];
-  int mrow[WROWS];
-#pragma unroll
-  for (int a = 0; a < WROWS; ++a) {
-    int r = DUAL ? orow0 + (a % OROWS) : orow0 + a;
-    mrow[a] = r < OUT ? r : OUT - 1;  // clamp reads; writes are masked
-    if (DUAL) {
-      const bool g = a < OROWS;
-      mats[a] = Mat{static_cast<const uint8_t*>(g ? A.gate_w : A.up_w), static_cast<const uint16_t*>(g ? A.gate_s : A.up_s),
-                    static_cast<const uint16_t*>(g ? A.gate_b : A.up_b), I, H};
-    } else {
-      mats[a] = Mat{static_cast<const uint8_t*>(A.down_w), static_cast<const uint16_t*>(A.down_s),
-                    static_cast<const uint16_t*>(A.down_b), H, I};
-    }
-  }
+  // matrix m (gate / up, or down) of this slot; row a of the warp is row
+  // r0 + a % ORW of matrix a / ORW, clamped so reads stay in range (writes
+  // of rows past OUT are masked)
+  const size_t slot_row0 = (size_t)(slot_ok ? slot : 0) * OUT;
+  const uint8_t* wm[2] = {static_cast<const uint8_t*>(DUAL ? A.gate_w : A.down_w),
+                          static_cast<const uint8_t*>(DUAL ? A.up_w : A.down_w)};
+  const uint16_t* sm_[2] = {static_cast<const uint16_t*>(DUAL ? A.gate_s : A.down_s),
+                            static_cast<const uint16_t*>(DUAL ? A.up_s : A.down_s)};
+  const uint16_t* bm[2] = {static_cast<const uint16_t*>(DUAL ? A.gate_b : A.down_b),
+                           static_cast<const uint16_t*>(DUAL ? A.up_b : A.down_b)};
+  auto row_of = [&](int a) -> size_t { return slot_row0 + min(r0 + (DUAL ? a % ORW : a), OUT - 1); };
 
-  for (int p0 = p_begin; p0 < p_end; p0 += GW_NT) {
-    const int nb = min(GW_NT, p_end - p0);
+  for (int p0 = p_begin; p0 < p_end; p0 += NT) {
+    const int nb = min(NT, p_end - p0);
     __syncthreads();
-    const int cpr = K / 8;  // 16-byte chunks per row
-    for (int c = threadIdx.x; c < GW_NT * cpr; c += blockDim.x) {
-      int b = c / cpr, cc = c - b * cpr;
+    for (int c = threadIdx.x; c < NT * (K / 8); c += blockDim.x) {  // stage the pairs' rows as fp32
+      const int b = c / (K / 8), cc = c - b * (K / 8);
       uint4 v = make_uint4(0, 0, 0, 0);
       if (b < nb) {
-        int row = in_by_pos ? p0 + b : perm[p0 + b] / pair_div;
+        const int row = in_by_pos ? p0 + b : perm[p0 + b] / pair_div;
         v = reinterpret_cast<const uint4*>(xin + (size_t)row * K)[cc];
       }
-      reinterpret_cast<uint4*>(xs)[c] = v;
+      float4* dst = reinterpret_cast<float4*>(xs + (size_t)b * K + cc * 8);
+      dst[0] = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
+      dst[1] = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
     }
     __syncthreads();
-    float acc[WROWS][GW_NT];
+    if (!rows_ok) continue;
+    unsigned long long acc[RW][NT];
 #pragma unroll
-    for (int a = 0; a < WROWS; ++a)
+    for (int a = 0; a < RW; ++a)
 #pragma unroll
-      for (int b = 0; b < GW_NT; ++b) acc[a][b] = 0.0f;
-    if (slot_ok && orow0 < OUT) {
-      if (nb == 1) gemv_rows<BITS, WROWS, 1>(mats, mrow, slot, xs, K, acc);
-      else if (nb == 2) gemv_rows<BITS, WROWS, 2>(mats, mrow, slot, xs, K, acc);
-      else if (nb <= 4) gemv_rows<BITS, WROWS, 4>(mats, mrow, slot, xs, K, acc);
-      else gemv_rows<BITS, WROWS, GW_NT>(mats, mrow, slot, xs, K, acc);
+      for (int b = 0; b < NT; ++b) acc[a][b] = 0ull;
+    if (slot_ok) {
+      for (int c0 = 0; c0 < CPR; c0 += 32 * NI) {
+        uint4 wv[RW][NI];
+        uint32_t sbw[RW][NI];  // (scale, bias) bf16 bits of the chunk's group
+#pragma unroll
+        for (int a = 0; a < RW; ++a) {
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int c = c0 + lane + 32 * i;
+            const bool ok = c < CPR;
+            const int m = DUAL && a >= ORW;
+            const size_t R = row_of(a);
+            wv[a][i] = ok ? ldg_nc_v4(wm[m] + R * rbytes + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+            if (BITS != 16) {
+              const size_t g = R * groups + c * W / 64;
+              sbw[a][i] = ok ? (static_cast<uint32_t>(__ldg(sm_[m] + g)) | (static_cast<uint32_t>(__ldg(bm[m] + g)) << 16))
+                             : 0u;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+          const int c = c0 + lane + 32 * i;
+          if (c >= CPR) continue;
+#pragma unroll
+          for (int sstep = 0; sstep < SUB; ++sstep) {
+            // x of these 8 weights for every staged pair, packed in pairs
+            unsigned long long x2[NT][4];
+#pragma unroll
+            for (int b = 0; b < NT; ++b) {
+              const float4* xp = reinterpret_cast<const float4*>(xs + (size_t)b * K + (size_t)c * W + sstep * 8);
+              const float4 lo = xp[0], hi = xp[1];
+              x2[b][0] = pk2(lo.x, lo.y);
+              x2[b][1] = pk2(lo.z, lo.w);
+              x2[b][2] = pk2(hi.x, hi.y);
+              x2[b][3] = pk2(hi.z, hi.w);
+            }
+#pragma unroll
+            for (int a = 0; a < RW; ++a) {
+              unsigned long long w[4];
+              if (BITS == 16) {
+                decode8<16>(wv[a][i], 0, 0ull, 0ull, w);
+              } else {
+                const float s = bf16_to_f32(static_cast<uint16_t>(sbw[a][i] & 0xFFFFu));
+                const float bb = bf16_to_f32(static_cast<uint16_t>(sbw[a][i] >> 16));
+                decode8<BITS>(wv[a][i], sstep, pk2(s, s), pk2(bb, bb), w);
+              }
+#pragma unroll
+              for (int b = 0; b < NT; ++b)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[a][b] = fma2(w[q], x2[b][q], acc[a][b]);
+            }
+          }
+        }
+      }
     }
-    if (orow0 >= OUT) continue;
-    // fold partials and write: lane (o * GW_NT + b) owns output row o, pair b
+    // fold: lane (o * NT + b) % 32 writes output row r0 + o of pair b
 #pragma unroll
-    for (int o = 0; o < OROWS; ++o) {
+    for (int o = 0; o < ORW; ++o) {
 #pragma unroll
-      for (int b = 0; b < GW_NT; ++b) {
+      for (int b = 0; b < NT; ++b) {
         if (b >= nb) break;
-        const int r = orow0 + o;
-        if (DUAL) {
-          float g = warp_fold_sum(acc[o][b]);
-          float up = warp_fold_sum(acc[o + OROWS][b]);
-          if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
-            const int p = out_by_pos ? p0 + b : perm[p0 + b];
-            out[(size_t)p * OUT + r] = slot_ok ? swiglu_bf16(g, up) : (uint16_t)0;
-          }
-        } else {
-          float y = warp_fold_sum(acc[o][b]);
-          if (lane == ((o * GW_NT + b) & 31) && r < OUT) {
-            const int p = out_by_pos ? p0 + b : perm[p0 + b];
-            out[(size_t)p * OUT + r] = slot_ok ? f32_to_bf16(y) : (uint16_t)0;
-          }
+        const int r = r0 + o;
+        const float g = warp_fold_sum(__fadd_rn(lo_f(acc[o][b]), hi_f(acc[o][b])));
+        float v2 = 0.0f;
+        if (DUAL) v2 = warp_fold_sum(__fadd_rn(lo_f(acc[o + ORW][b]), hi_f(acc[o + ORW][b])));
+        if (lane == ((o * NT + b) & 31) && r < OUT) {
+          const int p = out_by_pos ? p0 + b : perm[p0 + b];
+          uint16_t res = 0;
+          if (slot_ok) res = DUAL ? swiglu_bf16(g, v2) : f32_to_bf16(g);
+          out[(size_t)p * OUT + r] = res;
         }
       }
     }
   }
 }
 
+template <int BITS, bool DUAL, int NI, int NT>
+static int launch_gemv_nt(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
+                          const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                          uint16_t* out, int in_by_pos, int out_by_pos, cudaStream_t s) {
+  constexpr int RW0 = GW_LOADS / NI > 8 ? 8 : GW_LOADS / NI;
+  constexpr int RW = RW0 * NT > 32 ? 32 / NT : RW0;
+  constexpr int ORW = DUAL ? RW / 2 : RW;
+  const int K = DUAL ? A->hidden : A->inter;
+  const int OUT = DUAL ? A->inter : A->hidden;
+  const size_t smem = (size_t)NT * K * 4;
+  if (smem > 48 * 1024) {
+    static bool attr_done[64] = {};
+    int dev = 0;
+    SG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
+    if (!attr_done[dev]) {
+      SG_CUDA_TRY(cudaFuncSetAttribute(gemv_glu_kernel<BITS, DUAL, NI, NT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+      attr_done[dev] = true;
+    }
+  }
+  const int orows_cta = GW_WARPS * ORW;
+  dim3 grid((OUT + orows_cta - 1) / orows_cta, grid_groups);
+  gemv_glu_kernel<BITS, DUAL, NI, NT><<<grid, GW_WARPS * 32, smem, s>>>(*A, xin, pair_div, counts, slot_ids,
+                                                                        group_off, perm, out, in_by_pos, out_by_pos);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+template <int BITS, bool DUAL, int NI>
+static int launch_gemv_ni(const sg_arena* A, int nt, const uint16_t* xin, int pair_div, const int32_t* counts,
+                          const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
+                          uint16_t* out, int in_by_pos, int out_by_pos, cudaStream_t s) {
+  if (nt <= 1)
+    return launch_gemv_nt<BITS, DUAL, NI, 1>(A, xin, pair_div, counts, slot_ids, group_off, perm, grid_groups, out,
+                                             in_by_pos, out_by_pos, s);
+  if (nt <= 2)
+    return launch_gemv_nt<BITS, DUAL, NI, 2>(A, xin, pair_div, counts, slot_ids, group_off, perm, grid_groups, out,
+                                             in_by_pos, out_by_pos, s);
+  return launch_gemv_nt<BITS, DUAL, NI, 4>(A, xin, pair_div, counts, slot_ids, group_off, perm, grid_groups, out,
+                                           in_by_pos, out_by_pos, s);
+}
+
+// NI: chunks per lane per row in one K block, the smallest power of two
+// covering the row (at most 8); NT: the staged pairs, from the mean pairs per
+// group (a host bound; larger groups take several passes).
 template <int BITS, bool DUAL>
 static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
                        const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
-                       uint16_t* out, int in_by_pos, int out_by_pos, cudaStream_t s) {
+                       uint16_t* out, int in_by_pos, int out_by_pos, int num_pairs, cudaStream_t s) {
   const int K = DUAL ? A->hidden : A->inter;
-  const int OUT = DUAL ? A->inter : A->hidden;
-  const int orows_cta = GW_WARPS * (DUAL ? 2 : 4);
-  const size_t smem = (size_t)GW_NT * K * 2;
-  static bool attr_done = false;
-  if (!attr_done) {
-    SG_CUDA_TRY(cudaFuncSetAttribute(gemv_glu_kernel<BITS, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     160 * 1024));
-    attr_done = true;
-  }
-  dim3 grid((OUT + orows_cta - 1) / orows_cta, grid_groups);
-  gemv_glu_kernel<BITS, DUAL><<<grid, GW_WARPS * 32, smem, s>>>(*A, xin, pair_div, counts, slot_ids, group_off,
-                                                                 perm, out, in_by_pos, out_by_pos);
-  SG_LAUNCH_CHECK();
-  return SG_OK;
+  const int cpr = K / Wpc<BITS>::v;
+  const int need = (cpr + 31) / 32;
+  const int nt = grid_groups > 0 ? (num_pairs + grid_groups - 1) / grid_groups : 1;
+#define SG_GEMV_NI(NIV)                                                                                      \
+  return launch_gemv_ni<BITS, DUAL, NIV>(A, nt, xin, pair_div, counts, slot_ids, group_off, perm, grid_groups, \
+                                         out, in_by_pos, out_by_pos, s)
+  if (need <= 1) SG_GEMV_NI(1);
+  if (need <= 2) SG_GEMV_NI(2);
+  if (need <= 4) SG_GEMV_NI(4);
+  SG_GEMV_NI(8);
+#undef SG_GEMV_NI
 }
 
 int check_arena(const sg_arena* A) {
   if (!A || !A->gate_w || !A->up_w || !A->down_w) return SG_ERR_INVALID_ARG;
   if (A->num_slots < 1 || A->hidden < 64 || A->inter < 64) return SG_ERR_SHAPE;
   if (A->hidden % 64 || A->inter % 64) return SG_ERR_SHAPE;
-  if ((size_t)A->hidden * 2 * GW_NT > 160 * 1024 || (size_t)A->inter * 2 * GW_NT > 160 * 1024) return SG_ERR_SHAPE;
+  if ((size_t)A->hidden * 4 * GW_NTMAX > 160 * 1024 || (size_t)A->inter * 4 * GW_NTMAX > 160 * 1024) return SG_ERR_SHAPE;
   if (A->bits == 16) return SG_OK;
   if (A->bits != 4 && A->bits != 8) return SG_ERR_FORMAT;
   if (A->group_size != 64) return SG_ERR_FORMAT;
@@ -326,9 +364,9 @@ static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int
                          grid_groups, h, s);
   }
   switch (arena->bits) {
-    case 16: return launch_gemv<16, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
-    case 8: return launch_gemv<8, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
-    default: return launch_gemv<4, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, s);
+    case 16: return launch_gemv<16, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, num_pairs, s);
+    case 8: return launch_gemv<8, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, num_pairs, s);
+    default: return launch_gemv<4, true>(arena, x, div, counts, slot_ids, group_off, perm, grid_groups, h, in_pos, out_pos, num_pairs, s);
   }
 }
 
@@ -340,9 +378,9 @@ static int glu_single(const sg_arena* arena, const uint16_t* h, int num_pairs, c
     return tc_glu_launch(arena, false, h, num_pairs, 1, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
                          grid_groups, y, s);
   switch (arena->bits) {
-    case 16: return launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
-    case 8: return launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
-    default: return launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, s);
+    case 16: return launch_gemv<16, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, num_pairs, s);
+    case 8: return launch_gemv<8, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, num_pairs, s);
+    default: return launch_gemv<4, false>(arena, h, 1, counts, slot_ids, group_off, perm, grid_groups, y, in_pos, out_pos, num_pairs, s);
   }
 }
 

@@ -210,7 +210,9 @@ def test_dense_glu_matches_oracle(bits, H, I, T):
     assert_close(f32(h)[rows], href, max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="dense h")
     # down alone, from the device's own h: isolates the down projection
     ydown = orc._mm_bf16(f32(h)[rows], ew.down)
-    assert_close(f32(y)[rows], ydown, max_abs=1e-2, rel=4e-3, what="dense y|h")
+    # one bf16 ulp of the largest output (accumulation order differs)
+    assert_close(f32(y)[rows], ydown, max_abs=1e-2 * max(1.0, float(np.abs(ydown).max())), rel=4e-3,
+                 what="dense y|h")
     ref = orc._mm_bf16(href, ew.down)
     assert_close(f32(y)[rows], ref, max_abs=2e-2 * max(1.0, float(np.abs(ref).max())), what="dense y")
     assert torch.equal(ops.dense_glu(arena, x, sid=2), y)
@@ -243,7 +245,8 @@ def test_glu_cfg4_shape_prefill_pairs():
         xr = xf[p // k: p // k + 1]
         hr = orc.swiglu(orc._mm_bf16(xr, ew.up), orc._mm_bf16(xr, ew.gate))
         assert_close(hd[q: q + 1], hr, max_abs=2e-2 * max(1.0, float(np.abs(hr).max())), what=f"h pos {q}")
-        assert_close(yd[p: p + 1], orc._mm_bf16(hd[q: q + 1], ew.down), max_abs=1e-2, rel=4e-3, what=f"y|h pair {p}")
+        yr = orc._mm_bf16(hd[q: q + 1], ew.down)
+        assert_close(yd[p: p + 1], yr, max_abs=1e-2 * max(1.0, float(np.abs(yr).max())), rel=4e-3, what=f"y|h pair {p}")
     assert torch.equal(ops.gather_forward(arena, x, d, k), y)
     assert ops.device_status(reset=True) == 0
 
