@@ -114,16 +114,30 @@ int sg_dispatch(const int32_t* inds, int P, int E, const int32_t* eid2sid,
  * P = T * k pairs; the order of pairs inside a group is not specified).
  * work: caller-provided int32 [E + 1], all zero before the first call; every
  * call leaves it zero (calls using one work buffer must not overlap).
+ * trace (NULL: none): the kernel also writes each token's ids, scores and
+ * raw logits there as it produces them -- the router-selection telemetry that
+ * the reference's recorder captures, `self.recorder.capture(...)` at
+ * qwen3_x_moe.py:261-269 (recorder.py:57-111), without another launch.
  * Replaces `_get_routings` (qwen3_x_moe.py:26-40), the host np.unique and
  * miss set of `_maybe_admit` (:145-156) and `slot_ids =
  * self._eid_lookup_table[unique_eids]` (:277).
  * Requires E % 32 == 0, E <= 1024, 1 <= k <= 32, k <= E; max_unique >=
  * min(P, E) + 1. */
+typedef struct sg_route_trace {
+  int32_t* ids;      /* [T, k] the routed expert ids, or NULL */
+  uint16_t* scores;  /* [T, k] bf16 scores after renormalisation, or NULL */
+  uint16_t* logits;  /* [T, E] bf16 router logits (pre-softmax), or NULL */
+} sg_route_trace;
+
 int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, int norm_topk_prob,
                       const int32_t* eid2sid, int32_t* inds, uint16_t* scores,
                       int32_t* unique, int32_t* inverse, int32_t* counts, int32_t* slot_ids,
                       int32_t* miss_eids, int32_t* group_off, int32_t* perm, int max_unique,
-                      int32_t* work, void* stream);
+                      int32_t* work, const sg_route_trace* trace, void* stream);
+
+/* Device address of pinned host memory (cudaHostGetDevicePointer), for
+ * trace arrays the kernels write straight into host memory. */
+int sg_host_device_ptr(void* host, void** device);
 
 /* ------------------------------------------------- gathered SwiGLU (a9/a10)
  * y[p, H] = bf16(swiglu(x[p / pair_div] @ gate^T, ... @ up^T) @ down^T) for

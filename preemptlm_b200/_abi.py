@@ -28,7 +28,7 @@ SG_OUT_DISPATCH_ORDER = 2
 # Every symbol include/sg_abi.h declares (checked by the CPU tests).
 EXPORTED_SYMBOLS = (
     "sg_status_string", "sg_version", "sg_built_arch", "sg_router_logits", "sg_route_topk",
-    "sg_dispatch", "sg_route_dispatch", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_use_permute", "sg_permute_rows", "sg_glu_gate_up", "sg_glu_down",
+    "sg_dispatch", "sg_route_dispatch", "sg_host_device_ptr", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_use_permute", "sg_permute_rows", "sg_glu_gate_up", "sg_glu_down",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
     "sg_ep_region_bytes", "sg_ep_layout", "sg_ep_alloc", "sg_ep_free", "sg_ep_ipc_handle", "sg_ep_ipc_open",
@@ -41,6 +41,10 @@ class SlottedGLUError(RuntimeError):
     def __init__(self, status: int, where: str):
         self.status = status
         super().__init__(f"{where}: {status_string(status)} (status {status})")
+
+
+class sg_route_trace(ctypes.Structure):
+    _fields_ = [("ids", ctypes.c_void_p), ("scores", ctypes.c_void_p), ("logits", ctypes.c_void_p)]
 
 
 class sg_arena(ctypes.Structure):
@@ -81,7 +85,8 @@ def load() -> ctypes.CDLL:
         "sg_router_logits": (I32, [P, P, P, I32, I32, I32, P]),
         "sg_route_topk": (I32, [P, I32, I32, I32, I32, P, P, P]),
         "sg_dispatch": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I32, P]),
-        "sg_route_dispatch": (I32, [P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, I32, P, P]),
+        "sg_route_dispatch": (I32, [P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, I32, P, P, P]),
+        "sg_host_device_ptr": (I32, [P, P]),
         "sg_glu_forward": (I32, [A, P, I32, I32, P, P, P, P, I32, P, P, P, P]),
         "sg_glu_forward_noalloc": (I32, [A, P, I32, I32, P, P, P, P, I32, P, P]),
         "sg_glu_use_permute": (I32, [A, I32, I32]),

@@ -87,3 +87,11 @@ extern "C" int sg_refill_h2d(const void* blob, size_t blob_len, const sg_arena* 
   }
   return SG_OK;
 }
+
+extern "C" int sg_host_device_ptr(void* host, void** device) {
+  if (!host || !device) return SG_ERR_INVALID_ARG;
+  void* d = nullptr;
+  SG_CUDA_TRY(cudaHostGetDevicePointer(&d, host, 0));
+  *device = d;
+  return SG_OK;
+}

@@ -309,13 +309,22 @@ dispatch_kernel(const int32_t* __restrict__ inds, int P, int E, const int32_t* _
 constexpr int RD_WARPS = 32;  // 1024 threads: phase 2 runs on one CTA
 constexpr int RD_MAX_E = 1024;
 
+// Optional router trace: the same ids and scores, and the token's raw
+// logits, also written to trace memory (typically mapped pinned host memory,
+// so they cross PCIe as the kernel produces them; a NULL array is skipped).
+struct RouteTrace {
+  int32_t* ids;       // [T, k]
+  uint16_t* scores;   // [T, k] bf16
+  uint16_t* logits;   // [T, E] bf16
+};
+
 template <int C>
 __global__ void __launch_bounds__(RD_WARPS * 32)
 route_dispatch_kernel(const uint16_t* __restrict__ logits, int T, int E, int k, int norm,
                       const int32_t* __restrict__ eid2sid, int32_t* inds, uint16_t* __restrict__ scores,
                       int32_t* __restrict__ unique, int32_t* inverse, int32_t* __restrict__ counts,
                       int32_t* __restrict__ slot_ids, int32_t* __restrict__ miss_eids,
-                      int32_t* __restrict__ group_off, int32_t* __restrict__ perm, int32_t* work) {
+                      int32_t* __restrict__ group_off, int32_t* __restrict__ perm, int32_t* work, RouteTrace tr) {
   __shared__ int s_rank[RD_MAX_E];  // unique index of expert e (phase 2)
   __shared__ int s_base[RD_MAX_E];  // first permutation position of expert e's group
   __shared__ int warp_tot[32];
@@ -328,7 +337,9 @@ route_dispatch_kernel(const uint16_t* __restrict__ logits, int T, int E, int k, 
     float m = -INFINITY;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      v[c] = bf16_to_f32(row[c * 32 + lane]);
+      const uint16_t lb = row[c * 32 + lane];
+      if (tr.logits != nullptr) tr.logits[(size_t)t * E + c * 32 + lane] = lb;
+      v[c] = bf16_to_f32(lb);
       m = fmaxf(m, v[c]);
     }
 #pragma unroll
@@ -367,8 +378,11 @@ route_dispatch_kernel(const uint16_t* __restrict__ logits, int T, int E, int k, 
       float sc = bf16_to_f32(static_cast<uint16_t>(my_key >> 16));
       if (norm) sc = __fdiv_rn(sc, round_bf16(ssum));
       const size_t p = (size_t)t * k + lane;
+      const uint16_t scb = f32_to_bf16(sc);
       inds[p] = e;
-      scores[p] = f32_to_bf16(sc);
+      scores[p] = scb;
+      if (tr.ids != nullptr) tr.ids[p] = e;
+      if (tr.scores != nullptr) tr.scores[p] = scb;
       inverse[p] = atomicAdd(&work[e], 1);  // position inside the group of e
     }
   }
@@ -482,7 +496,8 @@ extern "C" int sg_route_topk(const uint16_t* logits, int T, int E, int k, int no
 extern "C" int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, int norm_topk_prob,
                                  const int32_t* eid2sid, int32_t* inds, uint16_t* scores, int32_t* unique,
                                  int32_t* inverse, int32_t* counts, int32_t* slot_ids, int32_t* miss_eids,
-                                 int32_t* group_off, int32_t* perm, int max_unique, int32_t* work, void* stream) {
+                                 int32_t* group_off, int32_t* perm, int max_unique, int32_t* work,
+                                 const sg_route_trace* trace, void* stream) {
   if (T < 0) return SG_ERR_INVALID_ARG;
   if (E % 32 != 0 || E < 32 || E > sg::RD_MAX_E || k < 1 || k > 32 || k > E) return SG_ERR_SHAPE;
   if (!eid2sid || !unique || !counts || !slot_ids || !miss_eids || !group_off || !work) return SG_ERR_INVALID_ARG;
@@ -496,6 +511,8 @@ extern "C" int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, in
     return SG_OK;
   }
   if (!logits || !inds || !scores || !inverse || !perm) return SG_ERR_INVALID_ARG;
+  sg::RouteTrace tr{nullptr, nullptr, nullptr};
+  if (trace != nullptr) tr = sg::RouteTrace{trace->ids, trace->scores, trace->logits};
   dim3 grid((T + sg::RD_WARPS - 1) / sg::RD_WARPS);
   const int C = E / 32;
 #define SG_RD_CASE(CC)                                                                                      \
@@ -503,7 +520,7 @@ extern "C" int sg_route_dispatch(const uint16_t* logits, int T, int E, int k, in
     sg::route_dispatch_kernel<CC><<<grid, sg::RD_WARPS * 32, 0, s>>>(logits, T, E, k, norm_topk_prob,       \
                                                                      eid2sid, inds, scores, unique, inverse, \
                                                                      counts, slot_ids, miss_eids, group_off, \
-                                                                     perm, work);                            \
+                                                                     perm, work, tr);                        \
     break;
   switch (C) {
     SG_RD_CASE(1) SG_RD_CASE(2) SG_RD_CASE(3) SG_RD_CASE(4) SG_RD_CASE(5) SG_RD_CASE(6) SG_RD_CASE(7)

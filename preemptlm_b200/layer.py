@@ -311,8 +311,13 @@ class Qwen3_xMoEWrapper(SlotTable):
         # permutation (sg_route_dispatch; _get_routings + the np.unique of
         # _maybe_admit + the slot lookup of qwen3_x_moe.py:277)
         table = self._identity if self.expert_cache is None else self.eid2sid_device
+        trace = None
+        if self.should_capture_traces and hasattr(self.recorder, "reserve"):
+            # the routing kernel writes the step's ids / scores / logits into
+            # the recorder's pinned host ring as it computes them
+            trace = self.recorder.reserve(B * S, self._capture_gate_logits)
         inds, scores, d_step = ops.route_dispatch(logits, self.inner.top_k, self.inner.norm_topk_prob, table,
-                                                  self._route_work)
+                                                  self._route_work, trace=trace)
         admitted = None
         early: dict = {}
         if self.expert_cache is not None:

@@ -93,11 +93,13 @@ def dispatch(ids: torch.Tensor, num_ids: int, eid2sid: torch.Tensor) -> Dispatch
 
 
 def route_dispatch(logits: torch.Tensor, top_k: int, norm_topk_prob: bool, eid2sid: torch.Tensor,
-                   work: torch.Tensor):
+                   work: torch.Tensor, trace=None):
     """``_get_routings`` plus the dispatch of the routed pairs in one launch
     (``sg_route_dispatch``): (inds int32 [T, k], scores bf16 [T, k],
     Dispatch).  ``work`` is an int32 [E + 1] zero buffer owned by the caller
-    (left zero; one call at a time per buffer)."""
+    (left zero; one call at a time per buffer).  ``trace``: an
+    ``_abi.sg_route_trace`` of device-visible addresses the kernel also writes
+    the ids, scores and logits to (router telemetry), or None."""
     logits = _bf16_2d(logits, "logits")
     T, E = logits.shape
     if eid2sid.dtype != torch.int32 or eid2sid.numel() < E:
@@ -123,7 +125,7 @@ def route_dispatch(logits: torch.Tensor, top_k: int, norm_topk_prob: bool, eid2s
     _abi.call("sg_route_dispatch", logits.data_ptr(), T, E, int(top_k), int(bool(norm_topk_prob)), eid2sid.data_ptr(),
               inds.data_ptr(), scores.data_ptr(), d.unique.data_ptr(), d.inverse.data_ptr(), d.counts.data_ptr(),
               d.slot_ids.data_ptr(), d.miss_eids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), mu,
-              work.data_ptr(), _stream())
+              work.data_ptr(), None if trace is None else ctypes.byref(trace), _stream())
     return inds, scores, d
 
 
