@@ -23,7 +23,7 @@ namespace sg {
 
 constexpr int GW_WARPS = 4;   // warps (work items) per CTA, all of one group
 constexpr int GW_NTMAX = 4;   // pairs staged per pass
-constexpr int GW_LOADS = 16;  // 16-byte weight loads per lane per K block
+constexpr int GW_LOADS = 8;   // 16-byte weight loads per lane per K block (4 KB per warp)
 
 template <int BITS>
 struct Wpc {  // weights per 16-byte chunk
@@ -83,13 +83,15 @@ __device__ __forceinline__ void decode8(const uint4& v, int s, unsigned long lon
   }
 }
 
+// At most 128 registers: four 4-warp CTAs per SM, 16 warps with 4 KB of
+// weight loads each in flight.
 template <int BITS, bool DUAL, int NI, int NT>
-__global__ void __launch_bounds__(GW_WARPS * 32)
+__global__ void __launch_bounds__(GW_WARPS * 32, 4)
 gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, const int32_t* __restrict__ counts,
                 const int32_t* __restrict__ slot_ids, const int32_t* __restrict__ group_off,
                 const int32_t* __restrict__ perm, uint16_t* __restrict__ out, int in_by_pos, int out_by_pos) {
-  constexpr int RW0 = GW_LOADS / NI > 8 ? 8 : GW_LOADS / NI;
-  constexpr int RW = RW0 * NT > 32 ? 32 / NT : RW0;  // weight rows per warp (accumulators RW x NT pairs)
+  constexpr int RW0 = GW_LOADS / NI < 2 ? 2 : (GW_LOADS / NI > 4 ? 4 : GW_LOADS / NI);
+  constexpr int RW = RW0 * NT > 16 ? 16 / NT : RW0;  // weight rows per warp (accumulators RW x NT pairs)
   constexpr int ORW = DUAL ? RW / 2 : RW;            // output rows per warp
   constexpr int W = Wpc<BITS>::v;
   constexpr int SUB = BITS == 16 ? 1 : W / 8;        // 8-weight steps per chunk (bf16: one chunk = 8 weights)
@@ -123,8 +125,33 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
                            static_cast<const uint16_t*>(DUAL ? A.up_b : A.down_b)};
   auto row_of = [&](int a) -> size_t { return slot_row0 + min(r0 + (DUAL ? a % ORW : a), OUT - 1); };
 
+  // one K block of this lane's weight chunks and their (scale, bias) words
+  auto load_block = [&](int c0, uint4 (&wv)[RW][NI], uint32_t (&sbw)[RW][NI]) {
+#pragma unroll
+    for (int a = 0; a < RW; ++a) {
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int c = c0 + lane + 32 * i;
+        const bool ok = c < CPR;
+        const int m = DUAL && a >= ORW;
+        const size_t R = row_of(a);
+        wv[a][i] = ok ? ldg_nc_v4(wm[m] + R * rbytes + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+        if (BITS != 16) {
+          const size_t g = R * groups + c * W / 64;
+          sbw[a][i] = ok ? (static_cast<uint32_t>(__ldg(sm_[m] + g)) | (static_cast<uint32_t>(__ldg(bm[m] + g)) << 16))
+                         : 0u;
+        }
+      }
+    }
+  };
+
   for (int p0 = p_begin; p0 < p_end; p0 += NT) {
     const int nb = min(NT, p_end - p0);
+    uint4 wv[RW][NI];
+    uint32_t sbw[RW][NI];
+    // the first K block's weights are requested before the pairs' rows are
+    // staged, so the two memory round trips overlap
+    if (rows_ok && slot_ok) load_block(0, wv, sbw);
     __syncthreads();
     for (int c = threadIdx.x; c < NT * (K / 8); c += blockDim.x) {  // stage the pairs' rows as fp32
       const int b = c / (K / 8), cc = c - b * (K / 8);
@@ -146,24 +173,7 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
       for (int b = 0; b < NT; ++b) acc[a][b] = 0ull;
     if (slot_ok) {
       for (int c0 = 0; c0 < CPR; c0 += 32 * NI) {
-        uint4 wv[RW][NI];
-        uint32_t sbw[RW][NI];  // (scale, bias) bf16 bits of the chunk's group
-#pragma unroll
-        for (int a = 0; a < RW; ++a) {
-#pragma unroll
-          for (int i = 0; i < NI; ++i) {
-            const int c = c0 + lane + 32 * i;
-            const bool ok = c < CPR;
-            const int m = DUAL && a >= ORW;
-            const size_t R = row_of(a);
-            wv[a][i] = ok ? ldg_nc_v4(wm[m] + R * rbytes + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-            if (BITS != 16) {
-              const size_t g = R * groups + c * W / 64;
-              sbw[a][i] = ok ? (static_cast<uint32_t>(__ldg(sm_[m] + g)) | (static_cast<uint32_t>(__ldg(bm[m] + g)) << 16))
-                             : 0u;
-            }
-          }
-        }
+        if (c0 > 0) load_block(c0, wv, sbw);
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
           const int c = c0 + lane + 32 * i;
@@ -225,8 +235,8 @@ template <int BITS, bool DUAL, int NI, int NT>
 static int launch_gemv_nt(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
                           const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
                           uint16_t* out, int in_by_pos, int out_by_pos, cudaStream_t s) {
-  constexpr int RW0 = GW_LOADS / NI > 8 ? 8 : GW_LOADS / NI;
-  constexpr int RW = RW0 * NT > 32 ? 32 / NT : RW0;
+  constexpr int RW0 = GW_LOADS / NI < 2 ? 2 : (GW_LOADS / NI > 4 ? 4 : GW_LOADS / NI);
+  constexpr int RW = RW0 * NT > 16 ? 16 / NT : RW0;
   constexpr int ORW = DUAL ? RW / 2 : RW;
   const int K = DUAL ? A->hidden : A->inter;
   const int OUT = DUAL ? A->inter : A->hidden;
@@ -265,7 +275,7 @@ static int launch_gemv_ni(const sg_arena* A, int nt, const uint16_t* xin, int pa
 }
 
 // NI: chunks per lane per row in one K block, the smallest power of two
-// covering the row (at most 8); NT: the staged pairs, from the mean pairs per
+// covering the row (at most 4); NT: the staged pairs, from the mean pairs per
 // group (a host bound; larger groups take several passes).
 template <int BITS, bool DUAL>
 static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, const int32_t* counts,
@@ -280,8 +290,7 @@ static int launch_gemv(const sg_arena* A, const uint16_t* xin, int pair_div, con
                                          out, in_by_pos, out_by_pos, s)
   if (need <= 1) SG_GEMV_NI(1);
   if (need <= 2) SG_GEMV_NI(2);
-  if (need <= 4) SG_GEMV_NI(4);
-  SG_GEMV_NI(8);
+  SG_GEMV_NI(4);  // longer rows take several K blocks
 #undef SG_GEMV_NI
 }
 

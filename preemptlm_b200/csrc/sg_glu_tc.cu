@@ -612,6 +612,9 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       load_packed<BITS, DUAL>(sP + sp_i * C::P_BYTES + mat * C::P_MAT, r, part, pk);
+      // these generic-proxy reads must be ordered before the TMA (async
+      // proxy) that refills the slot once it is released
+      fence_async_smem();
       __syncwarp();
       if ((threadIdx.x & 31) == 0) mbar_arrive(&p_empty[sp_i]);
       if (++sp_i == C::SP) { sp_i = 0; pp ^= 1; }
@@ -641,6 +644,7 @@ __device__ __forceinline__ void dequant_role(const Args& args, const int* plan, 
           gs = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc));
           gb = bf16_to_f32(*reinterpret_cast<const uint16_t*>(sc + BM * 16));
           if ((kb & 7) == 7) {  // chunk done (group counts are multiples of 8 here)
+            fence_async_smem();  // as for the packed slots: reads before the refilling TMA
             __syncwarp();
             if ((threadIdx.x & 31) == 0) mbar_arrive(&s_empty[ss]);
             if (++ss == C::SS) { ss = 0; sph ^= 1; }

@@ -373,3 +373,48 @@ def test_layer_ragged_and_empty():
                                 LazyExperts(tens["experts"], 8), LazyExperts(tens["shared"], 8)[0],
                                 bits16(tens["shared_gate"]))
         assert_close(f32(out), ref["out"], what=f"T={T}")
+
+
+@pytest.mark.parametrize("H,I,bits", [(4096, 1024, 4), (2048, 1024, 4), (4096, 1024, 8)])
+def test_glu_prefill_tiles_every_element_and_repeatable(H, I, bits):
+    """128-wide pair tiles with several tiles per CTA (64 experts x 128 pairs):
+    every element of h against a plain fp32 torch reference of the same op
+    (dequantised weights, bf16 roundings of x_up, x_gate, sigmoid, silu and
+    the product), and four calls bit-identical.  Guards the ordering of the
+    dequantising warps' shared-memory reads of a packed stage before the TMA
+    that refills it."""
+    from preemptlm_b200.quant import dequantize_affine
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    E, T, k = 64, 1024, 8
+    cfg = LayerConfig("rep", 9, H, E, k, I, None, bits, E)
+    block, tens = make_layer(cfg, device=DEV)
+    arena = block.switch_mlp
+    x = make_tokens(cfg, T)
+    g = np.random.default_rng(5)
+    inds = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    d = ops.dispatch(torch.from_numpy(inds).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    xs = ops.permute_rows(x, d, k)
+    hs = [ops.glu_gate_up(arena, xs, d, k, _abi_flags("in|out")) for _ in range(4)]
+    for h in hs[1:]:
+        assert torch.equal(h, hs[0])
+    ex = tens["experts"]
+    off = d.group_off.cpu().numpy()
+    U = int(d.counts[0].item())
+
+    def bf(t):
+        return t.to(torch.bfloat16).float()
+
+    worst = 0.0
+    for u in range(U):
+        e = int(d.unique[u].item())
+        a, b = int(off[u]), int(off[u + 1])
+        w = {p: dequantize_affine(ex[f"{p}.weight"][e], ex[f"{p}.scales"][e], ex[f"{p}.biases"][e], bits).float()
+             for p in ("gate_proj", "up_proj")}
+        xr = xs[a:b].float()
+        gate, up = bf(xr @ w["gate_proj"].T), bf(xr @ w["up_proj"].T)
+        ref = bf(bf(gate * bf(torch.sigmoid(gate))) * up)
+        scale = ref.abs().amax(dim=1, keepdim=True).clamp_min(1.0)
+        worst = max(worst, float(((hs[0][a:b].float() - ref).abs() / scale).max()))
+    assert worst <= 2e-2, f"worst element error {worst:.3e} of its row's scale"
+    assert ops.device_status(reset=True) == 0
