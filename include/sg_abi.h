@@ -144,17 +144,26 @@ int sg_host_device_ptr(void* host, void** device);
  * every pair p of every group u < counts[0], against arena slot slot_ids[u];
  * pairs listed by perm/group_off (sg_dispatch layout); num_pairs = P (length
  * of perm, rows of y; x has ceil(P / pair_div) rows); y in pair order.
- * xs [P, H] and h [P, I] are caller-provided intermediate storage (xs is
- * written only when sg_glu_use_permute says so: the pairs' token rows are
- * first copied into dispatch order, so that every tile's rows load as one
- * TMA box; h is kept in dispatch order).  pair_div = k for routed experts.
- * grid_groups is a host-side upper bound on counts[0].
+ * scratch and h [P, I] are caller-provided intermediate storage.  scratch
+ * holds sg_glu_forward_scratch_bytes() bytes: the pairs' token rows copied
+ * into dispatch order for prefill-sized groups (every tile's rows then load
+ * as one TMA box), or the token rows' 8-bit pieces for the integer-operand
+ * gate/up of 8-bit arenas at decode sizes (see sg_quantize_pieces).  NULL is
+ * allowed when that size is 0, and also when only the pieces would go there
+ * (the dequantising gate/up then runs instead).  h is kept in dispatch order.
+ * pair_div = k for routed experts.  grid_groups is a host-side upper bound
+ * on counts[0].
  * Replaces `_gather_forward`, qwen3_x_moe.py:210-248 (the `mx.take` of the
  * arena, two `gather_mm` + `swiglu_activation`, the down `gather_mm`). */
 int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                    const int32_t* counts, const int32_t* slot_ids,
                    const int32_t* group_off, const int32_t* perm,
-                   int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y, void* stream);
+                   int grid_groups, void* scratch, uint16_t* h, uint16_t* y, void* stream);
+
+/* Bytes of the scratch area sg_glu_forward uses for this problem (0: none),
+ * or a negative status for invalid arguments.  Same arguments as
+ * sg_glu_forward.  No counterpart in the reference. */
+long long sg_glu_forward_scratch_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups);
 
 /* sg_glu_forward without caller scratch: h (and the permuted token rows when
  * sg_glu_use_permute returns 1) live in a fixed 32 MiB device-resident scratch
@@ -189,6 +198,34 @@ int sg_glu_gate_up(const sg_arena* arena, const uint16_t* x, int num_pairs, int 
                    const int32_t* group_off, const int32_t* perm,
                    int grid_groups, uint16_t* h, int flags, void* stream);
 
+/* sg_glu_gate_up with a caller work area of work_bytes bytes: with 8-bit
+ * arenas at decode tile widths, and work_bytes >= sg_glu_gate_up_work_bytes(),
+ * the token rows are split into 8-bit pieces in the work area and the
+ * integer-operand tcgen05 kernel computes h (never dequantising the
+ * weights: sum_g scale * (q . x)_g + bias * (sum x)_g per 64-group); any
+ * other case runs sg_glu_gate_up's kernels.  h agrees with the dequantising
+ * kernels within the layer tolerance (the pieces hold every token element
+ * to 2^-14 of its group's largest magnitude; the weights are exact).
+ * Same replacement as sg_glu_gate_up. */
+long long sg_glu_gate_up_work_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups,
+                                    int flags);
+int sg_glu_gate_up_work(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                        const int32_t* counts, const int32_t* slot_ids,
+                        const int32_t* group_off, const int32_t* perm,
+                        int grid_groups, uint16_t* h, int flags, void* work, long long work_bytes,
+                        void* stream);
+
+/* 8-bit pieces of rows x K bf16 values (K % 64 == 0), per 64-group g of a
+ * row: x[k] = E * (256 * hi[k] + lo[k]) with E = 2^e the group's scale,
+ * chosen so the largest |x| of the group is below 2^14 * E; hi in [-64, 64],
+ * lo in [-128, 127]; an element's integer is exact when it lies within 2^6
+ * of the group's largest magnitude, else rounded to nearest.  pieces
+ * [rows, 2, K] int8 (hi row, then lo row); ex [rows, K / 64, 2] fp32 (E, E *
+ * sum(256 hi + lo)).  order 1 stores every 8 elements in the order
+ * 0,2,4,6,1,3,5,7.  Finite inputs only.  No counterpart in the reference. */
+int sg_quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex,
+                       void* stream);
+
 /* y[., H] = bf16(h[., I] @ down^T) for every listed pair (num_pairs rows),
  * orders per `flags`.  Replaces the down `gather_mm` in `_gather_forward`,
  * qwen3_x_moe.py:243-248. */
@@ -211,8 +248,11 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
  * automatic (tcgen05 when the shape allows -- in-dim % 64, out-dim % 128,
  * <= 2048 groups -- and either the mean pairs per group is >= 2 or the
  * groups make at least one 128-row tile per SM; token rows permuted once the
- * mean reaches 32), 1 = streaming GEMV always, 2 = tcgen05 whenever the shape
- * allows, 3 = as 2 with the token rows always permuted.
+ * mean reaches 32, and for 8-bit arenas the integer-operand gate/up while
+ * the mean is <= 16 and the caller passes a work area), 1 = streaming GEMV
+ * always, 2 = the dequantising tcgen05 kernels whenever the shape allows,
+ * 3 = as 2 with the token rows always permuted, 4 = as 0 with the
+ * integer-operand gate/up wherever it applies.
  * Process-wide.  No counterpart in the reference (MLX picks
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);

@@ -315,7 +315,14 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
                   const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
 int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
                     cudaStream_t s);
-static int g_glu_path = 0;  // 0 auto, 1 streaming GEMV, 2 tcgen05, 3 tcgen05 over permuted rows
+bool i8_supported(const sg_arena* A, int grid_groups);
+int i8_glu_launch(const sg_arena* A, const int8_t* pieces, const float* ex, int in_rows, int pair_div, int in_by_pos,
+                  int out_by_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
+int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s);
+// 0 auto, 1 streaming GEMV, 2 tcgen05 (dequantising), 3 tcgen05 over permuted
+// rows, 4 tcgen05 with the integer-operand gate/up wherever it applies
+static int g_glu_path = 0;
 
 static int sm_count() {
   static int n = 0;
@@ -335,7 +342,7 @@ static int sm_count() {
 // tiles would leave most SMs idle.
 static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || !tc_supported(A, dual, grid_groups)) return false;
-  if (g_glu_path >= 2) return true;
+  if (g_glu_path == 2 || g_glu_path == 3) return true;
   const int out = dual ? A->inter : A->hidden;
   const long long tiles = (long long)grid_groups * (out / 128);
   return P >= 2 * grid_groups || tiles >= sm_count();
@@ -344,10 +351,30 @@ static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
 // Whether sg_glu_forward first copies the pairs' token rows into dispatch
 // order: worth it once a group's pairs fill 64-wide tiles (a contiguous
 // tile of rows then loads with one TMA box per stage).
+static bool use_i8(const sg_arena* A, int P, int grid_groups);
 static bool use_permute(const sg_arena* A, int P, int grid_groups) {
   if (!use_tc(A, true, P, grid_groups) || !use_tc(A, false, P, grid_groups)) return false;
+  if (use_i8(A, P, grid_groups)) return false;  // the integer-operand gate/up reads the rows in place
   if (g_glu_path == 3) return true;
   return P >= 32 * grid_groups;
+}
+
+// The integer-operand gate/up (8-bit arenas): in auto mode wherever the
+// tensor-core path runs with pair tiles of 16 (decode batches); it needs a
+// caller work area for the token rows' pieces.
+static bool use_i8(const sg_arena* A, int P, int grid_groups) {
+  if (g_glu_path == 1 || g_glu_path == 2 || g_glu_path == 3) return false;
+  if (grid_groups <= 0 || !i8_supported(A, grid_groups) || !tc_supported(A, true, grid_groups)) return false;
+  if (g_glu_path == 4) return true;
+  return (P + grid_groups - 1) / grid_groups <= 16;
+}
+
+// Work area of the pieces of in_rows token rows: [in_rows, 2, H] int8, then
+// (256-byte aligned) [in_rows, H / 64, 2] fp32.
+static size_t pieces_bytes(const sg_arena* A, int in_rows, size_t* ex_off) {
+  const size_t p = ((size_t)in_rows * 2 * A->hidden + 255) & ~size_t(255);
+  if (ex_off) *ex_off = p;
+  return p + (size_t)in_rows * (A->hidden / 64) * 8;
 }
 
 // xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
@@ -364,9 +391,21 @@ permute_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ 
 
 static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div, const int32_t* counts,
                     const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
-                    uint16_t* h, int flags, cudaStream_t s) {
+                    uint16_t* h, int flags, cudaStream_t s, void* work = nullptr, size_t work_bytes = 0) {
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
   const int div = in_pos ? 1 : pair_div;
+  if (work && use_i8(arena, num_pairs, grid_groups)) {
+    // token rows -> pieces (in the caller's work area), then the integer-operand kernel
+    const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
+    size_t ex_off = 0;
+    if (pieces_bytes(arena, in_rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
+    int8_t* pieces = static_cast<int8_t*>(work);
+    float* ex = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ex_off);
+    int st = quantize_pieces(x, in_rows, arena->hidden, 0, pieces, ex, s);
+    if (st) return st;
+    return i8_glu_launch(arena, pieces, ex, in_rows, div, in_pos, out_pos, counts, slot_ids, group_off, perm,
+                         grid_groups, h, s);
+  }
   if (use_tc(arena, true, num_pairs, grid_groups)) {
     const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
     return tc_glu_launch(arena, true, x, in_rows, div, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
@@ -404,7 +443,7 @@ static int check_glu_args(const sg_arena* arena, int num_pairs, int pair_div, in
 }  // namespace sg
 
 extern "C" int sg_set_glu_path(int mode) {
-  if (mode < 0 || mode > 3) return SG_ERR_INVALID_ARG;
+  if (mode < 0 || mode > 4) return SG_ERR_INVALID_ARG;
   sg::g_glu_path = mode;
   return SG_OK;
 }
@@ -449,7 +488,7 @@ extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pai
 
 extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                               const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                              const int32_t* perm, int grid_groups, uint16_t* xs, uint16_t* h, uint16_t* y,
+                              const int32_t* perm, int grid_groups, void* scratch, uint16_t* h, uint16_t* y,
                               void* stream) {
   int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
   if (st) return st;
@@ -457,17 +496,64 @@ extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_
   if (!x || !counts || !slot_ids || !group_off || !perm || !h || !y) return SG_ERR_INVALID_ARG;
   cudaStream_t s = (cudaStream_t)stream;
   const bool permute = sg::use_permute(arena, num_pairs, grid_groups);
+  uint16_t* xs = static_cast<uint16_t*>(scratch);
   if (permute) {
     if (!xs) return SG_ERR_INVALID_ARG;
     st = sg_permute_rows(x, perm, pair_div, num_pairs, arena->hidden, xs, stream);
     if (st) return st;
   }
-  // h in dispatch order, so that the down projection's rows are contiguous
+  // h in dispatch order, so that the down projection's rows are contiguous.
+  // Without a work area the integer-operand gate/up is not used.
+  const size_t work_bytes = permute || !scratch ? 0
+                            : sg::pieces_bytes(arena, (num_pairs + pair_div - 1) / pair_div, nullptr);
   st = sg::glu_dual(arena, permute ? xs : x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h,
-                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s);
+                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s, permute ? nullptr : scratch,
+                    work_bytes);
   if (st) return st;
   return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, SG_IN_DISPATCH_ORDER,
                         s);
+}
+
+extern "C" long long sg_glu_forward_scratch_bytes(const sg_arena* arena, int num_pairs, int pair_div,
+                                                  int grid_groups) {
+  const int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
+  if (st) return st;
+  if (num_pairs == 0 || grid_groups == 0) return 0;
+  if (sg::use_permute(arena, num_pairs, grid_groups)) return (long long)num_pairs * arena->hidden * 2;
+  if (sg::use_i8(arena, num_pairs, grid_groups))
+    return (long long)sg::pieces_bytes(arena, (num_pairs + pair_div - 1) / pair_div, nullptr);
+  return 0;
+}
+
+extern "C" long long sg_glu_gate_up_work_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups,
+                                               int flags) {
+  const int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, flags);
+  if (st) return st;
+  if (num_pairs == 0 || grid_groups == 0 || !sg::use_i8(arena, num_pairs, grid_groups)) return 0;
+  const int in_rows = (flags & SG_IN_DISPATCH_ORDER) ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
+  return (long long)sg::pieces_bytes(arena, in_rows, nullptr);
+}
+
+extern "C" int sg_glu_gate_up_work(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
+                                   const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                                   const int32_t* perm, int grid_groups, uint16_t* h, int flags, void* work,
+                                   long long work_bytes, void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, flags);
+  if (st) return st;
+  if (work_bytes < 0) return SG_ERR_INVALID_ARG;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!x || !counts || !slot_ids || !group_off || !perm || !h) return SG_ERR_INVALID_ARG;
+  return sg::glu_dual(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, flags,
+                      (cudaStream_t)stream, work_bytes > 0 ? work : nullptr, static_cast<size_t>(work_bytes));
+}
+
+extern "C" int sg_quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex,
+                                  void* stream) {
+  if (rows < 0 || (order != 0 && order != 1)) return SG_ERR_INVALID_ARG;
+  if (K < 64 || K % 64) return SG_ERR_SHAPE;
+  if (rows == 0) return SG_OK;
+  if (!x || !pieces || !ex) return SG_ERR_INVALID_ARG;
+  return sg::quantize_pieces(x, rows, K, order, pieces, ex, (cudaStream_t)stream);
 }
 
 extern "C" int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint16_t* h, uint16_t* y,
@@ -523,14 +609,16 @@ extern "C" int sg_glu_forward_noalloc(const sg_arena* arena, const uint16_t* x, 
   if (num_pairs == 0 || grid_groups == 0) return SG_OK;
   if (!x || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
   const size_t h_bytes = ((size_t)num_pairs * arena->inter * 2 + 255) & ~size_t(255);
-  const size_t xs_bytes =
-      sg::use_permute(arena, num_pairs, grid_groups) ? (size_t)num_pairs * arena->hidden * 2 : 0;
+  // the permuted token rows or the token rows' pieces, as sg_glu_forward uses them
+  const long long xs_need = sg_glu_forward_scratch_bytes(arena, num_pairs, pair_div, grid_groups);
+  if (xs_need < 0) return static_cast<int>(xs_need);
+  const size_t xs_bytes = static_cast<size_t>(xs_need);
   if (h_bytes + xs_bytes > sg::NOALLOC_SCRATCH_BYTES) return SG_ERR_CAPACITY;
   void* base = nullptr;
   st = sg::noalloc_scratch(&base);
   if (st) return st;
   uint16_t* h = static_cast<uint16_t*>(base);
-  uint16_t* xs = xs_bytes ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(base) + h_bytes) : nullptr;
+  void* xs = xs_bytes ? static_cast<void*>(static_cast<uint8_t*>(base) + h_bytes) : nullptr;
   return sg_glu_forward(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, xs, h, y,
                         stream);
 }

@@ -1,0 +1,670 @@
+// Integer-operand gathered gate/up for quantised arenas at decode tile widths
+// (a9, a10, a12).  Included by sg_glu_tc.cu: it shares that translation
+// unit's PTX helpers and device status word.
+//
+// The affine weights are never dequantised.  With w[m,k] = s[m,g] q[m,k] +
+// b[m,g] (g = k / 64),
+//
+//   sum_k w[m,k] x[n,k] = sum_g s[m,g] * (sum_{k in g} q[m,k] x[n,k])
+//                       + sum_g b[m,g] * (sum_{k in g} x[n,k]).
+//
+// The token rows are first split into 8-bit pieces per 64-group
+// (sg_quantize_pieces): x[n,k] = E[n,g] * (256 hi[n,k] + lo[n,k]), E a power
+// of two chosen so the group's largest |x| maps below 2^14 -- every element
+// within 2^6 of the group maximum is represented exactly, smaller ones to
+// 2^-14 of the maximum.  The tensor cores then multiply the raw unsigned
+// 8-bit weights (the arena's q8 rows, loaded by TMA straight into the MMA
+// operand layout) with the signed pieces (tcgen05.mma kind::i8, exact int32
+// accumulation), one TMEM accumulator per 64-group: D[m, j] = sum q hi and
+// D[m, BN + j] = sum q lo for the tile's BN pairs j.  The epilogue warps fold
+// each group: y[m,j] += s[m,g] * (E[j,g] * float(256 D_hi + D_lo)) +
+// b[m,g] * X[j,g], X = E * sum(256 hi + lo), and finish with SwiGLU.
+//
+// Warp roles (11 warps, one CTA per SM, persistent over the tile list of the
+// dequantising kernel):
+//   w0      TMA producer: 128 rows x 128 bytes of gate and of up per stage
+//           (K = 128), and the tiles' scale/bias chunks (8 groups x 128 rows)
+//   w1      TMEM allocation + single-thread tcgen05.mma issue: two K = 32
+//           MMAs per matrix per group into a ring of 8 group accumulators
+//   w2      B producer: the pairs' hi/lo piece rows by 16-byte cp.async into
+//           the SW128 operand layout; per tile, the pairs' (E, X) table
+//   w3-w10  epilogue: warp (quadrant, matrix) folds its 32 rows of one matrix,
+//           the up warps hand their sums to the gate warps through shared
+//           memory, the gate warps write h = swiglu(gate, up) in bf16
+//
+// Every wait is bounded as in the dequantising kernel; on expiry the CTA
+// records SG_ERR_TIMEOUT, drains its copies, frees TMEM and returns.
+#pragma once
+
+namespace sg {
+namespace i8 {
+
+using namespace tc;
+
+constexpr int KS = 128;         // K per pipeline stage: one 128-byte swizzle atom of 8-bit operands
+constexpr int GSZ = 64;         // quantisation group
+constexpr int RING = 8;         // group accumulators in tensor memory
+constexpr int PIECE_BITS = 14;  // the group maximum maps below 2^PIECE_BITS
+
+// ------------------------------------------------------------------ pieces
+// Element value of a bf16 as a signed integer scaled so that biased exponent
+// eM (the group maximum's) maps the leading bit to 2^(PIECE_BITS - 1):
+//   |v| = m8 * 2^(ex - eM + PIECE_BITS - 8), m8 the 8-bit significand,
+// rounded to nearest (ties away from zero) when the shift is negative.
+__device__ __forceinline__ int piece_value(uint32_t b16, int eM) {
+  const int ex = (b16 >> 7) & 0xFF;
+  int m = b16 & 0x7F;
+  int e = ex;
+  if (ex == 0) {
+    e = 1;  // subnormal: no implicit bit
+  } else {
+    m |= 0x80;
+  }
+  const int sh = e - eM + (PIECE_BITS - 8);
+  int v;
+  if (sh >= 0) v = m << sh;
+  else if (sh > -31) v = (m + (1 << (-sh - 1))) >> (-sh);
+  else v = 0;
+  return (b16 & 0x8000u) ? -v : v;
+}
+
+// One thread per 8 elements, 8 threads per 64-group.  ORDER 0: pieces in k
+// order; ORDER 1 (4-bit arenas): within every 8 elements the order
+// 0, 2, 4, 6, 1, 3, 5, 7, the order of the unpacked nibbles.
+__global__ void __launch_bounds__(256)
+quantize_pieces_kernel(const uint16_t* __restrict__ x, int rows, int K, int order, int8_t* __restrict__ pieces,
+                       float* __restrict__ ex) {
+  const int G = K / GSZ;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // chunk of 8 elements
+  const long long nchunks = (long long)rows * (K / 8);
+  const bool live = t < nchunks;
+  const long long ci = live ? t : 0;
+  const int row = static_cast<int>(ci / (K / 8));
+  const int c = static_cast<int>(ci - (long long)row * (K / 8));  // chunk within the row
+  const uint4 v = live ? ldg_nc_v4(x + (size_t)row * K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t b[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    b[2 * i] = w[i] & 0xFFFFu;
+    b[2 * i + 1] = w[i] >> 16;
+  }
+  // largest biased exponent among the group's nonzero elements (the maximum
+  // magnitude's exponent); the 8 threads of a group are 8 consecutive lanes
+  int eM = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = (b[i] >> 7) & 0xFF;
+    eM = max(eM, (b[i] & 0x7FFFu) ? max(e, 1) : 0);
+  }
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) eM = max(eM, __shfl_xor_sync(0xffffffffu, eM, off));
+  int iv[8];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    iv[i] = piece_value(b[i], eM);
+    sum += iv[i];
+  }
+  uint32_t hi[2] = {0, 0}, lo[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int src = order ? ((i & 3) * 2 + (i >> 2)) : i;  // element placed at position i
+    const int h = (iv[src] + 128) >> 8;                    // arithmetic shift: floor
+    const int l = iv[src] - 256 * h;                       // [-128, 127]
+    hi[i >> 2] |= (static_cast<uint32_t>(h) & 0xFFu) << (8 * (i & 3));
+    lo[i >> 2] |= (static_cast<uint32_t>(l) & 0xFFu) << (8 * (i & 3));
+  }
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (!live) return;
+  int8_t* prow = pieces + (size_t)row * 2 * K;
+  *reinterpret_cast<uint2*>(prow + (size_t)c * 8) = make_uint2(hi[0], hi[1]);
+  *reinterpret_cast<uint2*>(prow + K + (size_t)c * 8) = make_uint2(lo[0], lo[1]);
+  if ((c & 7) == 0) {
+    // E = 2^(eM - 127 - (PIECE_BITS - 1)): a normal or subnormal power of two
+    const int e2 = eM - 127 - (PIECE_BITS - 1);
+    const float E = e2 >= -126 ? __uint_as_float(static_cast<uint32_t>(e2 + 127) << 23)
+                               : __uint_as_float(1u << (e2 + 149));
+    float* o = ex + ((size_t)row * G + c / 8) * 2;
+    o[0] = E;
+    o[1] = static_cast<float>(sum) * E;
+  }
+}
+
+// ------------------------------------------------------------------ kernel configuration
+template <int BN>
+struct Cfg {
+  static constexpr int NB = 2 * BN;                  // B rows: the pairs' hi pieces, then their lo pieces
+  static constexpr int A_MAT = BM * KS;              // one matrix's stage: 128 rows x 128 bytes (16 KB)
+  static constexpr int A_BYTES = 2 * A_MAT;          // gate and up
+  static constexpr int B_BYTES = NB * KS;            // 2 BN rows x 128 bytes
+  static constexpr int SA = 4;
+  static constexpr int SB = 6;
+  static constexpr int SS = 3;
+  static constexpr int S_BYTES = 2 * 2 * BM * 16;    // [matrix][scales, biases][128 rows][8 groups] bf16
+  static constexpr int GMAX = 64;                    // groups per row (K <= 4096)
+  static constexpr int T_BYTES = GMAX * 2 * BN * 4;  // pair table: [group][E, X][BN] fp32
+  static constexpr int X_STRIDE = BN + 4;            // hand-off rows: BN fp32 + padding
+  static constexpr int X_BYTES = BM * X_STRIDE * 4;
+  static constexpr int ACC_COLS = 2 * NB;            // one group: gate and up, NB columns each
+  static constexpr int TMEM_COLS = RING * ACC_COLS;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + SA * A_BYTES;
+  static constexpr int OFF_S = OFF_B + SB * B_BYTES;
+  static constexpr int OFF_T = OFF_S + SS * S_BYTES;
+  static constexpr int OFF_X = OFF_T + 2 * T_BYTES;
+  static constexpr int OFF_PLAN = OFF_X + 2 * X_BYTES;
+  static constexpr int OFF_BAR = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
+  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * RING + 2 * SS + 2 * 2 + 2 * 2;
+  static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+  static constexpr int EPI_WARP0 = 3;
+  static constexpr int THREADS = (EPI_WARP0 + 8) * 32;
+  static_assert(TMEM_COLS <= 512, "tensor memory budget");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(B_BYTES % 1024 == 0, "B stages keep 1024-byte alignment");
+};
+
+// Instruction descriptor, kind::i8: D s32, A unsigned 8-bit (the raw weights),
+// B signed 8-bit (the pieces), both K-major, M = 128, N = NB.
+template <int NB>
+__device__ __forceinline__ uint32_t idesc_i8() {
+  return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NB >> 3) << 17) |
+         (static_cast<uint32_t>(BM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+struct Args {
+  int num_slots, K, OUT;
+  const int8_t* pieces;  // [in_rows, 2, K]: hi then lo pieces of every input row
+  const float* ex;       // [in_rows, K / 64, 2]: (E, X) per group
+  int in_rows;
+  const int32_t* counts;
+  const int32_t* slot_ids;
+  const int32_t* group_off;
+  const int32_t* perm;
+  int pair_div;    // input row of pair position pos: perm[pos] / pair_div, or pos when in_by_pos
+  int in_by_pos;
+  int out_by_pos;  // output row: pos, or perm[pos]
+  int max_groups;
+  uint16_t* out;
+};
+
+// Tile t of the flat list: weight-row tile m, group u (the largest u with
+// plan[u] <= n-tile index), its first pair n0 and valid pair count.
+struct ITile {
+  int u, m, n0, nvalid, slot, goff;
+};
+template <int BN>
+__device__ __forceinline__ ITile itile_of(int t, const int* plan, int U, int NT, const Args& a) {
+  ITile tl;
+  tl.m = t / NT;
+  const int fn = t - tl.m * NT;
+  int lo = 0, hi = U;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (plan[mid] <= fn) lo = mid;
+    else hi = mid;
+  }
+  tl.u = lo;
+  tl.n0 = (fn - plan[lo]) * BN;
+  tl.goff = a.group_off[lo];
+  tl.nvalid = min(BN, a.group_off[lo + 1] - tl.goff - tl.n0);
+  tl.slot = a.slot_ids[lo];
+  return tl;
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
+glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+              const __grid_constant__ CUtensorMap tmS0, const __grid_constant__ CUtensorMap tmQ0,
+              const __grid_constant__ CUtensorMap tmS1, const __grid_constant__ CUtensorMap tmQ1, const Args args) {
+  using C = Cfg<BN>;
+  constexpr int NB = C::NB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sA = smem + C::OFF_A;
+  uint8_t* sB = smem + C::OFF_B;
+  uint8_t* sS = smem + C::OFF_S;
+  float* sT = reinterpret_cast<float*>(smem + C::OFF_T);
+  float* sX = reinterpret_cast<float*>(smem + C::OFF_X);
+  int* plan = reinterpret_cast<int*>(smem + C::OFF_PLAN);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* a_full = bars;                   // [SA] weight stage landed (TMA tx)
+  uint64_t* a_empty = a_full + C::SA;        // [SA] weight stage consumed (MMA commit)
+  uint64_t* b_full = a_empty + C::SA;        // [SB] piece rows landed (32 cp.async arrivals)
+  uint64_t* b_empty = b_full + C::SB;        // [SB] piece rows consumed (MMA commit)
+  uint64_t* acc_full = b_empty + C::SB;      // [RING] group accumulator ready (MMA commit)
+  uint64_t* acc_empty = acc_full + RING;     // [RING] group accumulator read (8 epilogue warps)
+  uint64_t* s_full = acc_empty + RING;       // [SS] scale/bias chunk landed (TMA tx)
+  uint64_t* s_empty = s_full + C::SS;        // [SS] scale/bias chunk read (8 epilogue warps)
+  uint64_t* t_full = s_empty + C::SS;        // [2] pair table written (32 producer lanes)
+  uint64_t* t_empty = t_full + 2;            // [2] pair table read (8 epilogue warps)
+  uint64_t* x_full = t_empty + 2;            // [2] up sums handed over (128 up threads)
+  uint64_t* x_empty = x_full + 2;            // [2] up sums taken (128 gate threads)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Ctl ctl{abort_flag};
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = args.K;
+  const int NKS = K / KS;
+  const int G = K / GSZ;
+  const int MT = args.OUT / BM;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::SA; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < C::SB; ++i) {
+      mbar_init(&b_full[i], 32);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    for (int i = 0; i < C::SS; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 8);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&t_full[i], 32);
+      mbar_init(&t_empty[i], 8);
+      mbar_init(&x_full[i], 128);
+      mbar_init(&x_empty[i], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // tile plan: plan[u] = first flat n-tile of group u (prefix of ceil(count / BN))
+  const int U = min(args.counts[0], args.max_groups);
+  for (int u = threadIdx.x; u < U; u += blockDim.x)
+    plan[u + 1] = (args.group_off[u + 1] - args.group_off[u] + BN - 1) / BN;
+  if (threadIdx.x == 0) plan[0] = 0;
+  __syncthreads();
+  if (warp == 0) {  // inclusive scan of plan[1..U] by one warp, in 32-entry blocks
+    int carry = 0;
+    for (int base = 1; base <= U; base += 32) {
+      const int i = base + lane;
+      int v = i <= U ? plan[i] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+      }
+      if (i <= U) plan[i] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int NT = plan[U];
+  const int total = NT * MT;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- weight + scale producer
+    if (lane == 0) {
+      int sa = 0, ss = 0, issued = 0, s_issued = 0;
+      uint32_t pa = 0, sph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const ITile tl = itile_of<BN>(t, plan, U, NT, args);
+        // a slot outside the arena gives negative or out-of-range rows: the
+        // TMA's zero fill (the epilogue writes zeros for such tiles)
+        const int row0 = (tl.slot >= 0 && tl.slot < args.num_slots) ? tl.slot * args.OUT + tl.m * BM : -BM;
+        for (int ks = 0; ks < NKS && ok; ++ks) {
+          if ((ks & 3) == 0) {  // scales and biases of groups [2 ks, 2 ks + 8) of the tile's rows
+            ok = wait_bar(&s_empty[ss], sph ^ 1, ctl, BACKOFF_NS);
+            if (!ok) break;
+            uint8_t* dst = sS + ss * C::S_BYTES;
+            mbar_expect_tx(&s_full[ss], C::S_BYTES);
+            tma_load_2d(dst, &tmS0, 2 * ks, row0, &s_full[ss]);
+            tma_load_2d(dst + BM * 16, &tmQ0, 2 * ks, row0, &s_full[ss]);
+            tma_load_2d(dst + 2 * BM * 16, &tmS1, 2 * ks, row0, &s_full[ss]);
+            tma_load_2d(dst + 3 * BM * 16, &tmQ1, 2 * ks, row0, &s_full[ss]);
+            ++s_issued;
+            if (++ss == C::SS) { ss = 0; sph ^= 1; }
+          }
+          ok = wait_bar(&a_empty[sa], pa ^ 1, ctl, BACKOFF_NS);
+          if (!ok) break;
+          mbar_expect_tx(&a_full[sa], C::A_BYTES);
+          tma_load_2d(sA + sa * C::A_BYTES, &tmA0, ks * 32, row0, &a_full[sa]);
+          tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, ks * 32, row0, &a_full[sa]);
+          ++issued;
+          if (++sa == C::SA) { sa = 0; pa ^= 1; }
+        }
+      }
+      if (!ok) {  // drain this thread's copies still in flight (bounded)
+        for (int i = 0; i < min(issued, C::SA); ++i) {
+          int s = sa - 1 - i;
+          uint32_t p = pa;
+          if (s < 0) { s += C::SA; p ^= 1; }
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&a_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
+          }
+        }
+        for (int i = 0; i < min(s_issued, C::SS); ++i) {
+          int s = ss - 1 - i;
+          uint32_t p = sph;
+          if (s < 0) { s += C::SS; p ^= 1; }
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&s_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8<NB>();
+      int sa = 0, sb = 0, gc = 0;
+      uint32_t pa = 0, pb = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        for (int ks = 0; ks < NKS && ok; ++ks) {
+          ok = wait_bar(&b_full[sb], pb, ctl) && wait_bar(&a_full[sa], pa, ctl);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t ad0 = desc_sw128(smem_u32(sA + sa * C::A_BYTES));
+          const uint64_t ad1 = desc_sw128(smem_u32(sA + sa * C::A_BYTES + C::A_MAT));
+          const uint64_t bd = desc_sw128(smem_u32(sB + sb * C::B_BYTES));
+#pragma unroll
+          for (int gi = 0; gi < KS / GSZ; ++gi) {
+            const int slot = gc % RING;
+            ok = wait_bar(&acc_empty[slot], ((gc / RING) & 1) ^ 1, ctl);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t d = tmem + slot * C::ACC_COLS;
+#pragma unroll
+            for (int kk = 0; kk < GSZ / 32; ++kk) {
+              // K step of 32 one-byte elements = 32 bytes: +2 in the descriptor's address field
+              const uint32_t ko = static_cast<uint32_t>((gi * GSZ + kk * 32) >> 4);
+              umma_i8(d, ad0 + ko, bd + ko, idesc, kk);
+              umma_i8(d + NB, ad1 + ko, bd + ko, idesc, kk);
+            }
+            umma_commit(&acc_full[slot]);
+            ++gc;
+          }
+          if (!ok) break;
+          umma_commit(&a_empty[sa]);
+          if (++sa == C::SA) { sa = 0; pa ^= 1; }
+          umma_commit(&b_empty[sb]);
+          if (++sb == C::SB) { sb = 0; pb ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- piece rows + pair table
+    // lane l copies chunk l % 8 of B rows l / 8 + 4 i (i = 0..7): pair
+    // (l / 8 + 4 i) % BN, plane (hi / lo) (l / 8 + 4 i) / BN
+    static_assert(BN == 16, "the row split below assumes 16 pairs per tile");
+    const int c = lane & 7, r0 = lane >> 3;
+    const size_t prow_bytes = static_cast<size_t>(2) * K;
+    int sb = 0, it = 0;
+    uint32_t pb = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+      const ITile tl = itile_of<BN>(t, plan, U, NT, args);
+      // input row of pair j (lane j < BN), -1 past the tile's pairs
+      int myrow = -1;
+      if (lane < BN && lane < tl.nvalid) {
+        const int pos = tl.goff + tl.n0 + lane;
+        const int rw = args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
+        myrow = (rw >= 0 && rw < args.in_rows) ? rw : -1;
+      }
+      int row[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) row[q] = __shfl_sync(0xffffffffu, myrow, r0 + 4 * q);
+      // the pairs' (E, X) per group, transposed to [group][E, X][pair]
+      const int buf = it & 1;
+      ok = wait_bar(&t_empty[buf], ((it >> 1) & 1) ^ 1, ctl, BACKOFF_NS);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      float* tp = sT + buf * (C::T_BYTES / 4);
+      for (int idx = lane; idx < BN * G; idx += 32) {
+        const int j = idx % BN, g = idx / BN;
+        const int rw = __shfl_sync(0xffffffffu, myrow, j);
+        float2 v = make_float2(0.f, 0.f);
+        if (rw >= 0) v = *reinterpret_cast<const float2*>(args.ex + ((size_t)rw * G + g) * 2);
+        tp[g * 2 * BN + j] = v.x;
+        tp[g * 2 * BN + BN + j] = v.y;
+      }
+      mbar_arrive(&t_full[buf]);
+      for (int ks = 0; ks < NKS; ++ks) {
+        ok = wait_bar(&b_empty[sb], pb ^ 1, ctl, BACKOFF_NS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        uint8_t* dst = sB + sb * C::B_BYTES;
+        const int8_t* col = args.pieces + ks * KS + c * 16;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = r0 + 4 * i;  // B row: pair rr % BN, plane rr / BN
+          const int rw = row[i & 3];
+          const bool v = rw >= 0;
+          cp_async16(dst + rr * KS + ((c ^ (rr & 7)) << 4),
+                     v ? col + rw * prow_bytes + (i >= 4 ? K : 0) : args.pieces, v ? 16u : 0u);
+        }
+        cp_async_arrive(&b_full[sb]);
+        if (++sb == C::SB) { sb = 0; pb ^= 1; }
+      }
+    }
+    cp_async_wait_all();  // no copy of this warp outlives the kernel
+  } else {
+    // ---------------------------------------------------------------- epilogue: 8 warps, (quadrant, matrix)
+    const int quad = warp & 3;
+    const int mat = (warp - C::EPI_WARP0) >> 2;  // 0 gate, 1 up
+    const int r = quad * 32 + lane;              // weight row within the tile, TMEM lane
+    int ss = 0, gc = 0, it = 0;
+    uint32_t sph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+      const ITile tl = itile_of<BN>(t, plan, U, NT, args);
+      const int buf = it & 1;
+      const uint32_t bph = (it >> 1) & 1;
+      ok = wait_bar(&t_full[buf], bph, ctl, BACKOFF_NS);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const float* tp = sT + buf * (C::T_BYTES / 4);
+      const int nq = (tl.nvalid + 3) >> 2;  // 4-pair chunks holding valid pairs (warp-uniform)
+      float y[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) y[j] = 0.0f;
+      for (int g8 = 0; g8 < G && ok; g8 += 8) {
+        ok = wait_bar(&s_full[ss], sph, ctl, BACKOFF_NS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const uint8_t* sc = sS + ss * C::S_BYTES + mat * (2 * BM * 16) + r * 16;
+        const uint4 sv = *reinterpret_cast<const uint4*>(sc);
+        const uint4 bv = *reinterpret_cast<const uint4*>(sc + BM * 16);
+        // generic reads of the chunk before the TMA (async proxy) refills it
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[ss]);
+        if (++ss == C::SS) { ss = 0; sph ^= 1; }
+        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) {
+          const int slot = gc % RING;
+          ok = wait_bar(&acc_full[slot], (gc / RING) & 1, ctl);
+          ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t a[32];
+          tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + slot * C::ACC_COLS + mat * NB, a);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[slot]);
+          ++gc;
+          const float s = (gi & 1) ? hi_bf16(sw[gi >> 1]) : lo_bf16(sw[gi >> 1]);
+          const float b = (gi & 1) ? hi_bf16(bw[gi >> 1]) : lo_bf16(bw[gi >> 1]);
+          const float* e = tp + (g8 + gi) * 2 * BN;
+#pragma unroll
+          for (int q = 0; q < BN / 4; ++q) {
+            if (q < nq) {
+              const float4 e4 = *reinterpret_cast<const float4*>(e + 4 * q);
+              const float4 x4 = *reinterpret_cast<const float4*>(e + BN + 4 * q);
+              const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int j = 4 * q + jj;
+                // 256 * sum(q hi) + sum(q lo): |.| < 2^28, exact in int32
+                const int qi = static_cast<int>(a[j]) * 256 + static_cast<int>(a[BN + j]);
+                const float f = __int2float_rn(qi) * ev[jj];
+                y[j] = fmaf(b, xv[jj], fmaf(f, s, y[j]));
+              }
+            }
+          }
+        }
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t_empty[buf]);
+      // hand-off: the up warps pass their sums to the gate warps of the quadrant
+      float* xr = sX + buf * (C::X_BYTES / 4) + r * C::X_STRIDE;
+      if (mat == 1) {
+        ok = wait_bar(&x_empty[buf], bph ^ 1, ctl, BACKOFF_NS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+#pragma unroll
+        for (int q = 0; q < BN / 4; ++q)
+          *reinterpret_cast<float4*>(xr + 4 * q) = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        mbar_arrive(&x_full[buf]);
+      } else {
+        ok = wait_bar(&x_full[buf], bph, ctl, BACKOFF_NS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        float u[BN];
+#pragma unroll
+        for (int q = 0; q < BN / 4; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + 4 * q);
+          u[4 * q] = v.x; u[4 * q + 1] = v.y; u[4 * q + 2] = v.z; u[4 * q + 3] = v.w;
+        }
+        mbar_arrive(&x_empty[buf]);
+        const bool slot_ok = tl.slot >= 0 && tl.slot < args.num_slots;
+        int my_row = 0;  // output row of pair `lane`, broadcast by shuffle
+        if (lane < tl.nvalid) {
+          const int pos = tl.goff + tl.n0 + lane;
+          my_row = args.out_by_pos ? pos : args.perm[pos];
+        }
+        const int ocol = tl.m * BM + r;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int orow = __shfl_sync(0xffffffffu, my_row, j);
+          if (j < tl.nvalid)
+            args.out[(size_t)orow * args.OUT + ocol] = slot_ok ? swiglu_bf16(y[j], u[j]) : 0;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------ host side
+// Whether the integer-operand gate/up serves this arena: 8-bit affine weights,
+// K a multiple of 128 with at most 64 groups (whole scale chunks of 8 groups),
+// 128-row output tiles.
+static bool supported(const sg_arena* A, int grid_groups) {
+  const int K = A->hidden, OUT = A->inter;
+  return A->bits == 8 && A->group_size == GSZ && K % KS == 0 && (K / GSZ) % 8 == 0 && K / GSZ <= Cfg<16>::GMAX &&
+         OUT % BM == 0 && grid_groups <= PLAN_MAX_GROUPS;
+}
+
+static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
+  constexpr int BN = 16;
+  using C = Cfg<BN>;
+  const int K = args.K;
+  const uint64_t rows_total = (uint64_t)A->num_slots * args.OUT;
+  const uint64_t words = (uint64_t)K / 4;
+  const uint64_t groups = (uint64_t)K / GSZ;
+  CUtensorMap m0, m1, ms0, mq0, ms1, mq1;
+  const bool ok =
+      make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, A->gate_w, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, A->up_w, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      make_map(&ms0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->gate_s, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&mq0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->gate_b, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&ms1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->up_s, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&mq1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->up_b, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return SG_ERR_CUDA;
+  static bool attr_done[64] = {};  // per device
+  int dev = 0;
+  SG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
+  if (!attr_done[dev]) {
+    SG_CUDA_TRY(cudaFuncSetAttribute(glu_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_done[dev] = true;
+  }
+  glu_i8_kernel<BN><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, ms0, mq0, ms1, mq1, args);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+}  // namespace i8
+
+// Pieces of `rows` rows of K bf16 values (see sg_quantize_pieces).
+int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s) {
+  if (rows == 0) return SG_OK;
+  const long long chunks = (long long)rows * (K / 8);
+  const long long blocks = (chunks + 255) / 256;
+  if (blocks > 0x7FFFFFFFLL) return SG_ERR_SHAPE;
+  i8::quantize_pieces_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, K, order, pieces, ex);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+bool i8_supported(const sg_arena* A, int grid_groups) { return i8::supported(A, grid_groups); }
+
+int i8_glu_launch(const sg_arena* A, const int8_t* pieces, const float* ex, int in_rows, int pair_div, int in_by_pos,
+                  int out_by_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s) {
+  i8::Args a;
+  a.num_slots = A->num_slots;
+  a.K = A->hidden;
+  a.OUT = A->inter;
+  a.pieces = pieces;
+  a.ex = ex;
+  a.in_rows = in_rows;
+  a.counts = counts;
+  a.slot_ids = slot_ids;
+  a.group_off = group_off;
+  a.perm = perm;
+  a.pair_div = pair_div;
+  a.in_by_pos = in_by_pos;
+  a.out_by_pos = out_by_pos;
+  a.max_groups = grid_groups;
+  a.out = out;
+  return i8::launch(A, a, s);
+}
+
+}  // namespace sg

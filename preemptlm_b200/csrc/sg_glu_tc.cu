@@ -1372,6 +1372,9 @@ int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, 
 
 }  // namespace sg
 
+// the integer-operand gate/up kernel shares this unit's helpers and status word
+#include "sg_glu_i8.cuh"
+
 namespace sg {
 int ep_device_status(int reset);  // the expert-parallel exchange kernels' word (sg_ep.cu)
 }

@@ -165,12 +165,38 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int =
     h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
     if P == 0:
         return h
-    LAUNCHES[0] += 1
     lib = _abi.load()
-    _abi.check(lib.sg_glu_gate_up(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
+    desc = ctypes.byref(arena.desc())
+    nwork = lib.sg_glu_gate_up_work_bytes(desc, P, int(pair_div), d.grid_groups, int(flags))
+    if nwork < 0:
+        _abi.check(int(nwork), "sg_glu_gate_up_work_bytes")
+    if nwork > 0:  # 8-bit arena at decode sizes: the token rows' pieces, then the integer-operand kernel
+        work = torch.empty(int(nwork), dtype=torch.uint8, device=x.device)
+        LAUNCHES[0] += 2
+        _abi.check(lib.sg_glu_gate_up_work(desc, x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
+                                           d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(),
+                                           d.grid_groups, h.data_ptr(), int(flags), work.data_ptr(), int(nwork),
+                                           _stream()), "sg_glu_gate_up_work")
+        return h
+    LAUNCHES[0] += 1
+    _abi.check(lib.sg_glu_gate_up(desc, x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                   d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                   h.data_ptr(), int(flags), _stream()), "sg_glu_gate_up")
     return h
+
+
+def quantize_pieces(x: torch.Tensor, order: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """8-bit pieces of the rows of x (``sg_quantize_pieces``): (pieces int8
+    [rows, 2, K], ex fp32 [rows, K // 64, 2])."""
+    x = _bf16_2d(x, "x")
+    rows, K = x.shape
+    pieces = torch.empty((rows, 2, K), dtype=torch.int8, device=x.device)
+    ex = torch.empty((rows, K // 64, 2), dtype=torch.float32, device=x.device)
+    if rows:
+        LAUNCHES[0] += 1
+        _abi.call("sg_quantize_pieces", x.data_ptr(), rows, K, int(order), pieces.data_ptr(), ex.data_ptr(),
+                  _stream())
+    return pieces, ex
 
 
 def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -219,10 +245,14 @@ def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: d
         if P == 0:
             return y
         h = torch.empty((P, arena.inter), dtype=torch.bfloat16, device=x.device)
-        permute = lib.sg_glu_use_permute(ctypes.byref(arena.desc()), P, d.grid_groups) == 1
-        xs = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device) if permute else None
-        LAUNCHES[0] += 3 if permute else 2
-        _abi.check(lib.sg_glu_forward(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
+        desc = ctypes.byref(arena.desc())
+        nscratch = lib.sg_glu_forward_scratch_bytes(desc, P, int(pair_div), d.grid_groups)
+        if nscratch < 0:
+            _abi.check(int(nscratch), "sg_glu_forward_scratch_bytes")
+        # the permuted token rows, or the token rows' pieces: one launch more either way
+        xs = torch.empty(int(nscratch), dtype=torch.uint8, device=x.device) if nscratch > 0 else None
+        LAUNCHES[0] += 3 if xs is not None else 2
+        _abi.check(lib.sg_glu_forward(desc, x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                       d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                       None if xs is None else xs.data_ptr(), h.data_ptr(), y.data_ptr(), _stream()),
                    "sg_glu_forward")
@@ -249,7 +279,8 @@ def gather_forward_noalloc(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -
     y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device)
     if P == 0:
         return y
-    LAUNCHES[0] += 2
+    nscratch = _abi.load().sg_glu_forward_scratch_bytes(ctypes.byref(arena.desc()), P, int(pair_div), d.grid_groups)
+    LAUNCHES[0] += 3 if nscratch > 0 else 2
     _abi.check(_abi.load().sg_glu_forward_noalloc(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div),
                                                   d.counts.data_ptr(), d.slot_ids.data_ptr(), d.group_off.data_ptr(),
                                                   d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),
@@ -278,7 +309,7 @@ def dense_glu(arena, x: torch.Tensor, sid: int = 0) -> torch.Tensor | None:
     return y
 
 
-GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2, "tc-perm": 3}
+GLU_PATHS = {"auto": 0, "gemv": 1, "tc": 2, "tc-perm": 3, "i8": 4}
 
 
 _GLU_PATH = ["auto"]
@@ -286,7 +317,9 @@ _GLU_PATH = ["auto"]
 
 def set_glu_path(mode: str) -> None:
     """Pick the gathered-GLU kernel: "auto", "gemv" (streaming CUDA-core
-    GEMV) or "tc" (tcgen05 tensor cores)."""
+    GEMV), "tc" (dequantising tcgen05 kernels), "tc-perm" (as "tc" with the
+    token rows permuted) or "i8" (the integer-operand tcgen05 gate/up for
+    8-bit arenas wherever it applies)."""
     _abi.call("sg_set_glu_path", GLU_PATHS[mode])
     _GLU_PATH[0] = mode
 

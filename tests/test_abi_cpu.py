@@ -73,7 +73,26 @@ def test_host_side_argument_checks(lib):
                               None) == _abi.SG_OK  # empty
     assert lib.sg_permute_rows(1, 1, 1, 4, 12, 1, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_permute_rows(1, 1, 0, 4, 16, 1, None) == _abi.SG_ERR_INVALID_ARG
-    assert lib.sg_set_glu_path(4) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_set_glu_path(5) == _abi.SG_ERR_INVALID_ARG
+    # integer-operand gate/up: work sizes and argument checks (no GPU touched)
+    assert lib.sg_quantize_pieces(1, 2, 100, 0, 1, 1, None) == _abi.SG_ERR_SHAPE
+    assert lib.sg_quantize_pieces(1, 2, 128, 2, 1, 1, None) == _abi.SG_ERR_INVALID_ARG
+    assert lib.sg_quantize_pieces(None, 0, 128, 0, None, None, None) == _abi.SG_OK
+    q8 = _abi.sg_arena(num_slots=512, hidden=2048, inter=512, bits=8, group_size=64, gate_w=1, gate_s=1, gate_b=1,
+                       up_w=1, up_s=1, up_b=1, down_w=1, down_s=1, down_b=1)
+    # decode: 256 tokens x top-10 over 512 groups (mean 5 pairs): the pieces of the 256 token rows
+    pieces = 256 * 2 * 2048 + 256 * 32 * 8
+    assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == pieces
+    assert lib.sg_glu_forward_scratch_bytes(ctypes.byref(q8), 2560, 10, 512) == pieces
+    # prefill-sized groups: the permuted token rows instead
+    assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 81920, 10, 512, 0) == 0
+    assert lib.sg_glu_forward_scratch_bytes(ctypes.byref(q8), 81920, 10, 512) == 81920 * 2048 * 2
+    for mode, want in ((2, 0), (1, 0), (4, pieces)):
+        assert lib.sg_set_glu_path(mode) == _abi.SG_OK
+        assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == want
+    assert lib.sg_set_glu_path(0) == _abi.SG_OK
+    q8.bits = 4  # 4-bit arenas keep the dequantising kernels
+    assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == 0
     # expert-parallel exchange: argument checks and the region layout (no GPU touched)
     assert lib.sg_ep_region_bytes(9, 16, 256) == _abi.SG_ERR_INVALID_ARG  # more than 8 ranks
     assert lib.sg_ep_region_bytes(2, 16, 100) == _abi.SG_ERR_SHAPE        # H % 8
