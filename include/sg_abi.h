@@ -147,10 +147,11 @@ int sg_host_device_ptr(void* host, void** device);
  * scratch and h [P, I] are caller-provided intermediate storage.  scratch
  * holds sg_glu_forward_scratch_bytes() bytes: the pairs' token rows copied
  * into dispatch order for prefill-sized groups (every tile's rows then load
- * as one TMA box), or the token rows' 8-bit pieces for the integer-operand
- * gate/up of 8-bit arenas at decode sizes (see sg_quantize_pieces).  NULL is
- * allowed when that size is 0, and also when only the pieces would go there
- * (the dequantising gate/up then runs instead).  h is kept in dispatch order.
+ * as one TMA box), or, for the integer-operand kernels of 8-bit arenas at
+ * decode sizes, the token rows' 8-bit pieces and afterwards h's (see
+ * sg_quantize_pieces).  NULL is allowed when that size is 0, and also when
+ * only pieces would go there (the dequantising kernels then run instead).
+ * h is kept in dispatch order.
  * pair_div = k for routed experts.  grid_groups is a host-side upper bound
  * on counts[0].
  * Replaces `_gather_forward`, qwen3_x_moe.py:210-248 (the `mx.take` of the
@@ -234,6 +235,18 @@ int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pairs,
                 const int32_t* group_off, const int32_t* perm,
                 int grid_groups, uint16_t* y, int flags, void* stream);
 
+/* sg_glu_down with a caller work area: with 8-bit arenas at decode tile
+ * widths and work_bytes >= sg_glu_down_work_bytes(), h is split into 8-bit
+ * pieces in the work area and the integer-operand tcgen05 kernel computes y
+ * (256-row tiles); otherwise sg_glu_down's kernels run.  Same replacement as
+ * sg_glu_down. */
+long long sg_glu_down_work_bytes(const sg_arena* arena, int num_pairs, int grid_groups);
+int sg_glu_down_work(const sg_arena* arena, const uint16_t* h, int num_pairs,
+                     const int32_t* counts, const int32_t* slot_ids,
+                     const int32_t* group_off, const int32_t* perm,
+                     int grid_groups, uint16_t* y, int flags, void* work, long long work_bytes,
+                     void* stream);
+
 /* Dense SwiGLU of one slot over every row: h[t, I] = swiglu(x @ gate^T, x @ up^T),
  * y[t, H] = bf16(h @ down^T) for t < T, slot sid of the arena (the shared
  * expert: one slot, all tokens).  h is caller-provided intermediate storage.
@@ -248,11 +261,11 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
  * automatic (tcgen05 when the shape allows -- in-dim % 64, out-dim % 128,
  * <= 2048 groups -- and either the mean pairs per group is >= 2 or the
  * groups make at least one 128-row tile per SM; token rows permuted once the
- * mean reaches 32, and for 8-bit arenas the integer-operand gate/up while
+ * mean reaches 32, and for 8-bit arenas the integer-operand kernels while
  * the mean is <= 16 and the caller passes a work area), 1 = streaming GEMV
  * always, 2 = the dequantising tcgen05 kernels whenever the shape allows,
  * 3 = as 2 with the token rows always permuted, 4 = as 0 with the
- * integer-operand gate/up wherever it applies.
+ * integer-operand kernels wherever they apply.
  * Process-wide.  No counterpart in the reference (MLX picks
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);

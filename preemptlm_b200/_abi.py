@@ -30,7 +30,7 @@ EXPORTED_SYMBOLS = (
     "sg_status_string", "sg_version", "sg_built_arch", "sg_router_logits", "sg_route_topk",
     "sg_dispatch", "sg_route_dispatch", "sg_host_device_ptr", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_forward_scratch_bytes", "sg_glu_use_permute",
     "sg_permute_rows", "sg_glu_gate_up", "sg_glu_gate_up_work_bytes", "sg_glu_gate_up_work", "sg_quantize_pieces",
-    "sg_glu_down",
+    "sg_glu_down", "sg_glu_down_work_bytes", "sg_glu_down_work",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
     "sg_ep_region_bytes", "sg_ep_layout", "sg_ep_alloc", "sg_ep_free", "sg_ep_ipc_handle", "sg_ep_ipc_open",
@@ -96,6 +96,8 @@ def load() -> ctypes.CDLL:
         "sg_glu_gate_up_work_bytes": (ctypes.c_longlong, [A, I32, I32, I32, I32]),
         "sg_glu_gate_up_work": (I32, [A, P, I32, I32, P, P, P, P, I32, P, I32, P, ctypes.c_longlong, P]),
         "sg_quantize_pieces": (I32, [P, I32, I32, I32, P, P, P]),
+        "sg_glu_down_work_bytes": (ctypes.c_longlong, [A, I32, I32]),
+        "sg_glu_down_work": (I32, [A, P, I32, P, P, P, P, I32, P, I32, P, ctypes.c_longlong, P]),
         "sg_permute_rows": (I32, [P, P, I32, I32, I32, P, P]),
         "sg_glu_gate_up": (I32, [A, P, I32, I32, P, P, P, P, I32, P, I32, P]),
         "sg_glu_down": (I32, [A, P, I32, P, P, P, P, I32, P, I32, P]),

@@ -315,10 +315,10 @@ int tc_glu_launch(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
                   const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
 int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, int sid, uint16_t* out,
                     cudaStream_t s);
-bool i8_supported(const sg_arena* A, int grid_groups);
-int i8_glu_launch(const sg_arena* A, const int8_t* pieces, const float* ex, int in_rows, int pair_div, int in_by_pos,
-                  int out_by_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
+bool i8_supported(const sg_arena* A, bool dual, int grid_groups);
+int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const float* ex, int in_rows, int pair_div,
+                  int in_by_pos, int out_by_pos, const int32_t* counts, const int32_t* slot_ids,
+                  const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
 int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s);
 // 0 auto, 1 streaming GEMV, 2 tcgen05 (dequantising), 3 tcgen05 over permuted
 // rows, 4 tcgen05 with the integer-operand gate/up wherever it applies
@@ -351,30 +351,47 @@ static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
 // Whether sg_glu_forward first copies the pairs' token rows into dispatch
 // order: worth it once a group's pairs fill 64-wide tiles (a contiguous
 // tile of rows then loads with one TMA box per stage).
-static bool use_i8(const sg_arena* A, int P, int grid_groups);
+static bool use_i8(const sg_arena* A, bool dual, int P, int grid_groups);
 static bool use_permute(const sg_arena* A, int P, int grid_groups) {
   if (!use_tc(A, true, P, grid_groups) || !use_tc(A, false, P, grid_groups)) return false;
-  if (use_i8(A, P, grid_groups)) return false;  // the integer-operand gate/up reads the rows in place
+  if (use_i8(A, true, P, grid_groups)) return false;  // the integer-operand gate/up reads the rows in place
   if (g_glu_path == 3) return true;
   return P >= 32 * grid_groups;
 }
 
-// The integer-operand gate/up (8-bit arenas): in auto mode wherever the
-// tensor-core path runs with pair tiles of 16 (decode batches); it needs a
-// caller work area for the token rows' pieces.
-static bool use_i8(const sg_arena* A, int P, int grid_groups) {
+// The integer-operand kernels (8-bit arenas, gate/up when dual, else down):
+// in auto mode wherever the tensor-core path runs with pair tiles of 16
+// (decode batches); they need a caller work area for the input rows' pieces.
+static bool use_i8(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || g_glu_path == 2 || g_glu_path == 3) return false;
-  if (grid_groups <= 0 || !i8_supported(A, grid_groups) || !tc_supported(A, true, grid_groups)) return false;
+  if (grid_groups <= 0 || !i8_supported(A, dual, grid_groups) || !tc_supported(A, dual, grid_groups)) return false;
   if (g_glu_path == 4) return true;
   return (P + grid_groups - 1) / grid_groups <= 16;
 }
 
-// Work area of the pieces of in_rows token rows: [in_rows, 2, H] int8, then
-// (256-byte aligned) [in_rows, H / 64, 2] fp32.
-static size_t pieces_bytes(const sg_arena* A, int in_rows, size_t* ex_off) {
-  const size_t p = ((size_t)in_rows * 2 * A->hidden + 255) & ~size_t(255);
+// Work area of the pieces of `rows` input rows of the projection's K
+// (hidden for gate/up, inter for down): [rows, 2, K] int8, then (256-byte
+// aligned) [rows, K / 64, 2] fp32.
+static size_t pieces_bytes(const sg_arena* A, bool dual, int rows, size_t* ex_off) {
+  const int K = dual ? A->hidden : A->inter;
+  const size_t p = ((size_t)rows * 2 * K + 255) & ~size_t(255);
   if (ex_off) *ex_off = p;
-  return p + (size_t)in_rows * (A->hidden / 64) * 8;
+  return p + (size_t)rows * (K / 64) * 8;
+}
+
+// Input rows' pieces into `work`, then the integer-operand kernel.
+static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_pos,
+                  int out_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+                  const int32_t* perm, int grid_groups, uint16_t* out, void* work, size_t work_bytes,
+                  cudaStream_t s) {
+  size_t ex_off = 0;
+  if (pieces_bytes(A, dual, in_rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
+  int8_t* pieces = static_cast<int8_t*>(work);
+  float* ex = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ex_off);
+  int st = quantize_pieces(in, in_rows, dual ? A->hidden : A->inter, 0, pieces, ex, s);
+  if (st) return st;
+  return i8_glu_launch(A, dual, pieces, ex, in_rows, pair_div, in_pos, out_pos, counts, slot_ids, group_off, perm,
+                       grid_groups, out, s);
 }
 
 // xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
@@ -394,17 +411,10 @@ static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int
                     uint16_t* h, int flags, cudaStream_t s, void* work = nullptr, size_t work_bytes = 0) {
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
   const int div = in_pos ? 1 : pair_div;
-  if (work && use_i8(arena, num_pairs, grid_groups)) {
-    // token rows -> pieces (in the caller's work area), then the integer-operand kernel
+  if (work && use_i8(arena, true, num_pairs, grid_groups)) {
     const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
-    size_t ex_off = 0;
-    if (pieces_bytes(arena, in_rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
-    int8_t* pieces = static_cast<int8_t*>(work);
-    float* ex = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ex_off);
-    int st = quantize_pieces(x, in_rows, arena->hidden, 0, pieces, ex, s);
-    if (st) return st;
-    return i8_glu_launch(arena, pieces, ex, in_rows, div, in_pos, out_pos, counts, slot_ids, group_off, perm,
-                         grid_groups, h, s);
+    return i8_run(arena, true, x, in_rows, div, in_pos, out_pos, counts, slot_ids, group_off, perm, grid_groups, h,
+                  work, work_bytes, s);
   }
   if (use_tc(arena, true, num_pairs, grid_groups)) {
     const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
@@ -420,8 +430,11 @@ static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int
 
 static int glu_single(const sg_arena* arena, const uint16_t* h, int num_pairs, const int32_t* counts,
                       const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm, int grid_groups,
-                      uint16_t* y, int flags, cudaStream_t s) {
+                      uint16_t* y, int flags, cudaStream_t s, void* work = nullptr, size_t work_bytes = 0) {
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
+  if (work && use_i8(arena, false, num_pairs, grid_groups))
+    return i8_run(arena, false, h, num_pairs, 1, in_pos, out_pos, counts, slot_ids, group_off, perm, grid_groups, y,
+                  work, work_bytes, s);
   if (use_tc(arena, false, num_pairs, grid_groups))
     return tc_glu_launch(arena, false, h, num_pairs, 1, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
                          grid_groups, y, s);
@@ -486,6 +499,18 @@ extern "C" int sg_glu_down(const sg_arena* arena, const uint16_t* h, int num_pai
                         (cudaStream_t)stream);
 }
 
+namespace sg {
+// Scratch of sg_glu_forward: the permuted token rows (prefill-sized groups),
+// or the pieces of the token rows for the integer-operand gate/up and then,
+// in the same bytes, the pieces of h for the integer-operand down projection.
+static size_t forward_scratch(const sg_arena* A, int P, int pair_div, int gg, size_t* gu, size_t* dn) {
+  *gu = use_i8(A, true, P, gg) ? pieces_bytes(A, true, (P + pair_div - 1) / pair_div, nullptr) : 0;
+  *dn = use_i8(A, false, P, gg) ? pieces_bytes(A, false, P, nullptr) : 0;
+  if (use_permute(A, P, gg)) return (size_t)P * A->hidden * 2;
+  return *gu > *dn ? *gu : *dn;
+}
+}  // namespace sg
+
 extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
                               const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
                               const int32_t* perm, int grid_groups, void* scratch, uint16_t* h, uint16_t* y,
@@ -503,15 +528,15 @@ extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_
     if (st) return st;
   }
   // h in dispatch order, so that the down projection's rows are contiguous.
-  // Without a work area the integer-operand gate/up is not used.
-  const size_t work_bytes = permute || !scratch ? 0
-                            : sg::pieces_bytes(arena, (num_pairs + pair_div - 1) / pair_div, nullptr);
+  // Without scratch the integer-operand kernels are not used.
+  size_t gu = 0, dn = 0;
+  sg::forward_scratch(arena, num_pairs, pair_div, grid_groups, &gu, &dn);
+  void* work = permute ? nullptr : scratch;
   st = sg::glu_dual(arena, permute ? xs : x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h,
-                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s, permute ? nullptr : scratch,
-                    work_bytes);
+                    (permute ? SG_IN_DISPATCH_ORDER : 0) | SG_OUT_DISPATCH_ORDER, s, work, work ? gu : 0);
   if (st) return st;
   return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, SG_IN_DISPATCH_ORDER,
-                        s);
+                        s, work, work ? dn : 0);
 }
 
 extern "C" long long sg_glu_forward_scratch_bytes(const sg_arena* arena, int num_pairs, int pair_div,
@@ -519,19 +544,17 @@ extern "C" long long sg_glu_forward_scratch_bytes(const sg_arena* arena, int num
   const int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, 0);
   if (st) return st;
   if (num_pairs == 0 || grid_groups == 0) return 0;
-  if (sg::use_permute(arena, num_pairs, grid_groups)) return (long long)num_pairs * arena->hidden * 2;
-  if (sg::use_i8(arena, num_pairs, grid_groups))
-    return (long long)sg::pieces_bytes(arena, (num_pairs + pair_div - 1) / pair_div, nullptr);
-  return 0;
+  size_t gu = 0, dn = 0;
+  return (long long)sg::forward_scratch(arena, num_pairs, pair_div, grid_groups, &gu, &dn);
 }
 
 extern "C" long long sg_glu_gate_up_work_bytes(const sg_arena* arena, int num_pairs, int pair_div, int grid_groups,
                                                int flags) {
   const int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, flags);
   if (st) return st;
-  if (num_pairs == 0 || grid_groups == 0 || !sg::use_i8(arena, num_pairs, grid_groups)) return 0;
+  if (num_pairs == 0 || grid_groups == 0 || !sg::use_i8(arena, true, num_pairs, grid_groups)) return 0;
   const int in_rows = (flags & SG_IN_DISPATCH_ORDER) ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
-  return (long long)sg::pieces_bytes(arena, in_rows, nullptr);
+  return (long long)sg::pieces_bytes(arena, true, in_rows, nullptr);
 }
 
 extern "C" int sg_glu_gate_up_work(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,
@@ -545,6 +568,26 @@ extern "C" int sg_glu_gate_up_work(const sg_arena* arena, const uint16_t* x, int
   if (!x || !counts || !slot_ids || !group_off || !perm || !h) return SG_ERR_INVALID_ARG;
   return sg::glu_dual(arena, x, num_pairs, pair_div, counts, slot_ids, group_off, perm, grid_groups, h, flags,
                       (cudaStream_t)stream, work_bytes > 0 ? work : nullptr, static_cast<size_t>(work_bytes));
+}
+
+extern "C" long long sg_glu_down_work_bytes(const sg_arena* arena, int num_pairs, int grid_groups) {
+  const int st = sg::check_glu_args(arena, num_pairs, 1, grid_groups, 0);
+  if (st) return st;
+  if (num_pairs == 0 || grid_groups == 0 || !sg::use_i8(arena, false, num_pairs, grid_groups)) return 0;
+  return (long long)sg::pieces_bytes(arena, false, num_pairs, nullptr);
+}
+
+extern "C" int sg_glu_down_work(const sg_arena* arena, const uint16_t* h, int num_pairs, const int32_t* counts,
+                                const int32_t* slot_ids, const int32_t* group_off, const int32_t* perm,
+                                int grid_groups, uint16_t* y, int flags, void* work, long long work_bytes,
+                                void* stream) {
+  int st = sg::check_glu_args(arena, num_pairs, 1, grid_groups, flags);
+  if (st) return st;
+  if (work_bytes < 0) return SG_ERR_INVALID_ARG;
+  if (num_pairs == 0 || grid_groups == 0) return SG_OK;
+  if (!h || !counts || !slot_ids || !group_off || !perm || !y) return SG_ERR_INVALID_ARG;
+  return sg::glu_single(arena, h, num_pairs, counts, slot_ids, group_off, perm, grid_groups, y, flags,
+                        (cudaStream_t)stream, work_bytes > 0 ? work : nullptr, static_cast<size_t>(work_bytes));
 }
 
 extern "C" int sg_quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex,

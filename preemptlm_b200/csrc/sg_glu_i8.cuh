@@ -230,7 +230,10 @@ __device__ __forceinline__ ITile itile_of(int t, const int* plan, int U, int NT,
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int BN>
+// MODE 1: gate/up, the two matrices of a 128-row tile and the SwiGLU
+// hand-off; MODE 2: down projection, the two 128-row halves of a 256-row
+// tile (the same bytes per stage), written straight out.
+template <int MODE, int BN>
 __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
               const __grid_constant__ CUtensorMap tmS0, const __grid_constant__ CUtensorMap tmQ0,
@@ -266,7 +269,9 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   const int K = args.K;
   const int NKS = K / KS;
   const int G = K / GSZ;
-  const int MT = args.OUT / BM;
+  constexpr int TR = MODE == 2 ? 2 * BM : BM;  // weight rows per tile
+  constexpr int RO1 = MODE == 2 ? BM : 0;      // row offset of the second matrix
+  const int MT = args.OUT / TR;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::SA; ++i) {
@@ -336,7 +341,7 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         const ITile tl = itile_of<BN>(t, plan, U, NT, args);
         // a slot outside the arena gives negative or out-of-range rows: the
         // TMA's zero fill (the epilogue writes zeros for such tiles)
-        const int row0 = (tl.slot >= 0 && tl.slot < args.num_slots) ? tl.slot * args.OUT + tl.m * BM : -BM;
+        const int row0 = (tl.slot >= 0 && tl.slot < args.num_slots) ? tl.slot * args.OUT + tl.m * TR : -TR;
         for (int ks = 0; ks < NKS && ok; ++ks) {
           if ((ks & 3) == 0) {  // scales and biases of groups [2 ks, 2 ks + 8) of the tile's rows
             ok = wait_bar(&s_empty[ss], sph ^ 1, ctl, BACKOFF_NS);
@@ -345,8 +350,8 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             mbar_expect_tx(&s_full[ss], C::S_BYTES);
             tma_load_2d(dst, &tmS0, 2 * ks, row0, &s_full[ss]);
             tma_load_2d(dst + BM * 16, &tmQ0, 2 * ks, row0, &s_full[ss]);
-            tma_load_2d(dst + 2 * BM * 16, &tmS1, 2 * ks, row0, &s_full[ss]);
-            tma_load_2d(dst + 3 * BM * 16, &tmQ1, 2 * ks, row0, &s_full[ss]);
+            tma_load_2d(dst + 2 * BM * 16, &tmS1, 2 * ks, row0 + RO1, &s_full[ss]);
+            tma_load_2d(dst + 3 * BM * 16, &tmQ1, 2 * ks, row0 + RO1, &s_full[ss]);
             ++s_issued;
             if (++ss == C::SS) { ss = 0; sph ^= 1; }
           }
@@ -354,7 +359,7 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           if (!ok) break;
           mbar_expect_tx(&a_full[sa], C::A_BYTES);
           tma_load_2d(sA + sa * C::A_BYTES, &tmA0, ks * 32, row0, &a_full[sa]);
-          tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, ks * 32, row0, &a_full[sa]);
+          tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, ks * 32, row0 + RO1, &a_full[sa]);
           ++issued;
           if (++sa == C::SA) { sa = 0; pa ^= 1; }
         }
@@ -477,7 +482,7 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   } else {
     // ---------------------------------------------------------------- epilogue: 8 warps, (quadrant, matrix)
     const int quad = warp & 3;
-    const int mat = (warp - C::EPI_WARP0) >> 2;  // 0 gate, 1 up
+    const int mat = (warp - C::EPI_WARP0) >> 2;  // gate / up, or the tile's first / second 128 rows
     const int r = quad * 32 + lane;              // weight row within the tile, TMEM lane
     int ss = 0, gc = 0, it = 0;
     uint32_t sph = 0;
@@ -545,6 +550,21 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[buf]);
+      if constexpr (MODE == 2) {  // down projection: this warp's 32 output columns of the tile's pairs
+        const bool slot_ok = tl.slot >= 0 && tl.slot < args.num_slots;
+        int my_row = 0;
+        if (lane < tl.nvalid) {
+          const int pos = tl.goff + tl.n0 + lane;
+          my_row = args.out_by_pos ? pos : args.perm[pos];
+        }
+        const int ocol = tl.m * TR + mat * BM + r;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int orow = __shfl_sync(0xffffffffu, my_row, j);
+          if (j < tl.nvalid) args.out[(size_t)orow * args.OUT + ocol] = slot_ok ? f32_to_bf16(y[j]) : 0;
+        }
+        continue;
+      }
       // hand-off: the up warps pass their sums to the gate warps of the quadrant
       float* xr = sX + buf * (C::X_BYTES / 4) + r * C::X_STRIDE;
       if (mat == 1) {
@@ -595,37 +615,45 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
 // Whether the integer-operand gate/up serves this arena: 8-bit affine weights,
 // K a multiple of 128 with at most 64 groups (whole scale chunks of 8 groups),
 // 128-row output tiles.
-static bool supported(const sg_arena* A, int grid_groups) {
-  const int K = A->hidden, OUT = A->inter;
+static bool supported(const sg_arena* A, bool dual, int grid_groups) {
+  const int K = dual ? A->hidden : A->inter, OUT = dual ? A->inter : A->hidden;
   return A->bits == 8 && A->group_size == GSZ && K % KS == 0 && (K / GSZ) % 8 == 0 && K / GSZ <= Cfg<16>::GMAX &&
-         OUT % BM == 0 && grid_groups <= PLAN_MAX_GROUPS;
+         OUT % (dual ? BM : 2 * BM) == 0 && grid_groups <= PLAN_MAX_GROUPS;
 }
 
+template <int MODE>
 static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
   constexpr int BN = 16;
   using C = Cfg<BN>;
+  constexpr bool DUAL = MODE == 1;
   const int K = args.K;
   const uint64_t rows_total = (uint64_t)A->num_slots * args.OUT;
   const uint64_t words = (uint64_t)K / 4;
   const uint64_t groups = (uint64_t)K / GSZ;
+  const void* w0 = DUAL ? A->gate_w : A->down_w;
+  const void* w1 = DUAL ? A->up_w : A->down_w;
+  const void* s0 = DUAL ? A->gate_s : A->down_s;
+  const void* b0 = DUAL ? A->gate_b : A->down_b;
+  const void* s1 = DUAL ? A->up_s : A->down_s;
+  const void* b1 = DUAL ? A->up_b : A->down_b;
   CUtensorMap m0, m1, ms0, mq0, ms1, mq1;
   const bool ok =
-      make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, A->gate_w, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-      make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, A->up_w, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-      make_map(&ms0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->gate_s, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-      make_map(&mq0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->gate_b, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-      make_map(&ms1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->up_s, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-      make_map(&mq1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A->up_b, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+      make_map(&m0, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w0, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      make_map(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w1, words, rows_total, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      make_map(&ms0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s0, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&mq0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b0, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&ms1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s1, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+      make_map(&mq1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b1, groups, rows_total, 8, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) return SG_ERR_CUDA;
   static bool attr_done[64] = {};  // per device
   int dev = 0;
   SG_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
   if (!attr_done[dev]) {
-    SG_CUDA_TRY(cudaFuncSetAttribute(glu_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    SG_CUDA_TRY(cudaFuncSetAttribute(glu_i8_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_done[dev] = true;
   }
-  glu_i8_kernel<BN><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, ms0, mq0, ms1, mq1, args);
+  glu_i8_kernel<MODE, BN><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, ms0, mq0, ms1, mq1, args);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -643,15 +671,17 @@ int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* piece
   return SG_OK;
 }
 
-bool i8_supported(const sg_arena* A, int grid_groups) { return i8::supported(A, grid_groups); }
+bool i8_supported(const sg_arena* A, bool dual, int grid_groups) { return i8::supported(A, dual, grid_groups); }
 
-int i8_glu_launch(const sg_arena* A, const int8_t* pieces, const float* ex, int in_rows, int pair_div, int in_by_pos,
-                  int out_by_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
-                  const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s) {
+// dual: gate/up + SwiGLU (K = hidden, OUT = inter); else the down projection
+// (K = inter, OUT = hidden).
+int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const float* ex, int in_rows, int pair_div,
+                  int in_by_pos, int out_by_pos, const int32_t* counts, const int32_t* slot_ids,
+                  const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s) {
   i8::Args a;
   a.num_slots = A->num_slots;
-  a.K = A->hidden;
-  a.OUT = A->inter;
+  a.K = dual ? A->hidden : A->inter;
+  a.OUT = dual ? A->inter : A->hidden;
   a.pieces = pieces;
   a.ex = ex;
   a.in_rows = in_rows;
@@ -664,7 +694,7 @@ int i8_glu_launch(const sg_arena* A, const int8_t* pieces, const float* ex, int 
   a.out_by_pos = out_by_pos;
   a.max_groups = grid_groups;
   a.out = out;
-  return i8::launch(A, a, s);
+  return dual ? i8::launch<1>(A, a, s) : i8::launch<2>(A, a, s);
 }
 
 }  // namespace sg

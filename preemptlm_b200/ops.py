@@ -212,9 +212,20 @@ def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0, out: torch.Ten
         y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=h.device)
     if P == 0:
         return y
-    LAUNCHES[0] += 1
     lib = _abi.load()
-    _abi.check(lib.sg_glu_down(ctypes.byref(arena.desc()), h.data_ptr(), P, d.counts.data_ptr(), d.slot_ids.data_ptr(),
+    desc = ctypes.byref(arena.desc())
+    nwork = lib.sg_glu_down_work_bytes(desc, P, d.grid_groups)
+    if nwork < 0:
+        _abi.check(int(nwork), "sg_glu_down_work_bytes")
+    if nwork > 0:  # 8-bit arena at decode sizes: h's pieces, then the integer-operand kernel
+        work = torch.empty(int(nwork), dtype=torch.uint8, device=h.device)
+        LAUNCHES[0] += 2
+        _abi.check(lib.sg_glu_down_work(desc, h.data_ptr(), P, d.counts.data_ptr(), d.slot_ids.data_ptr(),
+                                        d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(),
+                                        int(flags), work.data_ptr(), int(nwork), _stream()), "sg_glu_down_work")
+        return y
+    LAUNCHES[0] += 1
+    _abi.check(lib.sg_glu_down(desc, h.data_ptr(), P, d.counts.data_ptr(), d.slot_ids.data_ptr(),
                                d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups, y.data_ptr(), int(flags),
                                _stream()), "sg_glu_down")
     return y
@@ -230,6 +241,17 @@ def permute_rows(x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
         _abi.check(_abi.load().sg_permute_rows(x.data_ptr(), d.perm.data_ptr(), int(pair_div), P, x.shape[1],
                                                xs.data_ptr(), _stream()), "sg_permute_rows")
     return xs
+
+
+def _extra_launches(lib, desc, P: int, pair_div: int, grid_groups: int, scratch: bool) -> int:
+    """Launches sg_glu_forward adds to its two GLU kernels: the row
+    permutation, or one piece split per integer-operand projection."""
+    if not scratch:
+        return 0
+    if lib.sg_glu_use_permute(desc, P, grid_groups) == 1:
+        return 1
+    return int(lib.sg_glu_gate_up_work_bytes(desc, P, pair_div, grid_groups, 0) > 0) + int(
+        lib.sg_glu_down_work_bytes(desc, P, grid_groups) > 0)
 
 
 def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: dict | None = None) -> torch.Tensor:
@@ -249,9 +271,9 @@ def gather_forward(arena, x: torch.Tensor, d: Dispatch, pair_div: int, timing: d
         nscratch = lib.sg_glu_forward_scratch_bytes(desc, P, int(pair_div), d.grid_groups)
         if nscratch < 0:
             _abi.check(int(nscratch), "sg_glu_forward_scratch_bytes")
-        # the permuted token rows, or the token rows' pieces: one launch more either way
+        # the permuted token rows, or the pieces of the token rows / of h
         xs = torch.empty(int(nscratch), dtype=torch.uint8, device=x.device) if nscratch > 0 else None
-        LAUNCHES[0] += 3 if xs is not None else 2
+        LAUNCHES[0] += 2 + _extra_launches(lib, desc, P, int(pair_div), d.grid_groups, xs is not None)
         _abi.check(lib.sg_glu_forward(desc, x.data_ptr(), P, int(pair_div), d.counts.data_ptr(),
                                       d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                       None if xs is None else xs.data_ptr(), h.data_ptr(), y.data_ptr(), _stream()),
@@ -279,8 +301,10 @@ def gather_forward_noalloc(arena, x: torch.Tensor, d: Dispatch, pair_div: int) -
     y = torch.empty((P, arena.hidden), dtype=torch.bfloat16, device=x.device)
     if P == 0:
         return y
-    nscratch = _abi.load().sg_glu_forward_scratch_bytes(ctypes.byref(arena.desc()), P, int(pair_div), d.grid_groups)
-    LAUNCHES[0] += 3 if nscratch > 0 else 2
+    lib = _abi.load()
+    nscratch = lib.sg_glu_forward_scratch_bytes(ctypes.byref(arena.desc()), P, int(pair_div), d.grid_groups)
+    LAUNCHES[0] += 2 + _extra_launches(lib, ctypes.byref(arena.desc()), P, int(pair_div), d.grid_groups,
+                                       nscratch > 0)
     _abi.check(_abi.load().sg_glu_forward_noalloc(ctypes.byref(arena.desc()), x.data_ptr(), P, int(pair_div),
                                                   d.counts.data_ptr(), d.slot_ids.data_ptr(), d.group_off.data_ptr(),
                                                   d.perm.data_ptr(), d.grid_groups, y.data_ptr(), _stream()),

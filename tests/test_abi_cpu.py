@@ -83,7 +83,10 @@ def test_host_side_argument_checks(lib):
     # decode: 256 tokens x top-10 over 512 groups (mean 5 pairs): the pieces of the 256 token rows
     pieces = 256 * 2 * 2048 + 256 * 32 * 8
     assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == pieces
-    assert lib.sg_glu_forward_scratch_bytes(ctypes.byref(q8), 2560, 10, 512) == pieces
+    # the fused call reuses the bytes for h's pieces (2560 rows of 512), the larger of the two
+    h_pieces = 2560 * 2 * 512 + 2560 * 8 * 8
+    assert lib.sg_glu_down_work_bytes(ctypes.byref(q8), 2560, 512) == h_pieces
+    assert lib.sg_glu_forward_scratch_bytes(ctypes.byref(q8), 2560, 10, 512) == max(pieces, h_pieces)
     # prefill-sized groups: the permuted token rows instead
     assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 81920, 10, 512, 0) == 0
     assert lib.sg_glu_forward_scratch_bytes(ctypes.byref(q8), 81920, 10, 512) == 81920 * 2048 * 2

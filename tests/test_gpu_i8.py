@@ -1,8 +1,10 @@
-"""GPU: the integer-operand gate/up (8-bit arenas at decode tile widths).
+"""GPU: the integer-operand kernels (8-bit arenas at decode tile widths).
 
 * sg_quantize_pieces against a numpy statement of the piece split (exact);
-* h through the integer-operand kernel against the CPU oracle within the
+* h through the integer-operand gate/up against the CPU oracle within the
   bf16 tolerance of the layer, and against the dequantising tcgen05 kernel;
+  y through the integer-operand down projection against the oracle's down
+  projection of the device's h;
 * missing slots, several pair tiles per group, rows in dispatch order.
 """
 
@@ -95,6 +97,14 @@ def _h_oracle(tens, bits, x, inds, k, I):
     return href
 
 
+def _exact_down(tens, e):
+    """scale * q + bias of expert e's down projection in float64 (no rounding)."""
+    q = orc.unpack_affine(tens["experts"]["down_proj.weight"][int(e)].cpu().numpy().view(np.uint32), 8)
+    sc = f32(tens["experts"]["down_proj.scales"][int(e)]).astype(np.float64)
+    bi = f32(tens["experts"]["down_proj.biases"][int(e)]).astype(np.float64)
+    return q.astype(np.float64) * np.repeat(sc, 64, axis=1) + np.repeat(bi, 64, axis=1)
+
+
 @pytest.fixture
 def i8_path():
     ops.set_glu_path("i8")
@@ -104,9 +114,9 @@ def i8_path():
 
 
 @pytest.mark.parametrize("H,I,E,T,k", [(512, 128, 8, 5, 2), (2048, 512, 64, 33, 8), (1024, 256, 6, 1, 6),
-                                       (4096, 1024, 16, 9, 4),
+                                       (4096, 1024, 16, 9, 4), (512, 512, 8, 7, 3),
                                        # ~40 pairs per group: three 16-pair tiles per group, the last partial
-                                       (1024, 384, 4, 80, 2)])
+                                       (1024, 384, 4, 80, 2), (1024, 512, 4, 80, 2)])
 def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
     cfg = LayerConfig("t", 9, H, E, k, I, None, 8, E)
     block, tens = make_layer(cfg, device=DEV)
@@ -124,7 +134,30 @@ def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
     h_tc = ops.glu_gate_up(arena, x, d, pair_div=k)
     ops.set_glu_path("i8")
     assert_close(f32(h), f32(h_tc), max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="h vs tc")
-    # the fused layer call takes the same path (work area from sg_glu_forward_scratch_bytes)
+    # down projection of the device's h: the integer-operand kernel where the
+    # shape allows it (I % 512, H % 256), against the oracle's down of that h
+    down_i8 = _abi.load().sg_glu_down_work_bytes(ctypes.byref(arena.desc()), T * k, d.grid_groups) > 0
+    assert down_i8 == (I % 512 == 0 and H % 256 == 0)
+    y = ops.glu_down(arena, h, d)
+    ex = LazyExperts(tens["experts"], 8)
+    hdev = f32(h)
+    ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
+    if down_i8:
+        # the layer tolerance against the oracle (whose weights are rounded to
+        # bf16); against the exact affine weights scale * q + bias, which the
+        # integer kernel uses: the output rounding (half a bf16 ulp, < 2^-8
+        # relative) plus the piece rounding of h (each element to within 2^-14
+        # of its group's largest magnitude), summed through |w| as a bound
+        assert_close(f32(y), ydown, what="y|h")
+        for p in range(T * k):
+            w = _exact_down(tens, inds.reshape(-1)[p])
+            hp = hdev[p].astype(np.float64)
+            gmax = np.repeat(np.abs(hp).reshape(-1, 64).max(axis=1), 64)
+            bound = 2.0 ** -8 * np.abs(hp @ w.T) + 2.0 ** -14 * (np.abs(w) @ gmax) + 1e-6
+            assert np.all(np.abs(f32(y[p]) - hp @ w.T) <= bound), (p, float(np.abs(f32(y[p]) - hp @ w.T).max()))
+    else:
+        assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what="y|h")
+    # the fused layer call takes the same paths (work area from sg_glu_forward_scratch_bytes)
     y = ops.gather_forward(arena, x, d, k)
     y2 = ops.glu_down(arena, ops.glu_gate_up(arena, x, d, k, _abi.SG_OUT_DISPATCH_ORDER), d,
                       _abi.SG_IN_DISPATCH_ORDER)
@@ -149,7 +182,7 @@ def test_gate_up_i8_rows_in_dispatch_order(i8_path):
 
 
 def test_gate_up_i8_missing_slots(i8_path):
-    H, I, E = 512, 128, 4
+    H, I, E = 512, 512, 4
     cfg = LayerConfig("t", 9, H, E, 1, I, None, 8, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((3, H), 12)
@@ -159,3 +192,6 @@ def test_gate_up_i8_missing_slots(i8_path):
     assert torch.all(h[1] == 0) and torch.any(h[0] != 0)
     href = _h_oracle(tens, 8, x, np.array([0, -1, 2]), 1, I)
     assert_close(f32(h[[0, 2]]), href[[0, 2]], max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="h")
+    # the down projection writes zeros for the pairs of the missing slot too
+    y = ops.glu_down(block.switch_mlp, h, d)
+    assert torch.all(y[1] == 0) and torch.any(y[0] != 0)
