@@ -750,7 +750,7 @@ def run_ours(args, rank, world, local_rank):
             "timed_steps": "CUDA graph replays" if graph_ok else "eager",
         },
         "roofline": {
-            "bound": "hbm", "kernel": f"sg_glu_gate_up (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
+            "bound": "hbm", "kernel": f"{ops.LAST_GATE_UP[0]} (routed, q{cfg.bits})", "achieved": round(rl["gu_gbs"], 1),
             "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4), "peak_kind": peak_kind,
             "traffic": round(traffic_pe * us_mean) if traffic_pe else None,
             "traffic_source": traffic_src,

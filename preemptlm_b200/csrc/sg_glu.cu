@@ -388,7 +388,8 @@ static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   if (pieces_bytes(A, dual, in_rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
   int8_t* pieces = static_cast<int8_t*>(work);
   float* ex = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ex_off);
-  int st = quantize_pieces(in, in_rows, dual ? A->hidden : A->inter, 0, pieces, ex, s);
+  // 4-bit weights unpack with nibbles 0,2,4,6 before 1,3,5,7: the pieces follow that order
+  int st = quantize_pieces(in, in_rows, dual ? A->hidden : A->inter, A->bits == 4 ? 1 : 0, pieces, ex, s);
   if (st) return st;
   return i8_glu_launch(A, dual, pieces, ex, in_rows, pair_div, in_pos, out_pos, counts, slot_ids, group_off, perm,
                        grid_groups, out, s);

@@ -133,13 +133,23 @@ quantize_pieces_kernel(const uint16_t* __restrict__ x, int rows, int K, int orde
 }
 
 // ------------------------------------------------------------------ kernel configuration
-template <int BN>
+// BITS 8: the packed rows are the MMA's A operand as they are (TMA into shared
+// memory, SA stages).  BITS 4: TMA brings 128 packed bytes (256 weights) of
+// every row per stage (SP stages); 8 unpacking warps turn each half into 128
+// unsigned bytes per row -- in the order 0,2,4,6,1,3,5,7 within every 8
+// weights, the pieces' order 1 -- and store them into tensor memory (SAT
+// stages), where the MMAs read A.
+template <int BITS, int BN>
 struct Cfg {
+  static constexpr bool Q4 = BITS == 4;
   static constexpr int NB = 2 * BN;                  // B rows: the pairs' hi pieces, then their lo pieces
-  static constexpr int A_MAT = BM * KS;              // one matrix's stage: 128 rows x 128 bytes (16 KB)
-  static constexpr int A_BYTES = 2 * A_MAT;          // gate and up
+  static constexpr int A_MAT = BM * KS;              // one matrix's packed stage: 128 rows x 128 bytes (16 KB)
+  static constexpr int A_BYTES = 2 * A_MAT;          // both matrices
   static constexpr int B_BYTES = NB * KS;            // 2 BN rows x 128 bytes
-  static constexpr int SA = 4;
+  static constexpr int SA = Q4 ? 0 : 4;              // shared-memory A stages (8-bit)
+  static constexpr int SP = Q4 ? 3 : 0;              // packed stages (4-bit), two K stages each
+  static constexpr int SAT = Q4 ? 4 : 0;             // tensor-memory A stages (4-bit, unpacked)
+  static constexpr int A_TCOLS = 2 * KS / 4;         // TMEM columns of one unpacked stage: 2 matrices x 32
   static constexpr int SB = 6;
   static constexpr int SS = 3;
   static constexpr int S_BYTES = 2 * 2 * BM * 16;    // [matrix][scales, biases][128 rows][8 groups] bf16
@@ -148,19 +158,22 @@ struct Cfg {
   static constexpr int X_STRIDE = BN + 4;            // hand-off rows: BN fp32 + padding
   static constexpr int X_BYTES = BM * X_STRIDE * 4;
   static constexpr int ACC_COLS = 2 * NB;            // one group: gate and up, NB columns each
-  static constexpr int TMEM_COLS = RING * ACC_COLS;
+  static constexpr int RINGN = Q4 ? 4 : RING;        // group accumulators in flight
+  static constexpr int ACC_TOTAL = RINGN * ACC_COLS;
+  static constexpr int TMEM_COLS = ACC_TOTAL + SAT * A_TCOLS;
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + SA * A_BYTES;
+  static constexpr int OFF_B = OFF_A + (SA + SP) * A_BYTES;
   static constexpr int OFF_S = OFF_B + SB * B_BYTES;
   static constexpr int OFF_T = OFF_S + SS * S_BYTES;
   static constexpr int OFF_X = OFF_T + 2 * T_BYTES;
   static constexpr int OFF_PLAN = OFF_X + 2 * X_BYTES;
   static constexpr int OFF_BAR = (OFF_PLAN + (PLAN_MAX_GROUPS + 1) * 4 + 15) & ~15;
-  static constexpr int NUM_BARS = 2 * SA + 2 * SB + 2 * RING + 2 * SS + 2 * 2 + 2 * 2;
+  static constexpr int NUM_BARS = 2 * (SA + SAT) + 2 * SP + 2 * SB + 2 * RINGN + 2 * SS + 2 * 2 + 2 * 2;
   static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
   static constexpr int EPI_WARP0 = 3;
-  static constexpr int THREADS = (EPI_WARP0 + 8) * 32;
-  static_assert(TMEM_COLS <= 512, "tensor memory budget");
+  static constexpr int UNP_WARP0 = EPI_WARP0 + 8;    // 4-bit: the unpacking warps follow the epilogue
+  static constexpr int THREADS = (UNP_WARP0 + (Q4 ? 8 : 0)) * 32;
+  static_assert(TMEM_COLS == 512, "tensor memory budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(B_BYTES % 1024 == 0, "B stages keep 1024-byte alignment");
 };
@@ -177,6 +190,14 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b,
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// A from tensor memory: row m in lane m, four consecutive K bytes per column
+__device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -233,13 +254,14 @@ __device__ __forceinline__ ITile itile_of(int t, const int* plan, int U, int NT,
 // MODE 1: gate/up, the two matrices of a 128-row tile and the SwiGLU
 // hand-off; MODE 2: down projection, the two 128-row halves of a 256-row
 // tile (the same bytes per stage), written straight out.
-template <int MODE, int BN>
-__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
+template <int BITS, int MODE, int BN>
+__global__ void __launch_bounds__(Cfg<BITS, BN>::THREADS, 1)
 glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
               const __grid_constant__ CUtensorMap tmS0, const __grid_constant__ CUtensorMap tmQ0,
               const __grid_constant__ CUtensorMap tmS1, const __grid_constant__ CUtensorMap tmQ1, const Args args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BITS, BN>;
   constexpr int NB = C::NB;
+  constexpr int NA = C::SA + C::SAT;  // A stages (shared or tensor memory)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem + C::OFF_A;
@@ -249,13 +271,16 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   float* sX = reinterpret_cast<float*>(smem + C::OFF_X);
   int* plan = reinterpret_cast<int*>(smem + C::OFF_PLAN);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* a_full = bars;                   // [SA] weight stage landed (TMA tx)
-  uint64_t* a_empty = a_full + C::SA;        // [SA] weight stage consumed (MMA commit)
-  uint64_t* b_full = a_empty + C::SA;        // [SB] piece rows landed (32 cp.async arrivals)
+  // A stage ready: TMA tx (8-bit) or the 8 unpacking warps (4-bit); consumed: MMA commit
+  uint64_t* a_full = bars;                   // [NA]
+  uint64_t* a_empty = a_full + NA;           // [NA]
+  uint64_t* p_full = a_empty + NA;           // [SP] packed stage landed (TMA tx, 4-bit)
+  uint64_t* p_empty = p_full + C::SP;        // [SP] packed stage read (8 unpacking warps)
+  uint64_t* b_full = p_empty + C::SP;        // [SB] piece rows landed (32 cp.async arrivals)
   uint64_t* b_empty = b_full + C::SB;        // [SB] piece rows consumed (MMA commit)
-  uint64_t* acc_full = b_empty + C::SB;      // [RING] group accumulator ready (MMA commit)
-  uint64_t* acc_empty = acc_full + RING;     // [RING] group accumulator read (8 epilogue warps)
-  uint64_t* s_full = acc_empty + RING;       // [SS] scale/bias chunk landed (TMA tx)
+  uint64_t* acc_full = b_empty + C::SB;      // [RINGN] group accumulator ready (MMA commit)
+  uint64_t* acc_empty = acc_full + C::RINGN;  // [RINGN] group accumulator read (8 epilogue warps)
+  uint64_t* s_full = acc_empty + C::RINGN;   // [SS] scale/bias chunk landed (TMA tx)
   uint64_t* s_empty = s_full + C::SS;        // [SS] scale/bias chunk read (8 epilogue warps)
   uint64_t* t_full = s_empty + C::SS;        // [2] pair table written (32 producer lanes)
   uint64_t* t_empty = t_full + 2;            // [2] pair table read (8 epilogue warps)
@@ -274,15 +299,19 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   const int MT = args.OUT / TR;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < C::SA; ++i) {
-      mbar_init(&a_full[i], 1);
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&a_full[i], C::Q4 ? 8 : 1);
       mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < C::SP; ++i) {
+      mbar_init(&p_full[i], 1);
+      mbar_init(&p_empty[i], 8);
     }
     for (int i = 0; i < C::SB; ++i) {
       mbar_init(&b_full[i], 32);
       mbar_init(&b_empty[i], 1);
     }
-    for (int i = 0; i < RING; ++i) {
+    for (int i = 0; i < C::RINGN; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 8);
     }
@@ -334,6 +363,10 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
   if (warp == 0) {
     // ---------------------------------------------------------------- weight + scale producer
     if (lane == 0) {
+      // 8-bit: one A stage per K stage; 4-bit: one packed stage per two K stages
+      constexpr int WR = C::Q4 ? C::SP : C::SA;
+      uint64_t* wfull = C::Q4 ? p_full : a_full;
+      uint64_t* wempty = C::Q4 ? p_empty : a_empty;
       int sa = 0, ss = 0, issued = 0, s_issued = 0;
       uint32_t pa = 0, sph = 0;
       bool ok = true;
@@ -355,22 +388,24 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
             ++s_issued;
             if (++ss == C::SS) { ss = 0; sph ^= 1; }
           }
-          ok = wait_bar(&a_empty[sa], pa ^ 1, ctl, BACKOFF_NS);
+          if (C::Q4 && (ks & 1)) continue;  // this K stage came with the previous packed stage
+          ok = wait_bar(&wempty[sa], pa ^ 1, ctl, BACKOFF_NS);
           if (!ok) break;
-          mbar_expect_tx(&a_full[sa], C::A_BYTES);
-          tma_load_2d(sA + sa * C::A_BYTES, &tmA0, ks * 32, row0, &a_full[sa]);
-          tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, ks * 32, row0 + RO1, &a_full[sa]);
+          const int col = (C::Q4 ? ks / 2 : ks) * 32;  // 32 packed words = 128 bytes of every row
+          mbar_expect_tx(&wfull[sa], C::A_BYTES);
+          tma_load_2d(sA + sa * C::A_BYTES, &tmA0, col, row0, &wfull[sa]);
+          tma_load_2d(sA + sa * C::A_BYTES + C::A_MAT, &tmA1, col, row0 + RO1, &wfull[sa]);
           ++issued;
-          if (++sa == C::SA) { sa = 0; pa ^= 1; }
+          if (++sa == WR) { sa = 0; pa ^= 1; }
         }
       }
       if (!ok) {  // drain this thread's copies still in flight (bounded)
-        for (int i = 0; i < min(issued, C::SA); ++i) {
+        for (int i = 0; i < min(issued, WR); ++i) {
           int s = sa - 1 - i;
           uint32_t p = pa;
-          if (s < 0) { s += C::SA; p ^= 1; }
+          if (s < 0) { s += WR; p ^= 1; }
           const long long t0 = clock64();
-          while (!mbar_try_wait(&a_full[s], p) && clock64() - t0 < WAIT_CYCLES) {
+          while (!mbar_try_wait(&wfull[s], p) && clock64() - t0 < WAIT_CYCLES) {
           }
         }
         for (int i = 0; i < min(s_issued, C::SS); ++i) {
@@ -395,29 +430,37 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           ok = wait_bar(&b_full[sb], pb, ctl) && wait_bar(&a_full[sa], pa, ctl);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t ad0 = desc_sw128(smem_u32(sA + sa * C::A_BYTES));
-          const uint64_t ad1 = desc_sw128(smem_u32(sA + sa * C::A_BYTES + C::A_MAT));
+          // (8-bit A in shared memory; 4-bit A in tensor memory, addressed below)
+          const uint64_t ad0 = desc_sw128(smem_u32(sA + (C::Q4 ? 0 : sa) * C::A_BYTES));
+          const uint64_t ad1 = desc_sw128(smem_u32(sA + (C::Q4 ? 0 : sa) * C::A_BYTES + C::A_MAT));
           const uint64_t bd = desc_sw128(smem_u32(sB + sb * C::B_BYTES));
 #pragma unroll
           for (int gi = 0; gi < KS / GSZ; ++gi) {
-            const int slot = gc % RING;
-            ok = wait_bar(&acc_empty[slot], ((gc / RING) & 1) ^ 1, ctl);
+            const int slot = gc % C::RINGN;
+            ok = wait_bar(&acc_empty[slot], ((gc / C::RINGN) & 1) ^ 1, ctl);
             if (!ok) break;
             tc_fence_after();
             const uint32_t d = tmem + slot * C::ACC_COLS;
 #pragma unroll
             for (int kk = 0; kk < GSZ / 32; ++kk) {
-              // K step of 32 one-byte elements = 32 bytes: +2 in the descriptor's address field
+              // K step of 32 one-byte elements = 32 bytes: +2 in the descriptor's
+              // address field, 8 columns of tensor memory
               const uint32_t ko = static_cast<uint32_t>((gi * GSZ + kk * 32) >> 4);
-              umma_i8(d, ad0 + ko, bd + ko, idesc, kk);
-              umma_i8(d + NB, ad1 + ko, bd + ko, idesc, kk);
+              if constexpr (C::Q4) {
+                const uint32_t at = tmem + C::ACC_TOTAL + sa * C::A_TCOLS + (gi * GSZ + kk * 32) / 4;
+                umma_i8_ts(d, at, bd + ko, idesc, kk);
+                umma_i8_ts(d + NB, at + KS / 4, bd + ko, idesc, kk);
+              } else {
+                umma_i8(d, ad0 + ko, bd + ko, idesc, kk);
+                umma_i8(d + NB, ad1 + ko, bd + ko, idesc, kk);
+              }
             }
             umma_commit(&acc_full[slot]);
             ++gc;
           }
           if (!ok) break;
           umma_commit(&a_empty[sa]);
-          if (++sa == C::SA) { sa = 0; pa ^= 1; }
+          if (++sa == NA) { sa = 0; pa ^= 1; }
           umma_commit(&b_empty[sb]);
           if (++sb == C::SB) { sb = 0; pb ^= 1; }
         }
@@ -479,7 +522,7 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
       }
     }
     cp_async_wait_all();  // no copy of this warp outlives the kernel
-  } else {
+  } else if (warp < C::UNP_WARP0) {
     // ---------------------------------------------------------------- epilogue: 8 warps, (quadrant, matrix)
     const int quad = warp & 3;
     const int mat = (warp - C::EPI_WARP0) >> 2;  // gate / up, or the tile's first / second 128 rows
@@ -514,8 +557,8 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
-          const int slot = gc % RING;
-          ok = wait_bar(&acc_full[slot], (gc / RING) & 1, ctl);
+          const int slot = gc % C::RINGN;
+          ok = wait_bar(&acc_full[slot], (gc / C::RINGN) & 1, ctl);
           ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
           if (!ok) break;
           tc_fence_after();
@@ -601,6 +644,62 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         }
       }
     }
+  } else {
+    // ---------------------------------------------------------------- 4-bit unpacking: 8 warps, (quadrant, matrix)
+    // Each thread takes its row's 128 packed bytes of a stage into registers
+    // (releasing the slot at once), then per K stage turns 64 bytes into 128:
+    // word w -> (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F), nibbles 0,2,4,6 then
+    // 1,3,5,7, stored as 32 tensor-memory columns of its lane.
+    if constexpr (C::Q4) {
+      const int quad = warp & 3;
+      const int mat = (warp - C::UNP_WARP0) >> 2;
+      const int r = quad * 32 + lane;
+      int sp = 0, sa = 0;
+      uint32_t pp = 0, pa = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        for (int ks = 0; ks < NKS && ok; ks += 2) {
+          ok = wait_bar(&p_full[sp], pp, ctl);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          const uint8_t* prow = sA + sp * C::A_BYTES + mat * C::A_MAT + r * 128;
+          uint4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const uint4*>(prow + ((i ^ (r & 7)) << 4));
+          // generic reads of the slot before the TMA (async proxy) refills it
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_empty[sp]);
+          if (++sp == C::SP) { sp = 0; pp ^= 1; }
+#pragma unroll
+          for (int hs = 0; hs < 2; ++hs) {
+            if (ks + hs >= NKS) break;
+            ok = wait_bar(&a_empty[sa], pa ^ 1, ctl);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 w4 = v[4 * hs + c];
+              const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                o[2 * (4 * c + q)] = w[q] & 0x0F0F0F0Fu;
+                o[2 * (4 * c + q) + 1] = (w[q] >> 4) & 0x0F0F0F0Fu;
+              }
+            }
+            tc_fence_after();
+            tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + C::ACC_TOTAL + sa * C::A_TCOLS + mat * (KS / 4),
+                      o);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[sa]);
+            if (++sa == C::SAT) { sa = 0; pa ^= 1; }
+          }
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -617,18 +716,20 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
 // 128-row output tiles.
 static bool supported(const sg_arena* A, bool dual, int grid_groups) {
   const int K = dual ? A->hidden : A->inter, OUT = dual ? A->inter : A->hidden;
-  return A->bits == 8 && A->group_size == GSZ && K % KS == 0 && (K / GSZ) % 8 == 0 && K / GSZ <= Cfg<16>::GMAX &&
-         OUT % (dual ? BM : 2 * BM) == 0 && grid_groups <= PLAN_MAX_GROUPS;
+  // 4-bit stages hold two K stages each; whole scale chunks of 8 groups
+  return (A->bits == 8 || A->bits == 4) && A->group_size == GSZ && K % (A->bits == 4 ? 2 * KS : KS) == 0 &&
+         (K / GSZ) % 8 == 0 && K / GSZ <= Cfg<8, 16>::GMAX && OUT % (dual ? BM : 2 * BM) == 0 &&
+         grid_groups <= PLAN_MAX_GROUPS;
 }
 
-template <int MODE>
+template <int BITS, int MODE>
 static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
   constexpr int BN = 16;
-  using C = Cfg<BN>;
+  using C = Cfg<BITS, BN>;
   constexpr bool DUAL = MODE == 1;
   const int K = args.K;
   const uint64_t rows_total = (uint64_t)A->num_slots * args.OUT;
-  const uint64_t words = (uint64_t)K / 4;
+  const uint64_t words = (uint64_t)K * BITS / 32;
   const uint64_t groups = (uint64_t)K / GSZ;
   const void* w0 = DUAL ? A->gate_w : A->down_w;
   const void* w1 = DUAL ? A->up_w : A->down_w;
@@ -650,10 +751,11 @@ static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
   SG_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
   if (!attr_done[dev]) {
-    SG_CUDA_TRY(cudaFuncSetAttribute(glu_i8_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    SG_CUDA_TRY(cudaFuncSetAttribute(glu_i8_kernel<BITS, MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::SMEM));
     attr_done[dev] = true;
   }
-  glu_i8_kernel<MODE, BN><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, ms0, mq0, ms1, mq1, args);
+  glu_i8_kernel<BITS, MODE, BN><<<num_sms(), C::THREADS, C::SMEM, s>>>(m0, m1, ms0, mq0, ms1, mq1, args);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -694,7 +796,8 @@ int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const floa
   a.out_by_pos = out_by_pos;
   a.max_groups = grid_groups;
   a.out = out;
-  return dual ? i8::launch<1>(A, a, s) : i8::launch<2>(A, a, s);
+  if (A->bits == 4) return dual ? i8::launch<4, 1>(A, a, s) : i8::launch<4, 2>(A, a, s);
+  return dual ? i8::launch<8, 1>(A, a, s) : i8::launch<8, 2>(A, a, s);
 }
 
 }  // namespace sg

@@ -170,6 +170,7 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int =
     nwork = lib.sg_glu_gate_up_work_bytes(desc, P, int(pair_div), d.grid_groups, int(flags))
     if nwork < 0:
         _abi.check(int(nwork), "sg_glu_gate_up_work_bytes")
+    LAST_GATE_UP[0] = "sg_glu_gate_up_work (piece split + integer-operand tcgen05)" if nwork > 0 else "sg_glu_gate_up"
     if nwork > 0:  # 8-bit arena at decode sizes: the token rows' pieces, then the integer-operand kernel
         work = torch.empty(int(nwork), dtype=torch.uint8, device=x.device)
         LAUNCHES[0] += 2
@@ -183,6 +184,10 @@ def glu_gate_up(arena, x: torch.Tensor, d: Dispatch, pair_div: int, flags: int =
                                   d.slot_ids.data_ptr(), d.group_off.data_ptr(), d.perm.data_ptr(), d.grid_groups,
                                   h.data_ptr(), int(flags), _stream()), "sg_glu_gate_up")
     return h
+
+
+# which entry point the last glu_gate_up call took (for reports)
+LAST_GATE_UP = ["sg_glu_gate_up"]
 
 
 def quantize_pieces(x: torch.Tensor, order: int = 0) -> tuple[torch.Tensor, torch.Tensor]:

@@ -94,8 +94,10 @@ def test_host_side_argument_checks(lib):
         assert lib.sg_set_glu_path(mode) == _abi.SG_OK
         assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == want
     assert lib.sg_set_glu_path(0) == _abi.SG_OK
-    q8.bits = 4  # 4-bit arenas keep the dequantising kernels
-    assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == 0
+    q8.bits = 4  # 4-bit arenas: the same pieces (unpacked nibbles feed the same kernel)
+    assert lib.sg_glu_gate_up_work_bytes(ctypes.byref(q8), 2560, 10, 512, 0) == pieces
+    q8.bits, q8.inter = 4, 768  # I = 768: 12 groups per down row, not whole scale chunks of 8
+    assert lib.sg_glu_down_work_bytes(ctypes.byref(q8), 2560, 512) == 0
     # expert-parallel exchange: argument checks and the region layout (no GPU touched)
     assert lib.sg_ep_region_bytes(9, 16, 256) == _abi.SG_ERR_INVALID_ARG  # more than 8 ranks
     assert lib.sg_ep_region_bytes(2, 16, 100) == _abi.SG_ERR_SHAPE        # H % 8

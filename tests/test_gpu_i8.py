@@ -1,4 +1,4 @@
-"""GPU: the integer-operand kernels (8-bit arenas at decode tile widths).
+"""GPU: the integer-operand kernels (8- and 4-bit arenas at decode tile widths).
 
 * sg_quantize_pieces against a numpy statement of the piece split (exact);
 * h through the integer-operand gate/up against the CPU oracle within the
@@ -97,9 +97,9 @@ def _h_oracle(tens, bits, x, inds, k, I):
     return href
 
 
-def _exact_down(tens, e):
+def _exact_down(tens, e, bits):
     """scale * q + bias of expert e's down projection in float64 (no rounding)."""
-    q = orc.unpack_affine(tens["experts"]["down_proj.weight"][int(e)].cpu().numpy().view(np.uint32), 8)
+    q = orc.unpack_affine(tens["experts"]["down_proj.weight"][int(e)].cpu().numpy().view(np.uint32), bits)
     sc = f32(tens["experts"]["down_proj.scales"][int(e)]).astype(np.float64)
     bi = f32(tens["experts"]["down_proj.biases"][int(e)]).astype(np.float64)
     return q.astype(np.float64) * np.repeat(sc, 64, axis=1) + np.repeat(bi, 64, axis=1)
@@ -117,8 +117,9 @@ def i8_path():
                                        (4096, 1024, 16, 9, 4), (512, 512, 8, 7, 3),
                                        # ~40 pairs per group: three 16-pair tiles per group, the last partial
                                        (1024, 384, 4, 80, 2), (1024, 512, 4, 80, 2)])
-def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
-    cfg = LayerConfig("t", 9, H, E, k, I, None, 8, E)
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gate_up_i8_matches_oracle(i8_path, bits, H, I, E, T, k):
+    cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((T, H), 11)
     g = np.random.default_rng(T * 7 + E)
@@ -127,7 +128,7 @@ def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
     arena = block.switch_mlp
     assert _abi.load().sg_glu_gate_up_work_bytes(ctypes.byref(arena.desc()), T * k, k, d.grid_groups, 0) > 0
     h = ops.glu_gate_up(arena, x, d, pair_div=k)
-    href = _h_oracle(tens, 8, x, inds, k, I)
+    href = _h_oracle(tens, bits, x, inds, k, I)
     assert_close(f32(h), href, max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="h")
     # against the dequantising tensor-core kernel
     ops.set_glu_path("tc")
@@ -139,7 +140,7 @@ def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
     down_i8 = _abi.load().sg_glu_down_work_bytes(ctypes.byref(arena.desc()), T * k, d.grid_groups) > 0
     assert down_i8 == (I % 512 == 0 and H % 256 == 0)
     y = ops.glu_down(arena, h, d)
-    ex = LazyExperts(tens["experts"], 8)
+    ex = LazyExperts(tens["experts"], bits)
     hdev = f32(h)
     ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
     if down_i8:
@@ -150,7 +151,7 @@ def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
         # of its group's largest magnitude), summed through |w| as a bound
         assert_close(f32(y), ydown, what="y|h")
         for p in range(T * k):
-            w = _exact_down(tens, inds.reshape(-1)[p])
+            w = _exact_down(tens, inds.reshape(-1)[p], bits)
             hp = hdev[p].astype(np.float64)
             gmax = np.repeat(np.abs(hp).reshape(-1, 64).max(axis=1), 64)
             bound = 2.0 ** -8 * np.abs(hp @ w.T) + 2.0 ** -14 * (np.abs(w) @ gmax) + 1e-6
@@ -166,9 +167,10 @@ def test_gate_up_i8_matches_oracle(i8_path, H, I, E, T, k):
     assert torch.equal(ops.glu_gate_up(arena, x, d, pair_div=k), h)
 
 
-def test_gate_up_i8_rows_in_dispatch_order(i8_path):
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gate_up_i8_rows_in_dispatch_order(i8_path, bits):
     H, I, E, T, k = 1024, 256, 8, 24, 2
-    cfg = LayerConfig("t", 9, H, E, k, I, None, 8, E)
+    cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((T, H), 13)
     g = np.random.default_rng(3)
@@ -181,16 +183,17 @@ def test_gate_up_i8_rows_in_dispatch_order(i8_path):
     assert torch.equal(h_pos, h_ref)
 
 
-def test_gate_up_i8_missing_slots(i8_path):
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gate_up_i8_missing_slots(i8_path, bits):
     H, I, E = 512, 512, 4
-    cfg = LayerConfig("t", 9, H, E, 1, I, None, 8, E)
+    cfg = LayerConfig("t", 9, H, E, 1, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((3, H), 12)
     inds = torch.tensor([[0], [1], [2]], dtype=torch.int32, device=DEV)
     d = ops.dispatch(inds, E, torch.tensor([0, -1, 2, 3], dtype=torch.int32, device=DEV))
     h = ops.glu_gate_up(block.switch_mlp, x, d, pair_div=1)
     assert torch.all(h[1] == 0) and torch.any(h[0] != 0)
-    href = _h_oracle(tens, 8, x, np.array([0, -1, 2]), 1, I)
+    href = _h_oracle(tens, bits, x, np.array([0, -1, 2]), 1, I)
     assert_close(f32(h[[0, 2]]), href[[0, 2]], max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what="h")
     # the down projection writes zeros for the pairs of the missing slot too
     y = ops.glu_down(block.switch_mlp, h, d)
