@@ -270,6 +270,11 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
  * its own gather_mm kernels). */
 int sg_set_glu_path(int mode);
 
+/* Pair-tile width of the integer-operand kernels: 0 = automatic (8 while
+ * groups average at most 6 pairs, else 16), 8 or 16 to force one.
+ * Process-wide.  No counterpart in the reference. */
+int sg_set_glu_tile(int bn);
+
 /* First error a kernel of this library recorded on the current device since
  * the last reset (SG_OK if none; SG_ERR_TIMEOUT when a bounded wait inside a
  * kernel expired and the kernel gave up).  Synchronises with the device.

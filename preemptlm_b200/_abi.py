@@ -32,7 +32,7 @@ EXPORTED_SYMBOLS = (
     "sg_permute_rows", "sg_glu_gate_up", "sg_glu_gate_up_work_bytes", "sg_glu_gate_up_work", "sg_quantize_pieces",
     "sg_glu_down", "sg_glu_down_work_bytes", "sg_glu_down_work",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
-    "sg_expert_bytes", "sg_set_glu_path", "sg_device_status",
+    "sg_expert_bytes", "sg_set_glu_path", "sg_set_glu_tile", "sg_device_status",
     "sg_ep_region_bytes", "sg_ep_layout", "sg_ep_alloc", "sg_ep_free", "sg_ep_ipc_handle", "sg_ep_ipc_open",
     "sg_ep_ipc_close", "sg_ep_send", "sg_ep_wait_inbox", "sg_ep_send_back", "sg_ep_wait_back",
     "sg_ep_set_wait_limit",
@@ -103,6 +103,7 @@ def load() -> ctypes.CDLL:
         "sg_glu_down": (I32, [A, P, I32, P, P, P, P, I32, P, I32, P]),
         "sg_dense_glu": (I32, [A, I32, P, I32, P, P, P]),
         "sg_set_glu_path": (I32, [I32]),
+        "sg_set_glu_tile": (I32, [I32]),
         "sg_device_status": (I32, [I32]),
         "sg_combine": (I32, [P, P, I32, I32, I32, P, P, P, P]),
         "sg_refill_h2d": (I32, [P, SZ, A, I32, P]),

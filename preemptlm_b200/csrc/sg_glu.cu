@@ -318,7 +318,9 @@ int tc_dense_launch(const sg_arena* A, bool dual, const uint16_t* in, int rows, 
 bool i8_supported(const sg_arena* A, bool dual, int grid_groups);
 int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const float* ex, int in_rows, int pair_div,
                   int in_by_pos, int out_by_pos, const int32_t* counts, const int32_t* slot_ids,
-                  const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s);
+                  const int32_t* group_off, const int32_t* perm, int grid_groups, int num_pairs, uint16_t* out,
+                  cudaStream_t s);
+int set_i8_tile(int bn);
 int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s);
 // 0 auto, 1 streaming GEMV, 2 tcgen05 (dequantising), 3 tcgen05 over permuted
 // rows, 4 tcgen05 with the integer-operand gate/up wherever it applies
@@ -380,8 +382,8 @@ static size_t pieces_bytes(const sg_arena* A, bool dual, int rows, size_t* ex_of
 }
 
 // Input rows' pieces into `work`, then the integer-operand kernel.
-static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int pair_div, int in_pos,
-                  int out_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
+static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int num_pairs, int pair_div,
+                  int in_pos, int out_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
                   const int32_t* perm, int grid_groups, uint16_t* out, void* work, size_t work_bytes,
                   cudaStream_t s) {
   size_t ex_off = 0;
@@ -392,7 +394,7 @@ static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
   int st = quantize_pieces(in, in_rows, dual ? A->hidden : A->inter, A->bits == 4 ? 1 : 0, pieces, ex, s);
   if (st) return st;
   return i8_glu_launch(A, dual, pieces, ex, in_rows, pair_div, in_pos, out_pos, counts, slot_ids, group_off, perm,
-                       grid_groups, out, s);
+                       grid_groups, num_pairs, out, s);
 }
 
 // xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
@@ -414,8 +416,8 @@ static int glu_dual(const sg_arena* arena, const uint16_t* x, int num_pairs, int
   const int div = in_pos ? 1 : pair_div;
   if (work && use_i8(arena, true, num_pairs, grid_groups)) {
     const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
-    return i8_run(arena, true, x, in_rows, div, in_pos, out_pos, counts, slot_ids, group_off, perm, grid_groups, h,
-                  work, work_bytes, s);
+    return i8_run(arena, true, x, in_rows, num_pairs, div, in_pos, out_pos, counts, slot_ids, group_off, perm,
+                  grid_groups, h, work, work_bytes, s);
   }
   if (use_tc(arena, true, num_pairs, grid_groups)) {
     const int in_rows = in_pos ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
@@ -434,8 +436,8 @@ static int glu_single(const sg_arena* arena, const uint16_t* h, int num_pairs, c
                       uint16_t* y, int flags, cudaStream_t s, void* work = nullptr, size_t work_bytes = 0) {
   const int in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0, out_pos = (flags & SG_OUT_DISPATCH_ORDER) != 0;
   if (work && use_i8(arena, false, num_pairs, grid_groups))
-    return i8_run(arena, false, h, num_pairs, 1, in_pos, out_pos, counts, slot_ids, group_off, perm, grid_groups, y,
-                  work, work_bytes, s);
+    return i8_run(arena, false, h, num_pairs, num_pairs, 1, in_pos, out_pos, counts, slot_ids, group_off, perm,
+                  grid_groups, y, work, work_bytes, s);
   if (use_tc(arena, false, num_pairs, grid_groups))
     return tc_glu_launch(arena, false, h, num_pairs, 1, in_pos, out_pos, num_pairs, counts, slot_ids, group_off, perm,
                          grid_groups, y, s);
@@ -455,6 +457,8 @@ static int check_glu_args(const sg_arena* arena, int num_pairs, int pair_div, in
   return SG_OK;
 }
 }  // namespace sg
+
+extern "C" int sg_set_glu_tile(int bn) { return sg::set_i8_tile(bn); }
 
 extern "C" int sg_set_glu_path(int mode) {
   if (mode < 0 || mode > 4) return SG_ERR_INVALID_ARG;

@@ -43,7 +43,7 @@ using namespace tc;
 
 constexpr int KS = 128;         // K per pipeline stage: one 128-byte swizzle atom of 8-bit operands
 constexpr int GSZ = 64;         // quantisation group
-constexpr int RING = 8;         // group accumulators in tensor memory
+constexpr int TILE8_MAX = 6;    // 8-pair tiles while groups average at most this many pairs
 constexpr int PIECE_BITS = 14;  // the group maximum maps below 2^PIECE_BITS
 
 // ------------------------------------------------------------------ pieces
@@ -158,7 +158,8 @@ struct Cfg {
   static constexpr int X_STRIDE = BN + 4;            // hand-off rows: BN fp32 + padding
   static constexpr int X_BYTES = BM * X_STRIDE * 4;
   static constexpr int ACC_COLS = 2 * NB;            // one group: gate and up, NB columns each
-  static constexpr int RINGN = Q4 ? 4 : RING;        // group accumulators in flight
+  // group accumulators in flight: what tensor memory leaves after the A stages
+  static constexpr int RINGN = cmin(16, (512 - SAT * A_TCOLS) / ACC_COLS);
   static constexpr int ACC_TOTAL = RINGN * ACC_COLS;
   static constexpr int TMEM_COLS = ACC_TOTAL + SAT * A_TCOLS;
   static constexpr int OFF_A = 0;
@@ -209,6 +210,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+
+// NB columns of the warp's 32 lanes: the hi sums of the tile's pairs, then the lo sums
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[32]) { tmem_ld32(taddr, r); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
 
 struct Args {
   int num_slots, K, OUT;
@@ -468,9 +473,10 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------------- piece rows + pair table
-    // lane l copies chunk l % 8 of B rows l / 8 + 4 i (i = 0..7): pair
+    // lane l copies chunk l % 8 of B rows l / 8 + 4 i (i < 2 BN / 4): pair
     // (l / 8 + 4 i) % BN, plane (hi / lo) (l / 8 + 4 i) / BN
-    static_assert(BN == 16, "the row split below assumes 16 pairs per tile");
+    static_assert(BN == 8 || BN == 16, "8 or 16 pairs per tile");
+    constexpr int RPL = BN / 4;  // pairs per lane
     const int c = lane & 7, r0 = lane >> 3;
     const size_t prow_bytes = static_cast<size_t>(2) * K;
     int sb = 0, it = 0;
@@ -485,9 +491,9 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         const int rw = args.in_by_pos ? pos : args.perm[pos] / args.pair_div;
         myrow = (rw >= 0 && rw < args.in_rows) ? rw : -1;
       }
-      int row[4];
+      int row[RPL];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) row[q] = __shfl_sync(0xffffffffu, myrow, r0 + 4 * q);
+      for (int q = 0; q < RPL; ++q) row[q] = __shfl_sync(0xffffffffu, myrow, r0 + 4 * q);
       // the pairs' (E, X) per group, transposed to [group][E, X][pair]
       const int buf = it & 1;
       ok = wait_bar(&t_empty[buf], ((it >> 1) & 1) ^ 1, ctl, BACKOFF_NS);
@@ -510,12 +516,12 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         uint8_t* dst = sB + sb * C::B_BYTES;
         const int8_t* col = args.pieces + ks * KS + c * 16;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 2 * RPL; ++i) {
           const int rr = r0 + 4 * i;  // B row: pair rr % BN, plane rr / BN
-          const int rw = row[i & 3];
+          const int rw = row[i % RPL];
           const bool v = rw >= 0;
           cp_async16(dst + rr * KS + ((c ^ (rr & 7)) << 4),
-                     v ? col + rw * prow_bytes + (i >= 4 ? K : 0) : args.pieces, v ? 16u : 0u);
+                     v ? col + rw * prow_bytes + (i >= RPL ? K : 0) : args.pieces, v ? 16u : 0u);
         }
         cp_async_arrive(&b_full[sb]);
         if (++sb == C::SB) { sb = 0; pb ^= 1; }
@@ -562,8 +568,8 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
           ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
           if (!ok) break;
           tc_fence_after();
-          uint32_t a[32];
-          tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + slot * C::ACC_COLS + mat * NB, a);
+          uint32_t a[NB];
+          tmem_ld_cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + slot * C::ACC_COLS + mat * NB, a);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
@@ -722,9 +728,8 @@ static bool supported(const sg_arena* A, bool dual, int grid_groups) {
          grid_groups <= PLAN_MAX_GROUPS;
 }
 
-template <int BITS, int MODE>
+template <int BITS, int MODE, int BN>
 static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
-  constexpr int BN = 16;
   using C = Cfg<BITS, BN>;
   constexpr bool DUAL = MODE == 1;
   const int K = args.K;
@@ -775,11 +780,27 @@ int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* piece
 
 bool i8_supported(const sg_arena* A, bool dual, int grid_groups) { return i8::supported(A, dual, grid_groups); }
 
+// Pair-tile width of the integer-operand kernels: 8 (twice the accumulators
+// in flight, half the epilogue per group) while groups average at most
+// i8::TILE8_MAX pairs, else 16; sg_set_glu_tile forces one.
+static int g_i8_tile = 0;
+int i8_tile_width(int num_pairs, int grid_groups) {
+  if (g_i8_tile) return g_i8_tile;
+  const int avg = (num_pairs + grid_groups - 1) / (grid_groups > 0 ? grid_groups : 1);
+  return avg <= i8::TILE8_MAX ? 8 : 16;
+}
+int set_i8_tile(int bn) {
+  if (bn != 0 && bn != 8 && bn != 16) return SG_ERR_INVALID_ARG;
+  g_i8_tile = bn;
+  return SG_OK;
+}
+
 // dual: gate/up + SwiGLU (K = hidden, OUT = inter); else the down projection
 // (K = inter, OUT = hidden).
 int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const float* ex, int in_rows, int pair_div,
                   int in_by_pos, int out_by_pos, const int32_t* counts, const int32_t* slot_ids,
-                  const int32_t* group_off, const int32_t* perm, int grid_groups, uint16_t* out, cudaStream_t s) {
+                  const int32_t* group_off, const int32_t* perm, int grid_groups, int num_pairs, uint16_t* out,
+                  cudaStream_t s) {
   i8::Args a;
   a.num_slots = A->num_slots;
   a.K = dual ? A->hidden : A->inter;
@@ -796,8 +817,13 @@ int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const floa
   a.out_by_pos = out_by_pos;
   a.max_groups = grid_groups;
   a.out = out;
-  if (A->bits == 4) return dual ? i8::launch<4, 1>(A, a, s) : i8::launch<4, 2>(A, a, s);
-  return dual ? i8::launch<8, 1>(A, a, s) : i8::launch<8, 2>(A, a, s);
+  const int bn = i8_tile_width(num_pairs, grid_groups);
+  if (bn == 8) {
+    if (A->bits == 4) return dual ? i8::launch<4, 1, 8>(A, a, s) : i8::launch<4, 2, 8>(A, a, s);
+    return dual ? i8::launch<8, 1, 8>(A, a, s) : i8::launch<8, 2, 8>(A, a, s);
+  }
+  if (A->bits == 4) return dual ? i8::launch<4, 1, 16>(A, a, s) : i8::launch<4, 2, 16>(A, a, s);
+  return dual ? i8::launch<8, 1, 16>(A, a, s) : i8::launch<8, 2, 16>(A, a, s);
 }
 
 }  // namespace sg

@@ -353,6 +353,11 @@ def set_glu_path(mode: str) -> None:
     _GLU_PATH[0] = mode
 
 
+def set_glu_tile(bn: int) -> None:
+    """Pair-tile width of the integer-operand kernels: 0 (automatic), 8 or 16."""
+    _abi.call("sg_set_glu_tile", int(bn))
+
+
 def glu_path() -> str:
     return _GLU_PATH[0]
 

@@ -110,6 +110,7 @@ def i8_path():
     ops.set_glu_path("i8")
     yield
     ops.set_glu_path("auto")
+    ops.set_glu_tile(0)
     assert ops.device_status(reset=True) == 0
 
 
@@ -118,7 +119,9 @@ def i8_path():
                                        # ~40 pairs per group: three 16-pair tiles per group, the last partial
                                        (1024, 384, 4, 80, 2), (1024, 512, 4, 80, 2)])
 @pytest.mark.parametrize("bits", [8, 4])
-def test_gate_up_i8_matches_oracle(i8_path, bits, H, I, E, T, k):
+@pytest.mark.parametrize("tile", [8, 16])
+def test_gate_up_i8_matches_oracle(i8_path, tile, bits, H, I, E, T, k):
+    ops.set_glu_tile(tile)
     cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
     block, tens = make_layer(cfg, device=DEV)
     x = _bf16((T, H), 11)
