@@ -561,36 +561,52 @@ glu_i8_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ 
         if (lane == 0) mbar_arrive(&s_empty[ss]);
         if (++ss == C::SS) { ss = 0; sph ^= 1; }
         const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        // GP groups per hand-off: both accumulators are loaded before one
+        // wait, so the load latency is paid once per GP groups
+        constexpr int GP = BN == 8 ? 2 : 1;
 #pragma unroll
-        for (int gi = 0; gi < 8; ++gi) {
-          const int slot = gc % C::RINGN;
-          ok = wait_bar(&acc_full[slot], (gc / C::RINGN) & 1, ctl);
+        for (int gi0 = 0; gi0 < 8; gi0 += GP) {
+          int slot[GP];
+#pragma unroll
+          for (int p = 0; p < GP; ++p) {
+            slot[p] = (gc + p) % C::RINGN;
+            if (ok) ok = wait_bar(&acc_full[slot[p]], ((gc + p) / C::RINGN) & 1, ctl);
+          }
           ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
           if (!ok) break;
           tc_fence_after();
-          uint32_t a[NB];
-          tmem_ld_cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + slot * C::ACC_COLS + mat * NB, a);
+          uint32_t a[GP][NB];
+#pragma unroll
+          for (int p = 0; p < GP; ++p)
+            tmem_ld_cols(tmem + (static_cast<uint32_t>(quad * 32) << 16) + slot[p] * C::ACC_COLS + mat * NB, a[p]);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[slot]);
-          ++gc;
-          const float s = (gi & 1) ? hi_bf16(sw[gi >> 1]) : lo_bf16(sw[gi >> 1]);
-          const float b = (gi & 1) ? hi_bf16(bw[gi >> 1]) : lo_bf16(bw[gi >> 1]);
-          const float* e = tp + (g8 + gi) * 2 * BN;
+          if (lane == 0) {
 #pragma unroll
-          for (int q = 0; q < BN / 4; ++q) {
-            if (q < nq) {
-              const float4 e4 = *reinterpret_cast<const float4*>(e + 4 * q);
-              const float4 x4 = *reinterpret_cast<const float4*>(e + BN + 4 * q);
-              const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, xv[4] = {x4.x, x4.y, x4.z, x4.w};
+            for (int p = 0; p < GP; ++p) mbar_arrive(&acc_empty[slot[p]]);
+          }
+          gc += GP;
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const int j = 4 * q + jj;
-                // 256 * sum(q hi) + sum(q lo): |.| < 2^28, exact in int32
-                const int qi = static_cast<int>(a[j]) * 256 + static_cast<int>(a[BN + j]);
-                const float f = __int2float_rn(qi) * ev[jj];
-                y[j] = fmaf(b, xv[jj], fmaf(f, s, y[j]));
+          for (int p = 0; p < GP; ++p) {
+            const int gi = gi0 + p;
+            const float s = (gi & 1) ? hi_bf16(sw[gi >> 1]) : lo_bf16(sw[gi >> 1]);
+            const float b = (gi & 1) ? hi_bf16(bw[gi >> 1]) : lo_bf16(bw[gi >> 1]);
+            const float* e = tp + (g8 + gi) * 2 * BN;
+#pragma unroll
+            for (int q = 0; q < BN / 4; ++q) {
+              if (q < nq) {
+                const float4 e4 = *reinterpret_cast<const float4*>(e + 4 * q);
+                const float4 x4 = *reinterpret_cast<const float4*>(e + BN + 4 * q);
+                const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                  const int j = 4 * q + jj;
+                  // 256 * sum(q hi) + sum(q lo): |.| < 2^28, exact in int32
+                  const int qi = static_cast<int>(a[p][j]) * 256 + static_cast<int>(a[p][BN + j]);
+                  const float f = __int2float_rn(qi) * ev[jj];
+                  y[j] = fmaf(b, xv[jj], fmaf(f, s, y[j]));
+                }
               }
             }
           }
