@@ -321,7 +321,9 @@ int i8_glu_launch(const sg_arena* A, bool dual, const int8_t* pieces, const floa
                   const int32_t* group_off, const int32_t* perm, int grid_groups, int num_pairs, uint16_t* out,
                   cudaStream_t s);
 int set_i8_tile(int bn);
-int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s);
+int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s,
+                    const int32_t* perm = nullptr, int pair_div = 1, int in_pos = 0,
+                    const int32_t* counts = nullptr, const int32_t* group_off = nullptr);
 // 0 auto, 1 streaming GEMV, 2 tcgen05 (dequantising), 3 tcgen05 over permuted
 // rows, 4 tcgen05 with the integer-operand gate/up wherever it applies
 static int g_glu_path = 0;
@@ -381,20 +383,34 @@ static size_t pieces_bytes(const sg_arena* A, bool dual, int rows, size_t* ex_of
   return p + (size_t)rows * (K / 64) * 8;
 }
 
+// Rows of pieces the integer-operand kernel reads: the token rows when several
+// pairs share one (pair_div > 1: the layer's top-k), else one row per pair
+// position in dispatch order (rows per pair: expert-parallel inboxes, h), of
+// which only the filled positions are split.
+static int piece_rows(bool dual, int in_rows, int num_pairs, int pair_div) {
+  return dual && pair_div > 1 ? in_rows : num_pairs;
+}
+
 // Input rows' pieces into `work`, then the integer-operand kernel.
 static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows, int num_pairs, int pair_div,
                   int in_pos, int out_pos, const int32_t* counts, const int32_t* slot_ids, const int32_t* group_off,
                   const int32_t* perm, int grid_groups, uint16_t* out, void* work, size_t work_bytes,
                   cudaStream_t s) {
+  const bool by_token = dual && pair_div > 1 && !in_pos;
+  const int rows = by_token ? in_rows : num_pairs;
   size_t ex_off = 0;
-  if (pieces_bytes(A, dual, in_rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
+  if (pieces_bytes(A, dual, rows, &ex_off) > work_bytes) return SG_ERR_CAPACITY;
   int8_t* pieces = static_cast<int8_t*>(work);
   float* ex = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + ex_off);
   // 4-bit weights unpack with nibbles 0,2,4,6 before 1,3,5,7: the pieces follow that order
-  int st = quantize_pieces(in, in_rows, dual ? A->hidden : A->inter, A->bits == 4 ? 1 : 0, pieces, ex, s);
+  const int order = A->bits == 4 ? 1 : 0;
+  const int K = dual ? A->hidden : A->inter;
+  int st = by_token ? quantize_pieces(in, rows, K, order, pieces, ex, s)
+                    : quantize_pieces(in, rows, K, order, pieces, ex, s, perm, pair_div, in_pos, counts, group_off);
   if (st) return st;
-  return i8_glu_launch(A, dual, pieces, ex, in_rows, pair_div, in_pos, out_pos, counts, slot_ids, group_off, perm,
-                       grid_groups, num_pairs, out, s);
+  // per-pair pieces are in dispatch order: the kernel reads row pos
+  return i8_glu_launch(A, dual, pieces, ex, rows, by_token ? pair_div : 1, by_token ? 0 : 1, out_pos, counts,
+                       slot_ids, group_off, perm, grid_groups, num_pairs, out, s);
 }
 
 // xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
@@ -509,7 +525,9 @@ namespace sg {
 // or the pieces of the token rows for the integer-operand gate/up and then,
 // in the same bytes, the pieces of h for the integer-operand down projection.
 static size_t forward_scratch(const sg_arena* A, int P, int pair_div, int gg, size_t* gu, size_t* dn) {
-  *gu = use_i8(A, true, P, gg) ? pieces_bytes(A, true, (P + pair_div - 1) / pair_div, nullptr) : 0;
+  *gu = use_i8(A, true, P, gg) ? pieces_bytes(A, true, piece_rows(true, (P + pair_div - 1) / pair_div, P, pair_div),
+                                              nullptr)
+                                 : 0;
   *dn = use_i8(A, false, P, gg) ? pieces_bytes(A, false, P, nullptr) : 0;
   if (use_permute(A, P, gg)) return (size_t)P * A->hidden * 2;
   return *gu > *dn ? *gu : *dn;
@@ -558,8 +576,9 @@ extern "C" long long sg_glu_gate_up_work_bytes(const sg_arena* arena, int num_pa
   const int st = sg::check_glu_args(arena, num_pairs, pair_div, grid_groups, flags);
   if (st) return st;
   if (num_pairs == 0 || grid_groups == 0 || !sg::use_i8(arena, true, num_pairs, grid_groups)) return 0;
-  const int in_rows = (flags & SG_IN_DISPATCH_ORDER) ? num_pairs : (num_pairs + pair_div - 1) / pair_div;
-  return (long long)sg::pieces_bytes(arena, true, in_rows, nullptr);
+  const bool in_pos = (flags & SG_IN_DISPATCH_ORDER) != 0;
+  const int rows = in_pos ? num_pairs : sg::piece_rows(true, (num_pairs + pair_div - 1) / pair_div, num_pairs, pair_div);
+  return (long long)sg::pieces_bytes(arena, true, rows, nullptr);
 }
 
 extern "C" int sg_glu_gate_up_work(const sg_arena* arena, const uint16_t* x, int num_pairs, int pair_div,

@@ -71,17 +71,27 @@ __device__ __forceinline__ int piece_value(uint32_t b16, int eM) {
 // One thread per 8 elements, 8 threads per 64-group.  ORDER 0: pieces in k
 // order; ORDER 1 (4-bit arenas): within every 8 elements the order
 // 0, 2, 4, 6, 1, 3, 5, 7, the order of the unpacked nibbles.
+// Dispatch mode (perm != nullptr): output row pos < rows holds the pieces of
+// input row perm[pos] / pair_div (or pos when in_pos), for the pair positions
+// pos < group_off[counts[0]] only -- expert-parallel inboxes are padded, and
+// their unused entries are never read.
 __global__ void __launch_bounds__(256)
 quantize_pieces_kernel(const uint16_t* __restrict__ x, int rows, int K, int order, int8_t* __restrict__ pieces,
-                       float* __restrict__ ex) {
+                       float* __restrict__ ex, const int32_t* __restrict__ perm, int pair_div, int in_pos,
+                       const int32_t* __restrict__ counts, const int32_t* __restrict__ group_off) {
   const int G = K / GSZ;
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // chunk of 8 elements
   const long long nchunks = (long long)rows * (K / 8);
-  const bool live = t < nchunks;
+  bool live = t < nchunks;
   const long long ci = live ? t : 0;
   const int row = static_cast<int>(ci / (K / 8));
   const int c = static_cast<int>(ci - (long long)row * (K / 8));  // chunk within the row
-  const uint4 v = live ? ldg_nc_v4(x + (size_t)row * K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+  int src = row;
+  if (perm) {  // the 8 threads of a group share the row, so they agree on `live`
+    live = live && row < group_off[counts[0]];
+    src = live ? (in_pos ? row : perm[row] / pair_div) : 0;
+  }
+  const uint4 v = live ? ldg_nc_v4(x + (size_t)src * K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t b[8];
 #pragma unroll
@@ -783,13 +793,17 @@ static int launch(const sg_arena* A, const Args& args, cudaStream_t s) {
 
 }  // namespace i8
 
-// Pieces of `rows` rows of K bf16 values (see sg_quantize_pieces).
-int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s) {
+// Pieces of `rows` rows of K bf16 values (see sg_quantize_pieces); with
+// perm, of the rows the pair positions use, in dispatch order (above).
+int quantize_pieces(const uint16_t* x, int rows, int K, int order, int8_t* pieces, float* ex, cudaStream_t s,
+                    const int32_t* perm, int pair_div, int in_pos, const int32_t* counts,
+                    const int32_t* group_off) {
   if (rows == 0) return SG_OK;
   const long long chunks = (long long)rows * (K / 8);
   const long long blocks = (chunks + 255) / 256;
   if (blocks > 0x7FFFFFFFLL) return SG_ERR_SHAPE;
-  i8::quantize_pieces_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, K, order, pieces, ex);
+  i8::quantize_pieces_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, K, order, pieces, ex, perm,
+                                                                           pair_div, in_pos, counts, group_off);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }

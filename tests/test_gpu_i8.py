@@ -201,3 +201,31 @@ def test_gate_up_i8_missing_slots(i8_path, bits):
     # the down projection writes zeros for the pairs of the missing slot too
     y = ops.glu_down(block.switch_mlp, h, d)
     assert torch.all(y[1] == 0) and torch.any(y[0] != 0)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_i8_padded_inbox_rows(i8_path, bits):
+    """Rows per pair with unused entries (an expert-parallel inbox: id -1):
+    only the filled entries are split into pieces and computed, and they match
+    the dequantising kernels."""
+    H, I, E, N = 1024, 512, 8, 96
+    cfg = LayerConfig("t", 9, H, E, 1, I, None, bits, E)
+    block, _ = make_layer(cfg, device=DEV)
+    arena = block.switch_mlp
+    rows = _bf16((N, H), 21)
+    g = np.random.default_rng(5)
+    eids = g.integers(0, E, N).astype(np.int32)
+    eids[g.random(N) < 0.6] = -1  # about 60 % of the inbox unused
+    d = ops.dispatch(torch.from_numpy(eids).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    valid = torch.from_numpy(eids >= 0).to(DEV)
+    h = ops.glu_gate_up(arena, rows, d, 1, _abi.SG_OUT_DISPATCH_ORDER)
+    y = ops.glu_down(arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
+    ops.set_glu_path("tc")
+    h_tc = ops.glu_gate_up(arena, rows, d, 1, _abi.SG_OUT_DISPATCH_ORDER)
+    y_tc = ops.glu_down(arena, h_tc, d, _abi.SG_IN_DISPATCH_ORDER)
+    ops.set_glu_path("i8")
+    nvalid = int(valid.sum().item())
+    scale = max(1.0, float(f32(h_tc[:nvalid]).__abs__().max()))
+    assert_close(f32(h[:nvalid]), f32(h_tc[:nvalid]), max_abs=2e-2 * scale, what="h")
+    # y rows of filled entries (pair order), against the dequantising kernels
+    assert_close(f32(y[valid]), f32(y_tc[valid]), what="y")
