@@ -183,9 +183,17 @@ int sg_glu_forward_noalloc(const sg_arena* arena, const uint16_t* x, int num_pai
 /* 1 when sg_glu_forward permutes the token rows for this problem size. */
 int sg_glu_use_permute(const sg_arena* arena, int num_pairs, int grid_groups);
 
-/* xs[pos, :] = x[perm[pos] / pair_div, :] for pos < num_pairs (H % 8 == 0). */
+/* xs[pos, :] = x[perm[pos] / pair_div, :] for pos < num_pairs (H % 8 == 0);
+ * every perm[pos] must be written (a dispatch of ids without -1 entries).
+ * sg_glu_forward permutes only the filled positions itself. */
 int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_div, int num_pairs, int H,
                     uint16_t* xs, void* stream);
+
+/* sg_permute_rows over the filled pair positions of a dispatch only (pos <
+ * group_off[counts[0]]), so ids of -1 (padded expert-parallel inboxes) are
+ * allowed; rows past the filled ones are left as they are. */
+int sg_permute_pairs(const uint16_t* x, const int32_t* perm, int pair_div, const int32_t* counts,
+                     const int32_t* group_off, int num_pairs, int H, uint16_t* xs, void* stream);
 
 /* The two halves of sg_glu_forward.  h[., I] = swiglu(x @ gate^T, x @ up^T)
  * per pair; rows in pair or dispatch order per `flags` (sg_glu_flags; input

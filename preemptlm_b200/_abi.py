@@ -29,7 +29,7 @@ SG_OUT_DISPATCH_ORDER = 2
 EXPORTED_SYMBOLS = (
     "sg_status_string", "sg_version", "sg_built_arch", "sg_router_logits", "sg_route_topk",
     "sg_dispatch", "sg_route_dispatch", "sg_host_device_ptr", "sg_glu_forward", "sg_glu_forward_noalloc", "sg_glu_forward_scratch_bytes", "sg_glu_use_permute",
-    "sg_permute_rows", "sg_glu_gate_up", "sg_glu_gate_up_work_bytes", "sg_glu_gate_up_work", "sg_quantize_pieces",
+    "sg_permute_rows", "sg_permute_pairs", "sg_glu_gate_up", "sg_glu_gate_up_work_bytes", "sg_glu_gate_up_work", "sg_quantize_pieces",
     "sg_glu_down", "sg_glu_down_work_bytes", "sg_glu_down_work",
     "sg_dense_glu", "sg_combine", "sg_refill_h2d",
     "sg_expert_bytes", "sg_set_glu_path", "sg_set_glu_tile", "sg_device_status",
@@ -99,6 +99,7 @@ def load() -> ctypes.CDLL:
         "sg_glu_down_work_bytes": (ctypes.c_longlong, [A, I32, I32]),
         "sg_glu_down_work": (I32, [A, P, I32, P, P, P, P, I32, P, I32, P, ctypes.c_longlong, P]),
         "sg_permute_rows": (I32, [P, P, I32, I32, I32, P, P]),
+        "sg_permute_pairs": (I32, [P, P, I32, P, P, I32, I32, P, P]),
         "sg_glu_gate_up": (I32, [A, P, I32, I32, P, P, P, P, I32, P, I32, P]),
         "sg_glu_down": (I32, [A, P, I32, P, P, P, P, I32, P, I32, P]),
         "sg_dense_glu": (I32, [A, I32, P, I32, P, P, P]),

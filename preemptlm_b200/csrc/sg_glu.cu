@@ -413,12 +413,16 @@ static int i8_run(const sg_arena* A, bool dual, const uint16_t* in, int in_rows,
                        slot_ids, group_off, perm, grid_groups, num_pairs, out, s);
 }
 
-// xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.
+// xs[pos] = x[perm[pos] / pair_div]: one warp per row, 16-byte chunks.  With
+// counts / group_off, only the filled positions pos < group_off[counts[0]]
+// (ids of -1 leave perm's tail unwritten).
 __global__ void __launch_bounds__(256)
 permute_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm, int pair_div, int P, int H,
-                    uint16_t* __restrict__ xs) {
+                    uint16_t* __restrict__ xs, const int32_t* __restrict__ counts,
+                    const int32_t* __restrict__ group_off) {
   const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (pos >= P) return;
+  if (counts && pos >= group_off[counts[0]]) return;
   const int row = perm[pos] / pair_div;
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * H);
   uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)pos * H);
@@ -493,7 +497,20 @@ extern "C" int sg_permute_rows(const uint16_t* x, const int32_t* perm, int pair_
                                                                                             : SG_ERR_SHAPE;
   if (num_pairs == 0) return SG_OK;
   if (!x || !perm || !xs) return SG_ERR_INVALID_ARG;
-  sg::permute_rows_kernel<<<(num_pairs + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, perm, pair_div, num_pairs, H, xs);
+  sg::permute_rows_kernel<<<(num_pairs + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, perm, pair_div, num_pairs, H, xs,
+                                                                                  nullptr, nullptr);
+  SG_LAUNCH_CHECK();
+  return SG_OK;
+}
+
+extern "C" int sg_permute_pairs(const uint16_t* x, const int32_t* perm, int pair_div, const int32_t* counts,
+                                const int32_t* group_off, int num_pairs, int H, uint16_t* xs, void* stream) {
+  if (num_pairs < 0 || pair_div < 1) return SG_ERR_INVALID_ARG;
+  if (H < 8 || H % 8) return SG_ERR_SHAPE;
+  if (num_pairs == 0) return SG_OK;
+  if (!x || !perm || !counts || !group_off || !xs) return SG_ERR_INVALID_ARG;
+  sg::permute_rows_kernel<<<(num_pairs + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, perm, pair_div, num_pairs, H, xs,
+                                                                                  counts, group_off);
   SG_LAUNCH_CHECK();
   return SG_OK;
 }
@@ -547,8 +564,10 @@ extern "C" int sg_glu_forward(const sg_arena* arena, const uint16_t* x, int num_
   uint16_t* xs = static_cast<uint16_t*>(scratch);
   if (permute) {
     if (!xs) return SG_ERR_INVALID_ARG;
-    st = sg_permute_rows(x, perm, pair_div, num_pairs, arena->hidden, xs, stream);
-    if (st) return st;
+    // the filled positions only (the dispatch leaves perm's tail unwritten when ids hold -1)
+    sg::permute_rows_kernel<<<(num_pairs + 7) / 8, 256, 0, s>>>(x, perm, pair_div, num_pairs, arena->hidden, xs,
+                                                                 counts, group_off);
+    SG_LAUNCH_CHECK();
   }
   // h in dispatch order, so that the down projection's rows are contiguous.
   // Without scratch the integer-operand kernels are not used.

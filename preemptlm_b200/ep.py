@@ -108,20 +108,13 @@ class CudaBackend:
         # entries expected to be filled (a host hint; any bound >= the groups works)
         hint = -(-N * self.arena.num_slots // max(1, expected_pairs))
         d = replace(d, grid_groups=max(d.grid_groups, min(2048, hint)))
-        t = self.timing
-        if t is not None:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-            ev[0].record()
-        h = ops.glu_gate_up(self.arena, rows, d, 1, _abi.SG_OUT_DISPATCH_ORDER)
-        if t is not None:
-            ev[1].record()
-        y = ops.glu_down(self.arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
-        if t is not None:
-            ev[2].record()
-            t.setdefault("events", []).append(ev)
-            t.setdefault("dispatch", []).append(d.counts)
+        # the fused call: rows permuted into dispatch order first for large
+        # groups (TMA row loads), pieces of the filled entries for the
+        # integer-operand kernels at decode sizes
+        y = ops.gather_forward(self.arena, rows, d, 1, timing=self.timing)
+        if self.timing is not None:
             # filled entries (group_off[U]): read after timing
-            t.setdefault("rows", []).append((d.counts, d.group_off))
+            self.timing.setdefault("rows", []).append((d.counts, d.group_off))
         return y
 
     def shared_terms(self, x: torch.Tensor):

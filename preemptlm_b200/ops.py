@@ -237,14 +237,16 @@ def glu_down(arena, h: torch.Tensor, d: Dispatch, flags: int = 0, out: torch.Ten
 
 
 def permute_rows(x: torch.Tensor, d: Dispatch, pair_div: int) -> torch.Tensor:
-    """xs[pos] = x[perm[pos] // pair_div] (``sg_permute_rows``)."""
+    """xs[pos] = x[perm[pos] // pair_div] for the dispatch's filled pair
+    positions (``sg_permute_pairs``; rows past them are left unset)."""
     x = _bf16_2d(x, "x")
     P = d.perm.numel()
     xs = torch.empty((P, x.shape[1]), dtype=torch.bfloat16, device=x.device)
     if P:
         LAUNCHES[0] += 1
-        _abi.check(_abi.load().sg_permute_rows(x.data_ptr(), d.perm.data_ptr(), int(pair_div), P, x.shape[1],
-                                               xs.data_ptr(), _stream()), "sg_permute_rows")
+        _abi.check(_abi.load().sg_permute_pairs(x.data_ptr(), d.perm.data_ptr(), int(pair_div), d.counts.data_ptr(),
+                                                d.group_off.data_ptr(), P, x.shape[1], xs.data_ptr(), _stream()),
+                   "sg_permute_pairs")
     return xs
 
 

@@ -418,3 +418,28 @@ def test_glu_prefill_tiles_every_element_and_repeatable(H, I, bits):
         worst = max(worst, float(((hs[0][a:b].float() - ref).abs() / scale).max()))
     assert worst <= 2e-2, f"worst element error {worst:.3e} of its row's scale"
     assert ops.device_status(reset=True) == 0
+
+
+def test_forward_padded_ids_prefill_groups():
+    """Rows per pair with unused entries (id -1, an expert-parallel inbox) and
+    prefill-sized groups: the fused call permutes only the filled positions
+    (perm's tail is never written) and matches the two halves called apart."""
+    from preemptlm_b200 import _abi
+
+    H, I, E, N = 1024, 512, 4, 640
+    cfg = LayerConfig("t", 9, H, E, 1, I, None, 4, E)
+    block, _ = make_layer(cfg, device=DEV)
+    arena = block.switch_mlp
+    rows = _bf16((N, H), 31)
+    g = np.random.default_rng(9)
+    eids = g.integers(0, E, N).astype(np.int32)
+    eids[g.random(N) < 0.5] = -1
+    d = ops.dispatch(torch.from_numpy(eids).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    import ctypes
+    assert _abi.load().sg_glu_use_permute(ctypes.byref(arena.desc()), N, d.grid_groups) == 1
+    y = ops.gather_forward(arena, rows, d, 1)
+    h = ops.glu_gate_up(arena, rows, d, 1, _abi.SG_OUT_DISPATCH_ORDER)
+    y2 = ops.glu_down(arena, h, d, _abi.SG_IN_DISPATCH_ORDER)
+    valid = torch.from_numpy(eids >= 0).to(DEV)
+    assert torch.equal(y[valid], y2[valid])
+    assert ops.device_status(reset=True) == 0
