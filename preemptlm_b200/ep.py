@@ -280,6 +280,14 @@ class ExpertParallelMoE:
         ops.LAUNCHES[0] += self._graph_launches
         return self.graph_output
 
+    def host_pipeline(self) -> "ops.HostPipeline":
+        """Replays of the captured step fed from and drained to pinned host
+        buffers, the copies overlapped with the neighbouring steps' compute
+        (``ops.HostPipeline``).  ``capture`` first."""
+        if self._graph is None:
+            raise RuntimeError("capture() first")
+        return ops.HostPipeline(self.graph_input, self.graph_output, self.replay)
+
     def check(self) -> None:
         """Read the device status word (synchronises): raise
         ``ExchangeTimeoutError`` if a bounded wait of an exchange kernel gave

@@ -400,6 +400,14 @@ class Qwen3_xMoEWrapper(SlotTable):
         ops.LAUNCHES[0] += self._graph_launches
         return self.graph_output
 
+    def host_pipeline(self) -> "ops.HostPipeline":
+        """Replays of the captured call fed from and drained to pinned host
+        buffers, with the copies overlapped with the neighbouring steps'
+        compute (``ops.HostPipeline``).  ``capture`` first."""
+        if getattr(self, "_graph", None) is None:
+            raise RuntimeError("capture() first")
+        return ops.HostPipeline(self.graph_input, self.graph_output, self.replay)
+
     def forward_resident(self, x2: torch.Tensor, timing: dict | None = None) -> torch.Tensor:
         """The non-streaming step on [T, H] with no host synchronisation at all
         (capturable in a CUDA graph): every expert is resident.  ``timing``

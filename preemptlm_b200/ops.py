@@ -382,3 +382,54 @@ def combine(y: torch.Tensor, scores: torch.Tensor, shared_y: torch.Tensor | None
     LAUNCHES[0] += T > 0
     _abi.call("sg_combine", y.data_ptr(), scores.contiguous().data_ptr(), T, k, H, sy, sg, out.data_ptr(), _stream())
     return out
+
+
+class HostPipeline:
+    """Host-buffer steps of a captured layer graph with the PCIe copies taken
+    off the critical path: the host->device copy of step i+1 (into a device
+    staging buffer, on an upload stream) and the device->host copy of step
+    i-1 (from a staging buffer, on a download stream) run while the graph of
+    step i computes.  The compute stream only moves the staged rows into and
+    out of the graph's own buffers (device copies of a few microseconds).
+
+    ``step(x_host, out_host)`` queues one step; ``out_host`` holds that step's
+    output once ``drain()`` (or a synchronisation) has passed.  Steps are
+    ordered as issued; ``depth`` staging buffers per direction."""
+
+    def __init__(self, graph_input: torch.Tensor, graph_output: torch.Tensor, replay, depth: int = 2):
+        dev = graph_input.device
+        self._dev, self._gin, self._gout, self._replay, self._depth = dev, graph_input, graph_output, replay, depth
+        self._up, self._down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        self._inb = [torch.empty_like(graph_input) for _ in range(depth)]
+        self._outb = [torch.empty_like(graph_output) for _ in range(depth)]
+        ev = lambda: [torch.cuda.Event() for _ in range(depth)]  # noqa: E731
+        self._in_ready, self._in_free, self._out_ready, self._out_free = ev(), ev(), ev(), ev()
+        self._i = 0
+
+    def step(self, x_host: torch.Tensor, out_host: torch.Tensor) -> None:
+        j, first = self._i % self._depth, self._i < self._depth
+        cur = torch.cuda.current_stream(self._dev)
+        with torch.cuda.stream(self._up):
+            if not first:  # the compute stream has taken staging buffer j's previous rows
+                self._up.wait_event(self._in_free[j])
+            self._inb[j].copy_(x_host.view_as(self._inb[j]), non_blocking=True)
+            self._in_ready[j].record(self._up)
+        cur.wait_event(self._in_ready[j])
+        self._gin.copy_(self._inb[j], non_blocking=True)
+        self._in_free[j].record(cur)
+        self._replay()
+        if not first:  # staging buffer j's previous output has reached the host
+            cur.wait_event(self._out_free[j])
+        self._outb[j].copy_(self._gout, non_blocking=True)
+        self._out_ready[j].record(cur)
+        with torch.cuda.stream(self._down):
+            self._down.wait_event(self._out_ready[j])
+            out_host.view_as(self._outb[j]).copy_(self._outb[j], non_blocking=True)
+            self._out_free[j].record(self._down)
+        self._i += 1
+
+    def drain(self) -> None:
+        """Make the current stream wait for every queued copy."""
+        cur = torch.cuda.current_stream(self._dev)
+        cur.wait_stream(self._up)
+        cur.wait_stream(self._down)
