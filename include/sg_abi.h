@@ -266,16 +266,16 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
                  void* stream);
 
 /* Kernel choice for sg_glu_forward / sg_glu_gate_up / sg_glu_down: 0 =
- * automatic (tcgen05 when the shape allows -- in-dim % 64, out-dim % 128,
- * <= 2048 groups -- and either the mean pairs per group is >= 2 or the
- * groups make at least one 128-row tile per SM; token rows permuted once the
- * mean reaches 32, and for 8-bit arenas the integer-operand kernels while
- * the mean is <= 16 and the caller passes a work area), 1 = streaming GEMV
- * always, 2 = the dequantising tcgen05 kernels whenever the shape allows,
- * 3 = as 2 with the token rows always permuted, 4 = as 0 with the
- * integer-operand kernels wherever they apply.
- * Process-wide.  No counterpart in the reference (MLX picks
- * its own gather_mm kernels). */
+ * automatic: tcgen05 when the shape allows (in-dim % 64, out-dim % 128,
+ * <= 2048 groups) and either the mean pairs per group is >= 4 or the groups
+ * make at least one weight tile per SM (128 rows for gate/up, 256 for down),
+ * else the streaming GEMV; on tcgen05, the integer-operand kernels for 8- and
+ * 4-bit arenas while the mean is <= 16 and the caller passes a work area, the
+ * token rows permuted once the mean reaches 32.  1 = streaming GEMV always,
+ * 2 = the dequantising tcgen05 kernels whenever the shape allows, 3 = as 2
+ * with the token rows always permuted, 4 = tcgen05 whenever the shape allows,
+ * with the integer-operand kernels wherever they apply.  Process-wide.  No
+ * counterpart in the reference (MLX picks its own gather_mm kernels). */
 int sg_set_glu_path(int mode);
 
 /* Pair-tile width of the integer-operand kernels: 0 = automatic (8 while

@@ -97,7 +97,11 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
   constexpr int SUB = BITS == 16 ? 1 : W / 8;        // 8-weight steps per chunk (bf16: one chunk = 8 weights)
   static_assert(!DUAL || RW % 2 == 0, "gate/up rows come in pairs");
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  float* xs = reinterpret_cast<float*>(smem_raw);  // [NT][K] fp32
+  // the pairs' rows as fp32, lane-interleaved: the 4 values of (pair b, weight
+  // chunk c, 8-weight step, half) sit at float4 slot c % 32 of a 128-float
+  // block, so a warp's reads for chunks c0 + lane are contiguous (no bank
+  // conflicts) -- [b][c / 32][step][half][c % 32][4]
+  float* xs = reinterpret_cast<float*>(smem_raw);
   const int u = blockIdx.y;
   if (u >= counts[0]) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -105,6 +109,10 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
   const int K = DUAL ? H : I;
   const int OUT = DUAL ? I : H;
   const int CPR = K / W;  // 16-byte chunks per row (bf16: K / 8)
+  const int NCG = (CPR + 31) / 32;  // 32-chunk groups per row
+  auto xs_at = [&](int b, int c, int st, int hf) -> float* {
+    return xs + ((((size_t)b * NCG + (c >> 5)) * SUB + st) * 2 + hf) * 128 + (c & 31) * 4;
+  };
   const int r0 = (blockIdx.x * GW_WARPS + warp) * ORW;
   const int slot = slot_ids[u];
   const int p_begin = group_off[u], p_end = group_off[u + 1];
@@ -160,9 +168,9 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
         const int row = in_by_pos ? p0 + b : perm[p0 + b] / pair_div;
         v = reinterpret_cast<const uint4*>(xin + (size_t)row * K)[cc];
       }
-      float4* dst = reinterpret_cast<float4*>(xs + (size_t)b * K + cc * 8);
-      dst[0] = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
-      dst[1] = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
+      const int wc = cc * 8 / W, st = (cc * 8 - wc * W) >> 3;  // the weight chunk and 8-weight step of these values
+      *reinterpret_cast<float4*>(xs_at(b, wc, st, 0)) = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
+      *reinterpret_cast<float4*>(xs_at(b, wc, st, 1)) = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
     }
     __syncthreads();
     if (!rows_ok) continue;
@@ -184,8 +192,8 @@ gemv_glu_kernel(sg_arena A, const uint16_t* __restrict__ xin, int pair_div, cons
             unsigned long long x2[NT][4];
 #pragma unroll
             for (int b = 0; b < NT; ++b) {
-              const float4* xp = reinterpret_cast<const float4*>(xs + (size_t)b * K + (size_t)c * W + sstep * 8);
-              const float4 lo = xp[0], hi = xp[1];
+              const float4 lo = *reinterpret_cast<const float4*>(xs_at(b, c, sstep, 0));
+              const float4 hi = *reinterpret_cast<const float4*>(xs_at(b, c, sstep, 1));
               x2[b][0] = pk2(lo.x, lo.y);
               x2[b][1] = pk2(lo.z, lo.w);
               x2[b][2] = pk2(hi.x, hi.y);
@@ -240,7 +248,9 @@ static int launch_gemv_nt(const sg_arena* A, const uint16_t* xin, int pair_div, 
   constexpr int ORW = DUAL ? RW / 2 : RW;
   const int K = DUAL ? A->hidden : A->inter;
   const int OUT = DUAL ? A->inter : A->hidden;
-  const size_t smem = (size_t)NT * K * 4;
+  // lane-interleaved rows: whole 32-chunk groups per row
+  const int cpr = K / Wpc<BITS>::v;
+  const size_t smem = (size_t)NT * ((cpr + 31) / 32) * 32 * Wpc<BITS>::v * 4;
   if (smem > 48 * 1024) {
     static bool attr_done[64] = {};
     int dev = 0;
@@ -339,17 +349,18 @@ static int sm_count() {
   return n;
 }
 
-// auto: the tensor-core path once the mean pairs per group reaches 2, or once
-// the groups give at least one tile per SM (a tile streams 128 weight rows
-// at the HBM rate whatever its pair count, so it beats the CUDA-core GEMV
-// from one pair per group on); the GEMV serves the few-expert steps whose
-// tiles would leave most SMs idle.
+// auto: the tensor-core kernels once the mean pairs per group reaches 4 or
+// the groups make at least one weight tile per SM (128 rows for gate/up, 256
+// for down); the GEMV serves the smaller steps -- a few experts, a pair or two
+// each -- whose tiles would leave most SMs idle (measured: one token through
+// 10 experts, the GEMV streams 0.19 of the copy bandwidth, the tensor-core
+// kernels 0.13).
 static bool use_tc(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || !tc_supported(A, dual, grid_groups)) return false;
-  if (g_glu_path == 2 || g_glu_path == 3) return true;
+  if (g_glu_path >= 2) return true;
   const int out = dual ? A->inter : A->hidden;
-  const long long tiles = (long long)grid_groups * (out / 128);
-  return P >= 2 * grid_groups || tiles >= sm_count();
+  const long long tiles = (long long)grid_groups * (out / (dual ? 128 : 256));
+  return P >= 4 * grid_groups || tiles >= sm_count();
 }
 
 // Whether sg_glu_forward first copies the pairs' token rows into dispatch
@@ -368,7 +379,7 @@ static bool use_permute(const sg_arena* A, int P, int grid_groups) {
 // (decode batches); they need a caller work area for the input rows' pieces.
 static bool use_i8(const sg_arena* A, bool dual, int P, int grid_groups) {
   if (g_glu_path == 1 || g_glu_path == 2 || g_glu_path == 3) return false;
-  if (grid_groups <= 0 || !i8_supported(A, dual, grid_groups) || !tc_supported(A, dual, grid_groups)) return false;
+  if (grid_groups <= 0 || !i8_supported(A, dual, grid_groups) || !use_tc(A, dual, P, grid_groups)) return false;
   if (g_glu_path == 4) return true;
   return (P + grid_groups - 1) / grid_groups <= 16;
 }
