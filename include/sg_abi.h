@@ -278,8 +278,10 @@ int sg_dense_glu(const sg_arena* arena, int sid, const uint16_t* x, int T, uint1
  * counterpart in the reference (MLX picks its own gather_mm kernels). */
 int sg_set_glu_path(int mode);
 
-/* Pair-tile width of the integer-operand kernels: 0 = automatic (8 while
- * groups average at most 6 pairs, else 16), 8 or 16 to force one.
+/* Pair-tile width: 0 = automatic (integer-operand kernels 8 while groups
+ * average at most 6 pairs, else 16; dequantising kernels the smallest of
+ * 16/32/64/128 that holds the mean group).  8 fixes the integer-operand
+ * kernels' tile, 32, 64 or 128 the dequantising kernels', 16 both.
  * Process-wide.  No counterpart in the reference. */
 int sg_set_glu_tile(int bn);
 

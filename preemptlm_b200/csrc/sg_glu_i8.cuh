@@ -819,9 +819,12 @@ int i8_tile_width(int num_pairs, int grid_groups) {
   const int avg = (num_pairs + grid_groups - 1) / (grid_groups > 0 ? grid_groups : 1);
   return avg <= i8::TILE8_MAX ? 8 : 16;
 }
+// 0 automatic; 8 fixes the integer-operand kernels' tile, 32/64/128 the
+// dequantising kernels', 16 both.
 int set_i8_tile(int bn) {
-  if (bn != 0 && bn != 8 && bn != 16) return SG_ERR_INVALID_ARG;
-  g_i8_tile = bn;
+  if (bn != 0 && bn != 8 && bn != 16 && bn != 32 && bn != 64 && bn != 128) return SG_ERR_INVALID_ARG;
+  g_i8_tile = bn <= 16 ? bn : 0;
+  g_tc_tile = bn >= 16 ? bn : 0;
   return SG_OK;
 }
 

@@ -1288,8 +1288,11 @@ static int launch_mode(const sg_arena* A, int mode, int bn, const Args& args, cu
 
 }  // namespace tc
 
-// Choose BN from the mean pairs per group (host-side bound: P / grid_groups).
+// Choose BN from the mean pairs per group (host-side bound: P / grid_groups),
+// unless sg_set_glu_tile fixed one.
+static int g_tc_tile = 0;
 static int pick_bn(int P, int grid_groups) {
+  if (g_tc_tile) return g_tc_tile;
   const int avg = (P + grid_groups - 1) / (grid_groups > 0 ? grid_groups : 1);
   if (avg <= 16) return 16;
   if (avg <= 32) return 32;

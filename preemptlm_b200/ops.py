@@ -356,7 +356,8 @@ def set_glu_path(mode: str) -> None:
 
 
 def set_glu_tile(bn: int) -> None:
-    """Pair-tile width of the integer-operand kernels: 0 (automatic), 8 or 16."""
+    """Pair-tile width: 0 (automatic); 8 fixes the integer-operand kernels',
+    32/64/128 the dequantising kernels', 16 both."""
     _abi.call("sg_set_glu_tile", int(bn))
 
 

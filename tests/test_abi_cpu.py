@@ -75,7 +75,9 @@ def test_host_side_argument_checks(lib):
     assert lib.sg_permute_rows(1, 1, 0, 4, 16, 1, None) == _abi.SG_ERR_INVALID_ARG
     assert lib.sg_set_glu_path(5) == _abi.SG_ERR_INVALID_ARG
     assert lib.sg_set_glu_tile(12) == _abi.SG_ERR_INVALID_ARG
-    assert lib.sg_set_glu_tile(0) == _abi.SG_OK
+    assert lib.sg_set_glu_tile(256) == _abi.SG_ERR_INVALID_ARG
+    for bn in (8, 16, 32, 64, 128, 0):
+        assert lib.sg_set_glu_tile(bn) == _abi.SG_OK
     # integer-operand gate/up: work sizes and argument checks (no GPU touched)
     assert lib.sg_quantize_pieces(1, 2, 100, 0, 1, 1, None) == _abi.SG_ERR_SHAPE
     assert lib.sg_quantize_pieces(1, 2, 128, 2, 1, 1, None) == _abi.SG_ERR_INVALID_ARG

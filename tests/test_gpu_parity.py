@@ -185,6 +185,37 @@ def test_glu_matches_oracle(glu_path, bits, H, I, E, T, k):
     assert torch.equal(ops.gather_forward(block.switch_mlp, x, d, k), y)
 
 
+@pytest.mark.parametrize("glu_path", ["tc"], indirect=True)
+@pytest.mark.parametrize("bits", [16, 8, 4])
+def test_glu_forced_tile_widths(glu_path, bits):
+    """sg_set_glu_tile fixes the dequantising kernels' pair tile: every width
+    gives the oracle's h and y on groups of ~50 pairs (one 64- or 128-wide
+    tile, two 32-wide or four 16-wide tiles per group)."""
+    H, I, E, T, k = 512, 256, 4, 100, 2
+    cfg = LayerConfig("t", 9, H, E, k, I, None, bits, E)
+    block, tens = make_layer(cfg, device=DEV)
+    x = _bf16((T, H), 5)
+    g = np.random.default_rng(3)
+    inds = np.stack([g.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    d = ops.dispatch(torch.from_numpy(inds).to(DEV), E, torch.arange(E, dtype=torch.int32, device=DEV))
+    ex = LazyExperts(tens["experts"], bits)
+    xf = f32(x)
+    href = np.stack([orc.swiglu(orc._mm_bf16(xf[p // k: p // k + 1], ex[inds.reshape(-1)[p]].up),
+                                orc._mm_bf16(xf[p // k: p // k + 1], ex[inds.reshape(-1)[p]].gate))[0]
+                     for p in range(T * k)])
+    try:
+        for bn in (16, 32, 64, 128):
+            ops.set_glu_tile(bn)
+            h = ops.glu_gate_up(block.switch_mlp, x, d, pair_div=k)
+            assert_close(f32(h), href, max_abs=2e-2 * max(1.0, float(np.abs(href).max())), what=f"h bn={bn}")
+            y = ops.glu_down(block.switch_mlp, h, d)
+            hdev = f32(h)
+            ydown = np.stack([orc._mm_bf16(hdev[p: p + 1], ex[inds.reshape(-1)[p]].down)[0] for p in range(T * k)])
+            assert_close(f32(y), ydown, max_abs=1e-2, rel=4e-3, what=f"y|h bn={bn}")
+    finally:
+        ops.set_glu_tile(0)
+
+
 @pytest.mark.parametrize("bits", [16, 8, 4])
 @pytest.mark.parametrize("H,I,T", [(1024, 512, 2), (1024, 512, 37), (1024, 512, 256), (1024, 512, 1100),
                                    (1024, 512, 2400),  # 4 x 38 tiles of 64 > 148 SMs: 128-wide tiles
