@@ -85,6 +85,9 @@ def parse_args():
     ap.add_argument("--sweep-steps", type=int, default=20, help="timed steps per sweep point")
     ap.add_argument("--sweep-only", default=None,
                     help="comma-separated sweep configurations to run (default: all)")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="L > 1: an L-layer stack of the workload's MoE block, expert-parallel over the GPUs "
+                         "(cfg4 with 60: the 397B-style stack), one pass of the tokens through every layer per step")
     return ap.parse_args()
 
 
@@ -797,6 +800,181 @@ def run_ours(args, rank, world, local_rank):
 # --------------------------------------------------------------------------- reference arm
 
 
+def run_stack(args, rank, world, local_rank):
+    """``--layers L``: the MoE blocks of an L-layer decoder stack, each split
+    expert-parallel over the N GPUs and all sharing one peer exchange.  A step
+    is one pass of ``--tokens`` tokens per GPU through every layer on the
+    residual stream (x <- x + layer(x)); the whole step is one CUDA graph.
+    Per-kernel figures are layer 0's, from an eager pass."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from preemptlm_b200 import ops
+    from preemptlm_b200.ep import ExpertParallelMoE, ExpertParallelStack, PeerExchange, shard_layer
+    from preemptlm_b200.synthetic import CONFIGS, make_tokens
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.workload]
+    L, T, H = args.layers, args.tokens, cfg.hidden
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=300), device_id=dev)
+    else:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+
+    t_build = time.perf_counter()
+    ex = PeerExchange(None, world, rank, T, cfg.top_k, H, dev)
+    layers = []
+    for li in range(L):
+        backend, _ = shard_layer(cfg, rank, world, dev, layer=li)
+        layers.append(ExpertParallelMoE(backend, cfg.num_experts, H, cfg.top_k, transport="p2p", max_tokens=T,
+                                        exchange=ex))
+        torch.cuda.empty_cache()
+    stack = ExpertParallelStack(layers)
+    build_s = time.perf_counter() - t_build
+    mem_gb = torch.cuda.memory_allocated(dev) / 1e9
+    xs = [make_tokens(cfg, T, device=dev, step=i + 1000 * rank) for i in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        stack(xs[i])
+    torch.cuda.synchronize()
+    stack.capture(T)
+    for i in range(args.warmup):
+        stack.replay(xs[i])
+    torch.cuda.synchronize()
+    barrier()
+
+    # device-resident: graph replays queued behind a bounded device spin
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = ops.LAUNCHES[0]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gc.collect()
+    gc.disable()
+    torch.cuda._sleep(QUEUE_AHEAD_CYCLES)
+    stack.replay(xs[0])  # lines up the ranks after the spin (untimed)
+    start.record()
+    for i in range(args.steps):
+        stack.replay(xs[args.warmup + i])
+    end.record()
+    torch.cuda.synchronize()
+    gc.enable()
+    barrier()
+    clk = clocks.stop()
+    launches = ops.LAUNCHES[0] - launches0
+    t = torch.tensor([start.elapsed_time(end) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item())
+
+    # layer 0's kernels and exchange phases: an eager pass behind the same spin
+    timing: dict = {}
+    n_eager = min(args.steps, 5)
+    gc.disable()
+    torch.cuda._sleep(QUEUE_AHEAD_CYCLES)
+    layers[0].backend.timing = timing
+    for i in range(n_eager):
+        stack(xs[args.warmup + i])
+    torch.cuda.synchronize()
+    layers[0].backend.timing = None
+    gc.enable()
+    barrier()
+    rl = _kernel_roofline(cfg, timing, timing.get("rows"), T)
+    phases = None
+    if timing.get("phases"):
+        names = ("route_shared", "send", "wait_inbox", "experts", "send_back", "wait_back", "combine")
+        phases = {n: round(statistics.mean(m[j].elapsed_time(m[j + 1]) for m in timing["phases"]), 4)
+                  for j, n in enumerate(names)}
+    peak, peak_kind = hbm_peak()
+    us_mean = rl["mean_unique"]
+    step_bytes = L * (us_mean * cfg.expert_bytes() + cfg.shared_bytes() + cfg.num_experts * H * 2 + 2 * T * H * 2)
+    step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
+
+    # end to end: the captured stack fed from pinned host memory through the pipeline
+    x_host = [torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for i, xh in enumerate(x_host):
+        xh.copy_(xs[i].cpu())
+    out_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    pipe = stack.host_pipeline()
+    for i in range(args.warmup):
+        pipe.step(x_host[i % 2], out_host)
+    pipe.drain()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gc.disable()
+    e0.record()
+    for i in range(args.steps):
+        pipe.step(x_host[i % 2], out_host)
+    pipe.drain()
+    e1.record()
+    torch.cuda.synchronize()
+    gc.enable()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    stack.check()
+
+    shard = cfg.num_experts // world
+    value = T * world / (ms_step * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": f"u{cfg.bits}" if cfg.bits != 16 else "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, every layer its own seeds; N(0,1) tokens)",
+        "config": {
+            "workload": f"{cfg.name} x {L} layers: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
+                        f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, {T} tokens/GPU through every layer "
+                        f"(x <- x + moe(x)), expert-parallel over {world} GPU(s), {shard} experts of each "
+                        f"layer resident per GPU",
+            "layers": L, "tokens_per_gpu": T, "hidden": H, "experts": cfg.num_experts, "top_k": cfg.top_k,
+            "inter": cfg.inter, "shared_inter": cfg.shared_inter, "bits": cfg.bits, "slots_per_gpu_per_layer": shard,
+            "weights_gb_per_gpu": round(mem_gb, 1), "build_s": round(build_s, 1),
+            "unique_experts_per_layer_per_gpu": round(us_mean, 1),
+            "l2": "no flush: each step streams every layer's experts (GBs per GPU)",
+            "queue": "device-resident steps are queued behind a bounded device spin (not timed); e2e is not",
+            "parallelism": f"ep{world}", "exchange": "p2p, one region shared by the layers",
+            "timed_steps": "CUDA graph replays of the whole stack",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": f"{ops.LAST_GATE_UP[0]} (routed, q{cfg.bits}, layer 0)",
+            "achieved": round(rl["gu_gbs"], 1), "peak": peak, "unit": "GB/s", "frac": round(rl["gu_gbs"] / peak, 4),
+            "peak_kind": peak_kind, "traffic": None, "traffic_source": None,
+            "ms_per_launch": round(statistics.mean(rl["gu_ms"]), 5),
+            "down": {"achieved": round(rl["dn_gbs"], 1), "frac": round(rl["dn_gbs"] / peak, 4),
+                     "ms_per_launch": round(statistics.mean(rl["dn_ms"]), 5)},
+            "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+            "pairs_per_expert": round(rl["pairs_per_expert"], 1),
+        },
+        "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": launches,
+        "step_detail": {"ms_per_layer": round(ms_step / L, 4), "layer0_phases_ms": phases},
+        "clocks": clk,
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier()
+    stack.close()
+    dist.destroy_process_group()
+
+
 def run_reference(args, rank, world):
     """The CPU port of the layer (the oracle; the reference's own MLX numerics
     do not import here) on the same step as our arm: a batch of --tokens
@@ -955,6 +1133,9 @@ def main():
         return
     if args.workload == "cfg5":
         run_stream(args, rank, world, local_rank)
+        return
+    if args.layers > 1:
+        run_stack(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)
 

@@ -217,7 +217,12 @@ class ExpertParallelMoE:
     """One slotted MoE layer split expert-parallel over the process group."""
 
     def __init__(self, backend, num_experts: int, hidden: int, top_k: int, group=None, transport: str | None = None,
-                 max_tokens: int = 256):
+                 max_tokens: int = 256, exchange: "PeerExchange | None" = None):
+        """``exchange``: a peer exchange to use instead of allocating one (p2p
+        transport), e.g. one shared by the layers of a stack, which run one
+        after another.  It must have this layer's world, hidden size and room
+        for ``max_tokens * top_k`` pairs per source; the layer does not close
+        it."""
         self.backend = backend
         self.group = group
         self.world = dist.get_world_size(group)
@@ -233,9 +238,15 @@ class ExpertParallelMoE:
         self.transport = transport
         self.max_tokens = max_tokens
         self.exchange = None
+        self._owns_exchange = False
         if transport == "p2p":
-            self.exchange = PeerExchange(group, self.world, self.rank, max_tokens, top_k, hidden,
-                                         backend.router.device)
+            if exchange is None:
+                exchange = PeerExchange(group, self.world, self.rank, max_tokens, top_k, hidden,
+                                        backend.router.device)
+                self._owns_exchange = True
+            elif exchange.world != self.world or exchange.hidden != hidden or exchange.cap < max_tokens * top_k:
+                raise ValueError("the shared exchange does not fit this layer (world, hidden or pair capacity)")
+            self.exchange = exchange
         self._graph = None
         self.graph_input = self.graph_output = None
         self._graph_launches = 0
@@ -307,9 +318,9 @@ class ExpertParallelMoE:
         buffers (p2p transport)."""
         self._graph = None
         self.graph_input = self.graph_output = None
-        if self.exchange is not None:
+        if self.exchange is not None and self._owns_exchange:
             self.exchange.close()
-            self.exchange = None
+        self.exchange = None
 
     def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
         if self.broken:
@@ -430,14 +441,111 @@ class ExpertParallelMoE:
     __call__ = forward
 
 
-def shard_layer(cfg, rank: int, world: int, device, seed_offset: int = 0):
+class ExpertParallelStack:
+    """The MoE blocks of a decoder stack, each expert-parallel: L layers
+    applied in turn to the residual stream, ``x <- x + layer(x)`` (the
+    attention blocks between them are outside this library).  The layers may
+    share one peer exchange: they run one after another on the stream, so a
+    rank's next send into a peer follows its wait for that peer's outputs of
+    the layer before, as between two steps of one layer.  ``capture`` records
+    the whole stack as one CUDA graph."""
+
+    def __init__(self, layers):
+        self.layers = list(layers)
+        if not self.layers:
+            raise ValueError("a stack needs at least one layer")
+        self._graph = None
+        self.graph_input = self.graph_output = None
+        self._graph_launches = 0
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x [T, H] bf16 (this rank's tokens) -> the residual stream after
+        every layer, [T, H] bf16."""
+        for layer in self.layers:
+            x = x + layer.forward(x)
+        return x
+
+    __call__ = forward
+
+    def capture(self, T: int, warmup: int = 2, seed: int = 0) -> None:
+        """Collective: one CUDA graph of the whole stack for T tokens (p2p
+        layers; see ``ExpertParallelMoE.capture``)."""
+        if any(layer.transport != "p2p" for layer in self.layers):
+            raise ValueError("only p2p layers can be captured")
+        dev = self.layers[0].backend.router.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.graph_input = torch.randn((T, self.layers[0].hidden), generator=g, device=dev).to(torch.bfloat16)
+        timings = [layer.backend.timing for layer in self.layers]
+        for layer in self.layers:
+            layer.backend.timing = None
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.forward(self.graph_input)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        n0 = ops.LAUNCHES[0]
+        with torch.cuda.graph(graph):
+            self.graph_output = self.forward(self.graph_input)
+        self._graph_launches = ops.LAUNCHES[0] - n0
+        self._graph = graph
+        for layer, t in zip(self.layers, timings):
+            layer.backend.timing = t
+
+    def replay(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        """One captured pass through the stack (``x`` first copied into the
+        graph's input); returns the graph's output buffer."""
+        if any(layer.broken for layer in self.layers):
+            raise ExchangeTimeoutError(_abi.SG_ERR_TIMEOUT, "expert-parallel exchange (timed out earlier; rebuild it)")
+        if x is not None:
+            self.graph_input.copy_(x, non_blocking=True)
+        self._graph.replay()
+        ops.LAUNCHES[0] += self._graph_launches
+        return self.graph_output
+
+    def host_pipeline(self) -> "ops.HostPipeline":
+        """Replays fed from and drained to pinned host buffers, the copies
+        overlapped with the neighbouring steps' compute.  ``capture`` first."""
+        if self._graph is None:
+            raise RuntimeError("capture() first")
+        return ops.HostPipeline(self.graph_input, self.graph_output, self.replay)
+
+    def check(self) -> None:
+        """As ``ExpertParallelMoE.check``; a timeout marks every layer broken."""
+        st = ops.device_status(reset=True)
+        if st == _abi.SG_ERR_TIMEOUT:
+            for layer in self.layers:
+                layer.broken = True
+            raise ExchangeTimeoutError(st, "expert-parallel exchange")
+        _abi.check(st, "expert-parallel stack step")
+
+    def close(self) -> None:
+        """Collective: release the graph, the layers and every exchange they
+        use (a shared one once)."""
+        self._graph = None
+        self.graph_input = self.graph_output = None
+        shared = []
+        for layer in self.layers:
+            ex = layer.exchange
+            if ex is not None and not layer._owns_exchange and all(ex is not o for o in shared):
+                shared.append(ex)
+            layer.close()
+        for ex in shared:
+            ex.close()
+
+
+def shard_layer(cfg, rank: int, world: int, device, seed_offset: int = 0, layer: int = 0):
     """This rank's shard of the seeded synthetic layer ``cfg``: the same global
-    weights for any world size (all experts generated, the shard kept)."""
+    weights for any world size (all experts generated, the shard kept).
+    ``layer`` > 0 draws another layer of a stack (every tensor from its own
+    seeds)."""
     from .synthetic import _gen, _randn, fill_arena, make_expert_tensors
 
     check_divisible(cfg.num_experts, world)
     sh = ExpertShard(rank, world, cfg.num_experts)
-    c = cfg.cfg_id
+    c = cfg.cfg_id + 1_000_000 * layer
     router = _randn((cfg.num_experts, cfg.hidden), _gen(1000 * c + 1, device), device, 0.02)
     full = make_expert_tensors(cfg, cfg.num_experts, cfg.inter, 1000 * c + 2 + seed_offset, device)
     mine = {k: v[sh.first: sh.first + sh.count].contiguous() for k, v in full.items()}

@@ -24,13 +24,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _layer(H=256, E=32, k=4, I=128, bits=8):
+def _layer(H=256, E=32, k=4, I=128, bits=8, seed=77):
     """A tiny seeded q8 layer with a shared expert, as host tensors."""
     sys.path.insert(0, ROOT)
     from oracle import slotted_glu_oracle as orc
     from preemptlm_b200.quant import quantize_affine
 
-    g = torch.Generator().manual_seed(77)
+    g = torch.Generator().manual_seed(seed)
 
     def rnd(*shape, std=0.02):
         return (torch.randn(shape, generator=g) * std).to(torch.bfloat16)
@@ -139,6 +139,61 @@ def _worker(rank, world, port, mode, errfile):
         with open(errfile, "a") as f:
             f.write(f"rank {rank}:\n{traceback.format_exc()}\n")
         raise
+
+
+def _stack_worker(rank, world, port, errfile):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+        from oracle import slotted_glu_oracle as orc
+        from preemptlm_b200.ep import ExpertParallelMoE, ExpertParallelStack
+
+        H, E, k, L = 256, 32, 4, 3
+        per = E // world
+        layers, full = [], []
+        for li in range(L):
+            router, experts, shared, sgate = _layer(H=H, E=E, k=k, seed=77 + li)
+            full.append((router, experts, shared, sgate))
+            local = {e - rank * per: experts[e] for e in range(rank * per, (rank + 1) * per)}
+            layers.append(ExpertParallelMoE(OracleBackend(router, k, local, shared, sgate), E, H, k))
+        stack = ExpertParallelStack(layers)
+        g = torch.Generator().manual_seed(2000 + rank)
+        T = 4 + 3 * rank
+        x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        out = stack(x)
+        # the oracle's layers on the residual stream, in one process
+        ref = x
+        for router, experts, shared, sgate in full:
+            y = orc.layer_forward(OracleBackend._bits(ref), router, k, True, experts, shared, sgate)["out"]
+            ref = ref + torch.from_numpy(y).to(torch.bfloat16)
+        err = (out.float() - ref.float()).abs().max().item()
+        assert err <= 3e-2, f"rank {rank}: max-abs {err} after {L} layers"
+        stack.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException:
+        with open(errfile, "a") as f:
+            f.write(f"rank {rank}:\n{traceback.format_exc()}\n")
+        raise
+
+
+def test_ep_stack_two_ranks_gloo(tmp_path):
+    """Three expert-parallel layers on the residual stream (x <- x + layer(x))
+    over 2 gloo ranks, against the oracle's layers chained in one process."""
+    world, port = 2, _free_port()
+    err = tmp_path / "err.txt"
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, str(err))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("EP rank hung")
+    msg = err.read_text() if err.exists() else ""
+    assert all(p.exitcode == 0 for p in procs), msg
 
 
 @pytest.mark.parametrize("mode", ["parity", "fail"])

@@ -111,6 +111,94 @@ def _worker(rank, world, port, errfile, transport):
         raise
 
 
+def _stack_worker(rank, world, port, errfile):
+    """Three layers (their own seeds) sharing one peer exchange, on the
+    residual stream: eager steps with ragged tokens, then graph replays of the
+    whole stack, against the single-GPU layers chained the same way."""
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        from preemptlm_b200.ep import ExpertParallelMoE, ExpertParallelStack, PeerExchange, shard_layer
+        from preemptlm_b200.layer import Qwen3_xMoEWrapper
+        from preemptlm_b200.synthetic import LayerConfig, make_layer, make_tokens
+
+        from preemptlm_b200 import ops
+
+        cfg = LayerConfig("ep", 8, 1024, 64, 6, 256, 256, 8, 64)
+        L, Tmax = 3, 48
+        ex = PeerExchange(None, world, rank, Tmax, cfg.top_k, cfg.hidden, dev)
+        layers, singles = [], []
+        for li in range(L):
+            backend, _ = shard_layer(cfg, rank, world, dev, layer=li)
+            layers.append(ExpertParallelMoE(backend, cfg.num_experts, cfg.hidden, cfg.top_k, transport="p2p",
+                                            max_tokens=Tmax, exchange=ex))
+            block, _ = make_layer(cfg.scaled(cfg_id=cfg.cfg_id + 1_000_000 * li), device=dev)
+            singles.append(Qwen3_xMoEWrapper(block, "fp", f"l{li}", li))
+        stack = ExpertParallelStack(layers)
+
+        def reference(x):
+            for single in singles:
+                x = x + single.forward_resident(x)
+            return x
+
+        def check(out, ref, what):
+            tol = 2.0 ** -6 * L * max(1.0, ref.float().abs().max().item())
+            err = (out.float() - ref.float()).abs().max().item()
+            assert err <= tol, f"rank {rank} {what}: max-abs {err} (tolerance {tol}) vs the single-GPU layers"
+
+        for step in range(2):
+            T = 40 + 4 * (rank % 2) - 5 * step
+            x = make_tokens(cfg, T, device=dev, step=10 * step + rank)
+            check(stack(x), reference(x), f"step {step}")
+        stack.capture(T)
+        for step in range(2):
+            x = make_tokens(cfg, T, device=dev, step=200 + 10 * step + rank)
+            check(stack.replay(x).clone(), reference(x), f"replay {step}")
+        torch.cuda.synchronize()
+        stack.check()
+        assert ops.device_status(reset=True) == 0
+        stack.close()
+        assert ex.region is None  # the shared exchange was freed once, by the stack
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException:
+        with open(errfile, "a") as f:
+            f.write(f"rank {rank}:\n{traceback.format_exc()}\n")
+        raise
+
+
+def _spawn(target, world, tmp_path, *extra):
+    import torch.multiprocessing as mp
+
+    port, err = _free_port(), tmp_path / "err.txt"
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=target, args=(r, world, port, str(err), *extra)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("EP rank hung")
+    assert all(p.exitcode == 0 for p in procs), err.read_text() if err.exists() else ""
+
+
+def test_ep_stack_one_rank_shared_exchange(tmp_path):
+    """A three-layer expert-parallel stack, one rank exchanging with itself."""
+    _spawn(_stack_worker, 1, tmp_path)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_stack_two_gpus_shared_exchange(tmp_path):
+    """The same stack over 2 GPUs."""
+    _spawn(_stack_worker, 2, tmp_path)
+
+
 def test_ep_one_rank_exchange_and_graph(tmp_path):
     """One rank exchanging with itself over the same peer-memory kernels
     (inboxes, flags, outputs written back), eager and as a replayed CUDA
