@@ -844,7 +844,9 @@ def run_stack(args, rank, world, local_rank):
     for i in range(args.warmup):
         stack(xs[i])
     torch.cuda.synchronize()
+    mem_before = torch.cuda.memory_allocated(dev)
     stack.capture(T)
+    graph_pool_gb = (torch.cuda.memory_allocated(dev) - mem_before) / 1e9  # buffers the graph keeps
     for i in range(args.warmup):
         stack.replay(xs[i])
     torch.cuda.synchronize()
@@ -939,12 +941,14 @@ def run_stack(args, rank, world, local_rank):
         "data": "synthetic (seeded N(0,0.02) weights, every layer its own seeds; N(0,1) tokens)",
         "config": {
             "workload": f"{cfg.name} x {L} layers: H{cfg.hidden} E{cfg.num_experts} k{cfg.top_k} I{cfg.inter} "
-                        f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, {T} tokens/GPU through every layer "
+                        f"shared{cfg.shared_inter} affine-q{cfg.bits} g64, {'prefill' if T >= 1024 else 'decode'} {T} "
+                        f"tokens/GPU through every layer "
                         f"(x <- x + moe(x)), expert-parallel over {world} GPU(s), {shard} experts of each "
                         f"layer resident per GPU",
             "layers": L, "tokens_per_gpu": T, "hidden": H, "experts": cfg.num_experts, "top_k": cfg.top_k,
             "inter": cfg.inter, "shared_inter": cfg.shared_inter, "bits": cfg.bits, "slots_per_gpu_per_layer": shard,
-            "weights_gb_per_gpu": round(mem_gb, 1), "build_s": round(build_s, 1),
+            "weights_gb_per_gpu": round(mem_gb, 1), "graph_pool_gb_per_gpu": round(graph_pool_gb, 2),
+            "peak_gb_per_gpu": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1),
             "unique_experts_per_layer_per_gpu": round(us_mean, 1),
             "l2": "no flush: each step streams every layer's experts (GBs per GPU)",
             "queue": "device-resident steps are queued behind a bounded device spin (not timed); e2e is not",
